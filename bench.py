@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the decode hot path: KV-ring append + RoPE + attention, all 12 layers.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|5] [--impl ours|reference]
+
+A *step* is one decode frame of every stream this GPU owns: 12 launches of the
+fused append+attend kernel (one per layer), through the C ABI (mb_decode_step).
+Workloads:
+  2 (default)  64 streams/GPU, 12 layers x 12 heads x 64, fp32 ring of 512 slots;
+               positions 0..1499 (the ring wraps twice), repeated, reset between passes
+  5            512 streams/GPU, bf16 ring of 4096 slots, live lengths U[1, 4096]
+               from a seed, consecutive appends (streams shard by length at N > 1)
+Weak scaling: every GPU runs its own streams; no collective on the decode path
+(NCCL only for the barrier, the max-over-ranks timing and the report gather).
+
+--impl reference times the reference algorithm on the host cores instead: the
+CPU restatement in oracle/ (the reference is WGSL/TypeScript and cannot run
+here), on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode frames/sec/GPU (all 12 layers' append+attn) and HBM GB/s vs roofline, 1/2/4/8 GPU"
+H, HD = 12, 64
+HID = H * HD
+QKV = 3 * HID
+
+CONFIGS = {
+    2: dict(workload="config2: ring wraparound, 64 streams/GPU x 12 layers x 12 heads x 64, fp32 ring capacity "
+                     "512, 1500 appends per stream (wraps twice), attention over the last <=512 positions every step",
+            streams=64, layers=12, capacity=512, dtype="f32", job_steps=1500, steps=3000, warmup=30),
+    5: dict(workload="config5: long-text serving, 512 streams/GPU x 12 layers x 12 heads x 64, bf16 ring capacity "
+                     "4096, live lengths U[1,4096] from seed 0, consecutive appends",
+            streams=512, layers=12, capacity=4096, dtype="bf16", job_steps=None, steps=200, warmup=5),
+}
+
+
+def _esize(dtype):
+    return 4 if dtype == "f32" else 2
+
+
+def window_bytes(L, esize, layers=12):
+    """Algorithmic bytes of one stream-frame (all layers) at live window L:
+    K,V window read 2*L*768*E + K,V append 2*768*E + q,k,v in and ctx out 4*768*4."""
+    return layers * (2 * L * HID * esize + 2 * HID * esize + 4 * HID * 4)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.device_index), "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
+            os.unlink(self.path)
+        except Exception:
+            return None
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        if not sm:
+            return None
+        mx = max(float(r[2]) for r in rows if len(r) >= 9)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]})
+        loaded = [s for s in sm if s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons, "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ workloads
+def config5_lengths(total, capacity, seed=0):
+    return np.random.default_rng(seed).integers(1, capacity + 1, size=total)
+
+
+def setup_ours(cfg, rank, world, device):
+    """Rings, the qkv input pool in HBM, per-step positions."""
+    import torch
+
+    from mockbird_b200 import KvRing
+    from mockbird_b200.scheduler import partition_streams
+
+    n = cfg["streams"]
+    ring = KvRing(layers=cfg["layers"], capacity=cfg["capacity"], streams=n, dtype=cfg["dtype"], wrap=True,
+                  device=device.index, max_position=65536)
+    g = torch.Generator(device=device)
+    g.manual_seed(1234 + rank)
+    set_bytes = cfg["layers"] * n * QKV * 4
+    pool = max(2, -(-256 * 2**20 // set_bytes))  # > 2x L2 of distinct inputs
+    qkv_pool = torch.randn(pool, cfg["layers"], n, QKV, generator=g, device=device)
+    out = torch.empty(cfg["layers"], n, HID, device=device)
+    streams = torch.arange(n, dtype=torch.int32, device=device)
+    info = {"qkv_pool_sets": pool}
+    if cfg["job_steps"] is not None:  # config 2: everyone at the same position
+        lengths0 = None
+        shard_ids = partition_streams(n * world, world)[rank].streams
+    else:  # config 5: per-stream live lengths, length-balanced shards
+        total = n * world
+        all_len = config5_lengths(max(total, 4096), cfg["capacity"])[:total]
+        shard_ids = partition_streams(total, world, all_len)[rank].streams
+        lengths0 = all_len[shard_ids].astype(np.int64)
+        # fill positions 0..L-2 of every stream with N(0,1) K/V (the same rows for all layers)
+        for i, L in enumerate(lengths0):
+            if L <= 1:
+                continue
+            kv = torch.randn(2, H, int(L) - 1, HD, generator=g, device=device).to(ring.torch_dtype)
+            for layer in range(cfg["layers"]):
+                ring.ring_write(layer, i, 0, kv[0], kv[1])
+        torch.cuda.synchronize(device)
+    info["global_streams"] = n * world
+    info["shard"] = [int(shard_ids.min()), int(shard_ids.max())] if len(shard_ids) else []
+    return ring, qkv_pool, out, streams, lengths0, info
+
+
+def positions_for(cfg, step, n, lengths0):
+    """Host positions of every stream at `step` (a step of the job)."""
+    if lengths0 is None:
+        return np.full(n, step % cfg["job_steps"], np.int32)
+    return (lengths0 - 1 + step).astype(np.int32)
+
+
+def live_len(pos, capacity):
+    return np.minimum(pos + 1, capacity)
+
+
+def run_ours(args, cfg, rank, world, device):
+    import torch
+
+    from mockbird_b200.scheduler import max_over_ranks
+
+    ring, qkv_pool, out, streams, lengths0, info = setup_ours(cfg, rank, world, device)
+    n, L, C = cfg["streams"], cfg["layers"], cfg["capacity"]
+    K, W = args.steps, args.warmup
+    es = _esize(cfg["dtype"])
+    # positions of every step, staged on the device (warm-up steps first)
+    steps_total = W + K
+    pos_host = np.stack([positions_for(cfg, t if lengths0 is not None else t, n, lengths0)
+                         for t in range(steps_total)])
+    if lengths0 is None:  # config 2: warm-up at 0..W-1, then the timed job from position 0
+        pos_host[W:] = np.stack([positions_for(cfg, t, n, None) for t in range(K)])
+    pos_dev = torch.from_numpy(pos_host).to(device)
+    algo_bytes = sum(float(window_bytes(live_len(pos_host[t].astype(np.int64), C), es, L).sum())
+                     for t in range(W, steps_total))
+
+    def step(t):
+        if lengths0 is None and t >= W and (t - W) % cfg["job_steps"] == 0:
+            ring.reset()  # a new pass of the 1500-frame job starts from an empty ring
+        ring.decode_step(streams, pos_dev[t], qkv_pool[t % qkv_pool.shape[0]], out)
+
+    for t in range(W):
+        step(t)
+    ring.sync()
+    if lengths0 is None:
+        ring.reset()
+    dist = _dist()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for t in range(W, steps_total):
+        step(t)
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ring.sync()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, device if dist else None)
+    launches = L * K
+
+    # ---- end to end through the host-array C ABI call (pinned buffers), copies timed
+    e2e = None
+    if not args.no_e2e:
+        sets = 2
+        host_qkv = torch.empty(sets, L, n, QKV, dtype=torch.float32).pin_memory()
+        for i in range(sets):
+            host_qkv[i].copy_(qkv_pool[i])
+        host_out = torch.empty(L, n, HID, dtype=torch.float32).pin_memory()
+        ids = np.arange(n, dtype=np.int32)
+        if lengths0 is None:
+            ring.reset()
+        e2e_steps = K if lengths0 is None else min(K, 50)
+        base = W + K
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        for t in range(e2e_steps):
+            if lengths0 is None and t > 0 and t % cfg["job_steps"] == 0:
+                ring.reset()
+            pos = positions_for(cfg, t if lengths0 is None else base + t, n, lengths0)
+            ring.decode_step_host(ids, pos, host_qkv[t % sets], host_out)
+        torch.cuda.synchronize(device)
+        e2e_s = max_over_ranks(time.perf_counter() - t0, device if dist else None)
+        e2e = {"value": world * n * e2e_steps / e2e_s, "unit": "frames/s",
+               "h2d_bytes_per_step": int(L * n * QKV * 4 + 2 * n * 4),
+               "d2h_bytes_per_step": int(L * n * HID * 4),
+               "steps": e2e_steps, "api": "mb_decode_step_host (C ABI, pinned host buffers, blocking per step)"}
+
+    value = world * n * K / (ms_max / 1e3)
+    peak, peak_kind = peaks()
+    achieved = algo_bytes / (ms / 1e3) / 1e9  # this rank's algorithmic bytes over its own device time
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                else "fallback 6650 GB/s",
+                "kernel": "decode_kernel<fused append+RoPE+split-K attention>",
+                "algorithmic_bytes_per_launch": algo_bytes / launches,
+                "avg_launch_us": ms * 1e3 / launches,
+                "timing": "CUDA events over the timed region on the launching stream; every launch in the region "
+                          "is this kernel, so avg launch = region / launches (launch gaps included)"}
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "frames/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_max / K, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1) q/k/v; random ring contents)",
+        "config": {"workload": cfg["workload"], "streams_per_gpu": n, "global_streams": info["global_streams"],
+                   "layers": L, "heads": H, "head_dim": HD, "capacity": C, "storage": cfg["dtype"],
+                   "parallelism": f"stream-sharded x{world} (no collective on the decode path)",
+                   "l2": "inputs larger than L2: every step streams the live K/V windows "
+                         f"(~{algo_bytes / K / 1e9:.2f} GB/step) plus {info['qkv_pool_sets']} rotating qkv sets",
+                   "value_per_gpu": round(value / world, 1)},
+        "roofline": roofline, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+    }
+    return result, ring
+
+
+def _dist():
+    try:
+        import torch.distributed as dist
+        return dist if dist.is_initialized() else None
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------ CPU reference (oracle port)
+def run_cpu(cfg, steps, warmup, sample_streams, budget_s=None):
+    """The reference algorithm (oracle mirror of the WGSL kernels) on the host cores:
+    `sample_streams` streams of the workload, all 12 layers per frame."""
+    import oracle
+
+    n, L, C = sample_streams, cfg["layers"], cfg["capacity"]
+    ring = oracle.Ring(layers=L, streams=n, heads=H, capacity=C, dtype=cfg["dtype"], wrap=True,
+                       max_position=8192)
+    rng = np.random.default_rng(7)
+    if cfg["job_steps"] is None:
+        lengths0 = config5_lengths(4096, C)[:n].astype(np.int64)
+        kvv = ring.kv_view()
+        for s, Ls in enumerate(lengths0):
+            if Ls > 1:
+                rows = rng.standard_normal((2, H, int(Ls) - 1, HD)).astype(np.float32)
+                if cfg["dtype"] == "f32":
+                    kvv[:, s, :, :, :Ls - 1] = rows[None]
+                else:
+                    u = rows.view(np.uint32)
+                    kvv[:, s, :, :, :Ls - 1] = ((u >> 16).astype(np.uint16))[None]
+                ring.slot_pos[:, s, :Ls - 1] = np.arange(Ls - 1)
+    else:
+        lengths0 = None
+    qkv = rng.standard_normal((4, L, n, QKV)).astype(np.float32)
+    ids = np.arange(n, dtype=np.int32)
+
+    def frame(t):
+        pos = positions_for(cfg, t, n, lengths0)
+        for layer in range(L):
+            ring.append_attend(layer, ids, pos, qkv[t % 4, layer])
+
+    for t in range(warmup):
+        frame(t)
+    if lengths0 is None:
+        ring.reset()
+    t0 = time.perf_counter()
+    done = 0
+    for t in range(steps):
+        if lengths0 is None and t > 0 and t % cfg["job_steps"] == 0:
+            ring.reset()
+        frame(t if lengths0 is None else warmup + t)
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"value": round(n * done / dt, 2), "unit": "frames/s", "cores": cores, "kind": "port",
+            "sample": f"{n} of the workload's streams x {done} consecutive steps (positions as in the GPU run), "
+                      f"all {L} layers per frame, oracle/oracle.c fp32 mirror of the WGSL kernels, "
+                      f"OpenMP over (stream, head), {dt:.1f} s"}
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    args.steps = args.steps if args.steps is not None else cfg["steps"]
+    args.warmup = args.warmup if args.warmup is not None else cfg["warmup"]
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        base = run_cpu(cfg, args.steps, args.warmup, sample_streams=4)
+        line = {"metric": METRIC, "value": base["value"], "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic", "impl": "reference",
+                "config": {"workload": cfg["workload"]},
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "note": "reference = CPU restatement of the reference's WGSL kernels (oracle/); the WGSL itself needs "
+                        "a WebGPU runtime and Node, unavailable on this box"}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from mockbird_b200.scheduler import init_group
+        init_group("nccl", timeout_s=300)
+    result, ring = run_ours(args, cfg, rank, world, device)
+    dist = _dist()
+    if dist:
+        from mockbird_b200.scheduler import gather_reports
+        gather_reports({"rank": rank, "value_gpu": result["value"] / world}, device)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        result["cpu_baseline"] = run_cpu(cfg, min(args.steps, cfg["job_steps"] or args.steps), 2, sample_streams=4,
+                                         budget_s=30.0)
+    elif rank == 0:
+        result["cpu_baseline"] = None
+    ring.dispose()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,190 @@
+/*
+ * mockbird_kv.h -- C ABI of the B200 KV-ring / RoPE / attention library.
+ *
+ * Drop-in for the KV-cache/attention dispatch of the reference's WebGPU engine
+ * (liyu1981/mockbird, src/lib/tts/engine/).  Every entry point names the
+ * reference interface it replaces.  Plain pointers and sizes only: device
+ * pointers are CUDA device addresses, `cuda_stream` is a cudaStream_t (NULL =
+ * the legacy default stream), host pointers are ordinary process memory.
+ *
+ * Geometry.  One context owns, on one GPU, the rings of `streams` independent
+ * synthesis streams for `layers` layers:
+ *     kv[layer][stream][0=K,1=V][head][slot][64]   storage dtype (f32/bf16/f16)
+ *     slot_pos[layer][stream][slot]                 int32 absolute position, -1 = empty
+ * A query at position p attends the live slots among [0, min(p + 1, capacity)):
+ * slot j is live iff slot_pos[j] >= 0 and 0 <= p - slot_pos[j] < capacity
+ * (kernels-decode.ts:622-623).  Appends go to slot p % capacity
+ * (kernels-decode.ts:709); K is stored after RoPE, V raw.
+ *
+ * Row layouts (head-major, kernels-decode.ts:216-241):
+ *     qkv row  [3][heads][64] f32   (q | k | v, 2304 floats at 12 heads)
+ *     ctx row  [heads][64]    f32
+ *
+ * Errors.  Every call returns an mb_status; mb_last_error() holds the text.
+ * Checks a kernel makes on device data (a stream id or position read from a
+ * device array) are reported by the next mb_sync() as MB_ERR_DEVICE; the
+ * offending item is skipped, never dereferenced.
+ *
+ * Threading.  A context is not thread-safe; calls are asynchronous on the
+ * given CUDA stream unless documented as blocking.  One item per stream per
+ * call: two items with the same stream id in one call race.
+ */
+#ifndef MOCKBIRD_KV_H
+#define MOCKBIRD_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MB_API __attribute__((visibility("default")))
+#else
+#define MB_API
+#endif
+
+typedef struct mb_ctx mb_ctx;
+
+enum mb_dtype { MB_F32 = 0, MB_BF16 = 1, MB_F16 = 2 };
+
+enum mb_status {
+    MB_OK = 0,
+    MB_ERR_ARG = 1,      /* null pointer, bad size, bad config field            */
+    MB_ERR_STREAM = 2,   /* stream index out of range, or repeated in one call  */
+    MB_ERR_LAYER = 3,    /* layer index out of range                            */
+    MB_ERR_POSITION = 4, /* position < 0 or >= max_position                     */
+    MB_ERR_CAPACITY = 5, /* position >= capacity on a non-wrapping ring
+                            (decode.ts:719-724), or prefill rows > capacity     */
+    MB_ERR_CUDA = 6,     /* a CUDA runtime call failed                          */
+    MB_ERR_DEVICE = 7,   /* a kernel rejected an item (see mb_last_error)       */
+    MB_ERR_OOM = 8,      /* device allocation failed                            */
+    MB_ERR_TIMEOUT = 9   /* a bounded device-side wait gave up                  */
+};
+
+typedef struct mb_config {
+    int32_t layers;       /* transformer layers with a ring (12)                        */
+    int32_t heads;        /* attention heads (12)                                       */
+    int32_t head_dim;     /* must be 64                                                 */
+    int32_t capacity;     /* ring slots per (layer, stream); gpu.ts:300-306 maxSlots   */
+    int32_t streams;      /* independent stream rings in this context                   */
+    int32_t dtype;        /* enum mb_dtype of the ring storage                          */
+    int32_t wrap;         /* 1: slot = position % capacity (codec.ts ring semantics);
+                             0: position >= capacity is MB_ERR_CAPACITY (global ring)  */
+    int32_t max_position; /* positions must be < this (RoPE table rows); 0 -> 65536     */
+    float rope_theta;     /* RoPE base, 10000 (docs/moss-tts-runtime-analysis.md:929)  */
+    int32_t device;       /* CUDA device ordinal                                        */
+    int32_t max_batch;    /* largest item count per call; 0 -> streams                  */
+} mb_config;
+
+/* Device addresses and strides of a context's state (for tests and tools). */
+typedef struct mb_ring_info {
+    void* kv;              /* kv[layer][stream][2][head][slot][64]  */
+    int32_t* slot_pos;     /* slot_pos[layer][stream][slot]         */
+    size_t kv_bytes;
+    size_t elem_bytes;     /* 4 (f32) or 2 (bf16/f16)               */
+    size_t scratch_bytes;  /* split-K partials + counters           */
+} mb_ring_info;
+
+/* Fill `cfg` with the reference's global-ring geometry: 12 layers, 12 heads,
+ * 64 dims, capacity 570 (gpu.ts:362), fp32, no wrap, theta 10000, device 0. */
+MB_API void mb_config_default(mb_config* cfg);
+
+/* Allocate the rings (all slots empty), the RoPE table and the split-K scratch
+ * on cfg->device.  Replaces the KV parts of createGpuEngineFor (gpu.ts:316-388):
+ * the PrefillRunner kv buffer (prefill.ts:156-160) and the CodecRunner ring +
+ * slot array (codec.ts:204-245). */
+MB_API int mb_create(const mb_config* cfg, mb_ctx** out);
+
+/* Free everything the context owns.  GpuTtsEngine.dispose (gpu.ts:283-291). */
+MB_API int mb_destroy(mb_ctx* ctx);
+
+/* Mark every slot of `stream` (all streams if stream < 0) empty, all layers.
+ * WgpuTtsEngineImpl.reset (gpu.ts:237-242) / CodecRunner.resetRings (codec.ts:279-282). */
+MB_API int mb_reset(mb_ctx* ctx, int32_t stream, void* cuda_stream);
+
+/* ROPE_SPLIT_RING / ROPE_SPLIT_CODEC (kernels-decode.ts:216-241, 679-714),
+ * dispatched at decode.ts:527-535: for each of n items, rope Q IN PLACE in the
+ * qkv row, rope K into the key ring and copy V into the value ring at slot
+ * position % capacity, and record the position in slot_pos.
+ * streams, positions: device int32[n]; qkv: device f32 [n][3*heads*64]. */
+MB_API int mb_rope_append(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* streams,
+                          const int32_t* positions, float* qkv, void* cuda_stream);
+
+/* ATTEND_RING / ATTEND_RING_CODEC (kernels-decode.ts:254-327, 590-667),
+ * dispatched at decode.ts:536-552: one already-roped query per item against the
+ * item's live window, scale 0.125.  q: device f32, row i at q + i*q_stride
+ * (q_stride = 3*heads*64 reads the Q block of a roped qkv row);
+ * out: device f32 [n][heads*64]. */
+MB_API int mb_attend(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* streams,
+                     const int32_t* positions, const float* q, int32_t q_stride, float* out,
+                     void* cuda_stream);
+
+/* The hot path: mb_rope_append followed by mb_attend in ONE launch
+ * (decode.ts:527-552 for n streams at once).  qkv is read-only here (the
+ * roped Q stays on chip); out: device f32 [n][heads*64]. */
+MB_API int mb_append_attend(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* streams,
+                            const int32_t* positions, const float* qkv, float* out,
+                            void* cuda_stream);
+
+/* mb_append_attend for every layer of one decode step: the layer loop of
+ * DecodeRunner.globalStep (decode.ts:735-748), one launch per layer from C.
+ * qkv: device f32 [layers][n][3*heads*64]; out: device f32 [layers][n][heads*64]. */
+MB_API int mb_decode_step(mb_ctx* ctx, int32_t n, const int32_t* streams, const int32_t* positions,
+                          const float* qkv, float* out, void* cuda_stream);
+
+/* mb_append_attend with HOST arrays: copies streams/positions/qkv in, runs,
+ * copies out and waits for the result (the per-layer readback of
+ * DecodeRunner, decode.ts:450-463).  Validates every item on the host first. */
+MB_API int mb_append_attend_host(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* streams,
+                                 const int32_t* positions, const float* qkv, float* out,
+                                 void* cuda_stream);
+
+/* One global decode step for n streams through ALL layers, HOST arrays:
+ * qkv [layers][n][3*heads*64], out [layers][n][heads*64]; one copy in, one
+ * launch per layer, one copy out, blocking -- the granularity of
+ * DecodeRunner.globalStep (decode.ts:712-775: one submit, one readback). */
+MB_API int mb_decode_step_host(mb_ctx* ctx, int32_t n, const int32_t* streams, const int32_t* positions,
+                               const float* qkv, float* out, void* cuda_stream);
+
+/* Causal prefill of positions 0..rows-1 of n streams for one layer:
+ * ROPE_SPLIT_CACHE + ATTENTION_SCORES/_SOFTMAX/_APPLY (kernels-batch.ts:194-350,
+ * dispatched at prefill.ts:424-462).  The item's slots >= rows are marked empty
+ * first (a prefill starts an utterance).  qkv: device f32 [n][rows][3*heads*64]
+ * (read-only), out: device f32 [n][rows][heads*64].  rows <= capacity. */
+MB_API int mb_prefill(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* streams, int32_t rows,
+                      const float* qkv, float* out, void* cuda_stream);
+
+/* The live window of (layer, stream) for a query at `position`, in POSITION
+ * order: W = min(position + 1, capacity) rows, row w = position - W + 1 + w.
+ * k_out, v_out: device [heads][W][64] in the storage dtype; slots_out: device
+ * int32[W], the slot holding that position or -1 (its rows are zero).
+ * PrefillRunner.readLayerCache (prefill.ts:644-664), generalised to the wrap. */
+MB_API int mb_gather(mb_ctx* ctx, int32_t layer, int32_t stream, int32_t position, void* k_out,
+                     void* v_out, int32_t* slots_out, void* cuda_stream);
+
+/* Write `count` rows of already-roped K and raw V, [heads][count][64] in the
+ * storage dtype (device pointers), at positions first_position.. of (layer,
+ * stream), recording the positions.  The writeBuffer of PrefillRunner.poisonKv
+ * (prefill.ts:610-620); also restores a gathered window. */
+MB_API int mb_ring_write(mb_ctx* ctx, int32_t layer, int32_t stream, int32_t first_position, int32_t count,
+                         const void* k, const void* v, void* cuda_stream);
+
+/* Wait for `cuda_stream` and report device-side rejections (then clear them). */
+MB_API int mb_sync(mb_ctx* ctx, void* cuda_stream);
+
+/* Device addresses and sizes of the context's state. */
+MB_API int mb_ring_info_get(const mb_ctx* ctx, mb_ring_info* out);
+
+/* Text of the last error on this context ("" if none). */
+MB_API const char* mb_last_error(const mb_ctx* ctx);
+
+/* Library version string. */
+MB_API const char* mb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOCKBIRD_KV_H */

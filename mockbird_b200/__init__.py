@@ -1,0 +1,11 @@
+"""mockbird_b200 -- B200 (sm_100a) KV-ring / RoPE / attention path of Mockbird's
+MOSS-TTS-Nano decoder, behind the C ABI of include/mockbird_kv.h.
+
+    from mockbird_b200 import KvRing
+    ring = KvRing(capacity=512, streams=64, wrap=True)
+    ctx = ring.append_attend(layer, streams, positions, qkv)   # one fused launch
+"""
+from .engine import KvRing, MockbirdError  # noqa: F401
+from ._lib import LIB_PATH, load  # noqa: F401
+
+__all__ = ["KvRing", "MockbirdError", "LIB_PATH", "load"]

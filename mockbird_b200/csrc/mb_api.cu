@@ -1,0 +1,399 @@
+// Host side of the C ABI declared in include/mockbird_kv.h: context lifetime,
+// argument validation, staging for the host-array entry points, and launches.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <vector>
+
+#include "mb_internal.cuh"
+
+using namespace mb;
+
+#define MB_VERSION "mockbird-b200 0.1.0 (sm_100a)"
+
+namespace {
+
+int fail(mb_ctx* c, int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (c) c->last_error = buf;
+    return code;
+}
+
+int cuda_fail(mb_ctx* c, cudaError_t e, const char* what) {
+    return fail(c, e == cudaErrorMemoryAllocation ? MB_ERR_OOM : MB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call, what)                                        \
+    do {                                                      \
+        cudaError_t e_ = (call);                              \
+        if (e_ != cudaSuccess) return cuda_fail(c, e_, what); \
+    } while (0)
+
+// Switch to the context's device for the duration of a call.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_layer(mb_ctx* c, int layer) {
+    if (layer < 0 || layer >= c->cfg.layers)
+        return fail(c, MB_ERR_LAYER, "layer %d out of range [0, %d)", layer, c->cfg.layers);
+    return MB_OK;
+}
+
+int check_batch(mb_ctx* c, int n) {
+    if (n < 0 || n > c->cfg.max_batch)
+        return fail(c, MB_ERR_ARG, "item count %d out of range [0, %d] (max_batch)", n, c->cfg.max_batch);
+    return MB_OK;
+}
+
+// Host-side checks of one position (decode.ts:719-724 for the non-wrapping ring).
+int check_position(mb_ctx* c, int pos) {
+    if (pos < 0 || pos >= c->cfg.max_position)
+        return fail(c, MB_ERR_POSITION, "position %d out of range [0, %d)", pos, c->cfg.max_position);
+    if (!c->cfg.wrap && pos >= c->cfg.capacity)
+        return fail(c, MB_ERR_CAPACITY,
+                    "decode position %d exceeds the KV ring (%d slots); it must be sized prefill_rows + "
+                    "max_new_frames",
+                    pos, c->cfg.capacity);
+    return MB_OK;
+}
+
+int check_items_host(mb_ctx* c, int n, const int32_t* streams, const int32_t* positions) {
+    std::vector<char> seen(c->cfg.streams, 0);
+    for (int i = 0; i < n; i++) {
+        const int s = streams[i];
+        if (s < 0 || s >= c->cfg.streams)
+            return fail(c, MB_ERR_STREAM, "item %d: stream %d out of range [0, %d)", i, s, c->cfg.streams);
+        if (seen[s]) return fail(c, MB_ERR_STREAM, "item %d: stream %d appears twice in one call", i, s);
+        seen[s] = 1;
+        int rc = check_position(c, positions[i]);
+        if (rc) return rc;
+    }
+    return MB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+MB_API const char* mb_version(void) { return MB_VERSION; }
+
+MB_API void mb_config_default(mb_config* cfg) {
+    if (!cfg) return;
+    cfg->layers = 12;
+    cfg->heads = 12;
+    cfg->head_dim = 64;
+    cfg->capacity = 570;
+    cfg->streams = 1;
+    cfg->dtype = MB_F32;
+    cfg->wrap = 0;
+    cfg->max_position = 65536;
+    cfg->rope_theta = 10000.0f;
+    cfg->device = 0;
+    cfg->max_batch = 0;
+}
+
+MB_API const char* mb_last_error(const mb_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
+    if (!cfg_in || !out) return MB_ERR_ARG;
+    *out = nullptr;
+    mb_config cfg = *cfg_in;
+    if (cfg.max_position <= 0) cfg.max_position = 65536;
+    if (cfg.max_batch <= 0) cfg.max_batch = cfg.streams;
+    if (cfg.head_dim != HD || cfg.layers <= 0 || cfg.heads <= 0 || cfg.heads > 64 || cfg.capacity <= 0 ||
+        cfg.streams <= 0 || cfg.dtype < MB_F32 || cfg.dtype > MB_F16 || cfg.max_batch > 65535 ||
+        !(cfg.rope_theta > 0.0f))
+        return MB_ERR_ARG;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || cfg.device < 0 || cfg.device >= ndev) return MB_ERR_CUDA;
+
+    mb_ctx* c = new mb_ctx();
+    c->cfg = cfg;
+    c->esize = cfg.dtype == MB_F32 ? 4 : 2;
+    DeviceGuard g(cfg.device);
+    auto bail = [&](int rc) {
+        mb_destroy(c);
+        return rc;
+    };
+    if (!g.ok) return bail(MB_ERR_CUDA);
+
+    const size_t slots = (size_t)cfg.layers * cfg.streams * cfg.capacity;
+    c->kv_bytes = slots * 2 * cfg.heads * HD * c->esize;
+    if (cudaMalloc(&c->kv, c->kv_bytes) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMalloc(&c->slot_pos, slots * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMemset(c->kv, 0, c->kv_bytes) != cudaSuccess) return bail(MB_ERR_CUDA);
+    if (cudaMemset(c->slot_pos, 0xFF, slots * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_CUDA);
+
+    // RoPE table: angle and cos/sin in fp64, rounded once to fp32
+    // (tools/onnx-probe/ref-decode.mjs:111-124 evaluates them in fp64)
+    {
+        std::vector<float2> tab((size_t)cfg.max_position * 32);
+        for (int p = 0; p < cfg.max_position; p++)
+            for (int i = 0; i < 32; i++) {
+                const double inv = pow((double)cfg.rope_theta, -(2.0 * i) / 64.0);
+                const double a = (double)p * inv;
+                tab[(size_t)p * 32 + i] = make_float2((float)cos(a), (float)sin(a));
+            }
+        if (cudaMalloc(&c->rope, tab.size() * sizeof(float2)) != cudaSuccess) return bail(MB_ERR_OOM);
+        if (cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(MB_ERR_CUDA);
+    }
+    if (cudaMalloc(&c->d_err, sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMemset(c->d_err, 0, sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_CUDA);
+
+    // split-K scratch: one (m, l, acc[64]) partial per chunk and a ticket per (item, head)
+    const int rows = chunk_rows(cfg.dtype);
+    c->scratch.max_splits = (cfg.capacity + rows - 1) / rows;
+    const size_t part_bytes = (size_t)cfg.max_batch * cfg.heads * c->scratch.max_splits * (2 + HD) * sizeof(float);
+    const size_t cnt_bytes = (size_t)cfg.max_batch * cfg.heads * sizeof(int32_t);
+    c->scratch_bytes = part_bytes + cnt_bytes;
+    if (cudaMalloc(&c->scratch.part, part_bytes) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMalloc(&c->scratch.counters, cnt_bytes) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMemset(c->scratch.counters, 0, cnt_bytes) != cudaSuccess) return bail(MB_ERR_CUDA);
+
+    // staging for the host-array entry points
+    const size_t hid = (size_t)cfg.heads * HD;
+    if (cudaMalloc(&c->d_streams, cfg.max_batch * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMalloc(&c->d_positions, cfg.max_batch * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMalloc(&c->d_qkv, (size_t)cfg.layers * cfg.max_batch * 3 * hid * sizeof(float)) != cudaSuccess)
+        return bail(MB_ERR_OOM);
+    if (cudaMalloc(&c->d_out, (size_t)cfg.layers * cfg.max_batch * hid * sizeof(float)) != cudaSuccess)
+        return bail(MB_ERR_OOM);
+    if (cudaDeviceSynchronize() != cudaSuccess) return bail(MB_ERR_CUDA);
+    *out = c;
+    return MB_OK;
+}
+
+MB_API int mb_destroy(mb_ctx* c) {
+    if (!c) return MB_ERR_ARG;
+    {
+        DeviceGuard g(c->cfg.device);
+        void* ptrs[] = {c->kv, c->slot_pos, c->rope, c->d_err, c->scratch.part, c->scratch.counters,
+                        c->d_streams, c->d_positions, c->d_qkv, c->d_out};
+        for (void* p : ptrs)
+            if (p) cudaFree(p);
+    }
+    delete c;
+    return MB_OK;
+}
+
+MB_API int mb_reset(mb_ctx* c, int32_t stream, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    if (stream >= c->cfg.streams) return fail(c, MB_ERR_STREAM, "stream %d out of range", stream);
+    DeviceGuard g(c->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    CK(launch_reset(c, stream, st), "reset");
+    if (stream < 0) {  // a full reset also re-arms the split-K tickets
+        CK(cudaMemsetAsync(c->scratch.counters, 0, (size_t)c->cfg.max_batch * c->cfg.heads * sizeof(int32_t), st),
+           "reset tickets");
+    }
+    return MB_OK;
+}
+
+MB_API int mb_rope_append(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams, const int32_t* positions,
+                          float* qkv, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_layer(c, layer)) || (rc = check_batch(c, n))) return rc;
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !qkv || !aligned(qkv, 16))
+        return fail(c, MB_ERR_ARG, "null or misaligned device pointer");
+    DeviceGuard g(c->cfg.device);
+    CK(launch_rope_append(c->cfg.dtype, ring_view(c, layer), n, streams, positions, qkv,
+                          static_cast<cudaStream_t>(cuda_stream)),
+       "rope_append launch");
+    return MB_OK;
+}
+
+MB_API int mb_attend(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams, const int32_t* positions,
+                     const float* q, int32_t q_stride, float* out, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_layer(c, layer)) || (rc = check_batch(c, n))) return rc;
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !q || !out || !aligned(q, 16) || !aligned(out, 16) || q_stride < c->cfg.heads * HD ||
+        (q_stride & 1))
+        return fail(c, MB_ERR_ARG, "null/misaligned device pointer or bad q_stride %d", q_stride);
+    DeviceGuard g(c->cfg.device);
+    CK(launch_decode(c->cfg.dtype, false, ring_view(c, layer), c->scratch, n, streams, positions, q, q_stride, out,
+                     static_cast<cudaStream_t>(cuda_stream)),
+       "attend launch");
+    return MB_OK;
+}
+
+MB_API int mb_append_attend(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams, const int32_t* positions,
+                            const float* qkv, float* out, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_layer(c, layer)) || (rc = check_batch(c, n))) return rc;
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !qkv || !out || !aligned(qkv, 16) || !aligned(out, 16))
+        return fail(c, MB_ERR_ARG, "null or misaligned device pointer");
+    DeviceGuard g(c->cfg.device);
+    CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, streams, positions, qkv,
+                     3 * c->cfg.heads * HD, out, static_cast<cudaStream_t>(cuda_stream)),
+       "append_attend launch");
+    return MB_OK;
+}
+
+MB_API int mb_decode_step(mb_ctx* c, int32_t n, const int32_t* streams, const int32_t* positions, const float* qkv,
+                          float* out, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_batch(c, n))) return rc;
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !qkv || !out || !aligned(qkv, 16) || !aligned(out, 16))
+        return fail(c, MB_ERR_ARG, "null or misaligned device pointer");
+    DeviceGuard g(c->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const size_t hid = (size_t)c->cfg.heads * HD;
+    for (int layer = 0; layer < c->cfg.layers; layer++)
+        CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, streams, positions,
+                         qkv + (size_t)layer * n * 3 * hid, 3 * (int)hid, out + (size_t)layer * n * hid, st),
+           "append_attend launch");
+    return MB_OK;
+}
+
+MB_API int mb_sync(mb_ctx* c, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    DeviceGuard g(c->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    CK(cudaStreamSynchronize(st), "synchronize");
+    int32_t bits = 0;
+    CK(cudaMemcpy(&bits, c->d_err, sizeof bits, cudaMemcpyDeviceToHost), "read device status");
+    if (!bits) return MB_OK;
+    CK(cudaMemset(c->d_err, 0, sizeof(int32_t)), "clear device status");
+    if (bits & DERR_TIMEOUT)
+        return fail(c, MB_ERR_TIMEOUT, "a bounded device-side wait gave up (bits 0x%x)", bits);
+    return fail(c, MB_ERR_DEVICE, "a kernel rejected an item:%s%s%s", (bits & DERR_STREAM) ? " stream out of range" : "",
+                (bits & DERR_POSITION) ? " position out of range" : "",
+                (bits & DERR_CAPACITY) ? " position beyond a non-wrapping ring" : "");
+}
+
+MB_API int mb_append_attend_host(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams,
+                                 const int32_t* positions, const float* qkv, float* out, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_layer(c, layer)) || (rc = check_batch(c, n))) return rc;
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !qkv || !out) return fail(c, MB_ERR_ARG, "null host pointer");
+    if ((rc = check_items_host(c, n, streams, positions))) return rc;
+    DeviceGuard g(c->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const size_t hid = (size_t)c->cfg.heads * HD;
+    CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy streams");
+    CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy positions");
+    CK(cudaMemcpyAsync(c->d_qkv, qkv, n * 3 * hid * sizeof(float), cudaMemcpyHostToDevice, st), "copy qkv");
+    CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, c->d_streams, c->d_positions, c->d_qkv,
+                     3 * (int)hid, c->d_out, st),
+       "append_attend launch");
+    CK(cudaMemcpyAsync(out, c->d_out, n * hid * sizeof(float), cudaMemcpyDeviceToHost, st), "copy out");
+    return mb_sync(c, cuda_stream);
+}
+
+MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, const int32_t* positions,
+                               const float* qkv, float* out, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_batch(c, n))) return rc;
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !qkv || !out) return fail(c, MB_ERR_ARG, "null host pointer");
+    if ((rc = check_items_host(c, n, streams, positions))) return rc;
+    DeviceGuard g(c->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const size_t hid = (size_t)c->cfg.heads * HD, L = c->cfg.layers;
+    CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy streams");
+    CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy positions");
+    CK(cudaMemcpyAsync(c->d_qkv, qkv, L * n * 3 * hid * sizeof(float), cudaMemcpyHostToDevice, st), "copy qkv");
+    for (int layer = 0; layer < (int)L; layer++)
+        CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, c->d_streams, c->d_positions,
+                         c->d_qkv + (size_t)layer * n * 3 * hid, 3 * (int)hid, c->d_out + (size_t)layer * n * hid, st),
+           "append_attend launch");
+    CK(cudaMemcpyAsync(out, c->d_out, L * n * hid * sizeof(float), cudaMemcpyDeviceToHost, st), "copy out");
+    return mb_sync(c, cuda_stream);
+}
+
+MB_API int mb_prefill(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams, int32_t rows, const float* qkv,
+                      float* out, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_layer(c, layer)) || (rc = check_batch(c, n))) return rc;
+    if (n == 0) return MB_OK;
+    if (rows <= 0) return fail(c, MB_ERR_ARG, "prefill called with no rows");
+    if (rows > c->cfg.capacity)
+        return fail(c, MB_ERR_CAPACITY, "prefill of %d rows exceeds the ring capacity %d", rows, c->cfg.capacity);
+    if (rows > c->cfg.max_position) return fail(c, MB_ERR_POSITION, "prefill rows beyond max_position");
+    if (!streams || !qkv || !out || !aligned(qkv, 16) || !aligned(out, 16))
+        return fail(c, MB_ERR_ARG, "null or misaligned device pointer");
+    DeviceGuard g(c->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    void* stage = nullptr;
+    CK(cudaMallocAsync(&stage, prefill_stage_bytes(c->cfg.dtype, n, c->cfg.heads, rows), st), "prefill stage");
+    cudaError_t e = launch_prefill(c->cfg.dtype, ring_view(c, layer), n, streams, rows, qkv, out, stage, st);
+    cudaError_t e2 = cudaFreeAsync(stage, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "prefill launch");
+    if (e2 != cudaSuccess) return cuda_fail(c, e2, "prefill stage free");
+    return MB_OK;
+}
+
+MB_API int mb_gather(mb_ctx* c, int32_t layer, int32_t stream, int32_t position, void* k_out, void* v_out,
+                     int32_t* slots_out, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_layer(c, layer))) return rc;
+    if (stream < 0 || stream >= c->cfg.streams) return fail(c, MB_ERR_STREAM, "stream %d out of range", stream);
+    if ((rc = check_position(c, position))) return rc;
+    if (!k_out || !v_out || !slots_out) return fail(c, MB_ERR_ARG, "null device pointer");
+    DeviceGuard g(c->cfg.device);
+    CK(launch_gather(c->cfg.dtype, ring_view(c, layer), stream, position, k_out, v_out, slots_out,
+                     static_cast<cudaStream_t>(cuda_stream)),
+       "gather launch");
+    return MB_OK;
+}
+
+MB_API int mb_ring_write(mb_ctx* c, int32_t layer, int32_t stream, int32_t first_position, int32_t count,
+                         const void* k, const void* v, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    int rc;
+    if ((rc = check_layer(c, layer))) return rc;
+    if (stream < 0 || stream >= c->cfg.streams) return fail(c, MB_ERR_STREAM, "stream %d out of range", stream);
+    if (count <= 0 || count > c->cfg.capacity)
+        return fail(c, MB_ERR_ARG, "count %d out of range [1, capacity %d]", count, c->cfg.capacity);
+    if ((rc = check_position(c, first_position)) || (rc = check_position(c, first_position + count - 1))) return rc;
+    if (!k || !v) return fail(c, MB_ERR_ARG, "null device pointer");
+    DeviceGuard g(c->cfg.device);
+    CK(launch_ring_write(c->cfg.dtype, ring_view(c, layer), stream, first_position, count, k, v,
+                         static_cast<cudaStream_t>(cuda_stream)),
+       "ring_write launch");
+    return MB_OK;
+}
+
+MB_API int mb_ring_info_get(const mb_ctx* c, mb_ring_info* out) {
+    if (!c || !out) return MB_ERR_ARG;
+    out->kv = c->kv;
+    out->slot_pos = c->slot_pos;
+    out->kv_bytes = c->kv_bytes;
+    out->elem_bytes = c->esize;
+    out->scratch_bytes = c->scratch_bytes;
+    return MB_OK;
+}
+
+}  // extern "C"

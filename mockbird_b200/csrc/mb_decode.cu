@@ -1,0 +1,403 @@
+// Decode-side kernels: append + RoPE into the ring, and split-K flash-decode
+// attention over the live window, fused into one launch for the hot path.
+//
+// Reference semantics (liyu1981/mockbird, src/lib/tts/engine/):
+//   ROPE_SPLIT_RING  kernels-decode.ts:216-241 / ROPE_SPLIT_CODEC :679-714
+//   ATTEND_RING      kernels-decode.ts:254-327 / ATTEND_RING_CODEC :590-667
+// The reference runs one 64-lane workgroup per head with a serial 64-FMA dot per
+// lane and six barriers per 64-slot tile.  Here every (item, head) window is cut
+// into 16 KB chunks of K and V; each CTA pulls its chunk into shared memory with
+// two bulk copies (cp.async.bulk, no multicast), scores it with bank-conflict-
+// free rotated 16-byte reads, and leaves an (m, l, acc[64]) partial.  The last
+// CTA of an (item, head) to finish folds the partials (online-softmax rescale)
+// and writes the context row.  No tensor cores: one query per head is a GEMV.
+#include "mb_internal.cuh"
+
+namespace mb {
+
+// ---------------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
+// dst, src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Bounded wait for `phase` of `bar`; false if the bound ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, long long limit) {
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(phase)
+            : "memory");
+        if (done) return true;
+        if (clock64() - t0 > limit) return false;
+    }
+}
+
+constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s at 1.9 GHz; a bulk copy takes microseconds
+
+// ---------------------------------------------------------------- storage types
+
+template <typename T>
+struct Store;
+template <>
+struct Store<float> {
+    __device__ static float2 load2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+    __device__ static void store2(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
+    __device__ static float2 round2(float2 v) { return v; }
+};
+template <>
+struct Store<__nv_bfloat16> {
+    __device__ static float2 load2(const __nv_bfloat16* p) {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    }
+    __device__ static void store2(__nv_bfloat16* p, float2 v) {
+        *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v.x, v.y);
+    }
+    __device__ static float2 round2(float2 v) { return __bfloat1622float2(__floats2bfloat162_rn(v.x, v.y)); }
+};
+template <>
+struct Store<__half> {
+    __device__ static float2 load2(const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p)); }
+    __device__ static void store2(__half* p, float2 v) {
+        *reinterpret_cast<__half2*>(p) = __floats2half2_rn(v.x, v.y);
+    }
+    __device__ static float2 round2(float2 v) { return __half22float2(__floats2half2_rn(v.x, v.y)); }
+};
+
+// dot of 8 consecutive stored elements (one 16-byte vector) with q[0..7]
+__device__ __forceinline__ float dot8(uint4 raw, const float4* q2, float acc, __nv_bfloat16*) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float4 qa = q2[0], qb = q2[1];
+    float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    float2 c = __bfloat1622float2(h[2]), d = __bfloat1622float2(h[3]);
+    acc = fmaf(a.x, qa.x, acc); acc = fmaf(a.y, qa.y, acc);
+    acc = fmaf(b.x, qa.z, acc); acc = fmaf(b.y, qa.w, acc);
+    acc = fmaf(c.x, qb.x, acc); acc = fmaf(c.y, qb.y, acc);
+    acc = fmaf(d.x, qb.z, acc); acc = fmaf(d.y, qb.w, acc);
+    return acc;
+}
+__device__ __forceinline__ float dot8(uint4 raw, const float4* q2, float acc, __half*) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+    float4 qa = q2[0], qb = q2[1];
+    float2 a = __half22float2(h[0]), b = __half22float2(h[1]);
+    float2 c = __half22float2(h[2]), d = __half22float2(h[3]);
+    acc = fmaf(a.x, qa.x, acc); acc = fmaf(a.y, qa.y, acc);
+    acc = fmaf(b.x, qa.z, acc); acc = fmaf(b.y, qa.w, acc);
+    acc = fmaf(c.x, qb.x, acc); acc = fmaf(c.y, qb.y, acc);
+    acc = fmaf(d.x, qb.z, acc); acc = fmaf(d.y, qb.w, acc);
+    return acc;
+}
+
+// RoPE of one (even, odd) pair: out = (a c - b s, b c + a s) with every product
+// and sum rounded separately (no FMA) so the stored K matches a CPU restatement
+// bit for bit (kernels-decode.ts:220-232; partner -v[d+1] / +v[d-1]).
+__device__ __forceinline__ float2 rope_pair(float2 v, float2 cs) {
+    return make_float2(__fadd_rn(__fmul_rn(v.x, cs.x), -__fmul_rn(v.y, cs.y)),
+                       __fadd_rn(__fmul_rn(v.y, cs.x), __fmul_rn(v.x, cs.y)));
+}
+
+// Validate one item against the ring; on failure record why (every thread of
+// the CTA evaluates the same condition, so the early return is uniform).
+__device__ __forceinline__ bool item_ok(const RingView& r, int s, int pos) {
+    int bad = 0;
+    if (s < 0 || s >= r.streams) bad |= DERR_STREAM;
+    if (pos < 0 || pos >= r.max_position) bad |= DERR_POSITION;
+    else if (!r.wrap && pos >= r.capacity) bad |= DERR_CAPACITY;
+    if (bad && threadIdx.x == 0) atomicOr(r.err, bad);
+    return bad == 0;
+}
+
+// ---------------------------------------------------------------- append (a1/a3)
+
+// One CTA per item, one thread per (head, pair): Q roped in place, K roped and V
+// copied into slot pos % C, slot_pos[slot] = pos.
+template <typename T>
+__global__ void __launch_bounds__(384) rope_append_kernel(RingView r, const int32_t* __restrict__ streams,
+                                                          const int32_t* __restrict__ positions, float* qkv) {
+    const int item = blockIdx.x;
+    const int s = streams[item], pos = positions[item];
+    if (!item_ok(r, s, pos)) return;
+    const int H = r.heads, HID = H * HD, C = r.capacity, slot = pos % C;
+    float* row = qkv + (size_t)item * 3 * HID;
+    for (int t = threadIdx.x; t < H * 32; t += blockDim.x) {
+        const int h = t >> 5, i = t & 31;
+        const float2 cs = r.rope[(size_t)pos * 32 + i];
+        float2 q = *reinterpret_cast<const float2*>(row + h * HD + 2 * i);
+        float2 k = *reinterpret_cast<const float2*>(row + HID + h * HD + 2 * i);
+        float2 v = *reinterpret_cast<const float2*>(row + 2 * HID + h * HD + 2 * i);
+        *reinterpret_cast<float2*>(row + h * HD + 2 * i) = rope_pair(q, cs);
+        T* kd = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD + (size_t)slot * HD + 2 * i;
+        T* vd = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD + (size_t)slot * HD + 2 * i;
+        Store<T>::store2(kd, rope_pair(k, cs));
+        Store<T>::store2(vd, v);
+    }
+    if (threadIdx.x == 0) r.slot_pos[(size_t)s * C + slot] = pos;
+}
+
+// ---------------------------------------------------------------- decode attention
+
+template <typename T>
+struct DecodeShape {
+    static constexpr int E = sizeof(T);
+    static constexpr int ROWS = 16384 / (HD * E);  // slots per chunk: 64 (f32) / 128 (16-bit)
+    static constexpr int TPR = E / 2;              // score threads per slot: 2 (f32) / 1 (16-bit)
+    static constexpr int ROW_BYTES = HD * E;
+};
+
+// grid (max_splits, heads, n), 128 threads.  APPEND: q_in is the raw qkv row
+// (stride q_stride) and this launch also appends K/V; otherwise q_in holds an
+// already-roped query.
+template <typename T, bool APPEND>
+__global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, const int32_t* __restrict__ streams,
+                                                     const int32_t* __restrict__ positions,
+                                                     const float* __restrict__ q_in, int q_stride,
+                                                     float* __restrict__ out) {
+    using S = DecodeShape<T>;
+    constexpr int ROWS = S::ROWS, TPR = S::TPR, RB = S::ROW_BYTES;
+    __shared__ __align__(128) unsigned char sk[ROWS * RB];
+    __shared__ __align__(128) unsigned char sv[ROWS * RB];
+    __shared__ __align__(16) float qs[HD];
+    __shared__ float ps[ROWS];
+    __shared__ float red[4][HD];
+    __shared__ float wmax[4], wsum[4];
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ int ticket;
+
+    const int c = blockIdx.x, h = blockIdx.y, item = blockIdx.z, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int s = streams[item], pos = positions[item];
+    if (!item_ok(r, s, pos)) return;
+    const int C = r.capacity, H = r.heads, HID = H * HD;
+    const int count = min(pos + 1, C);
+    const int nsplit = (count + ROWS - 1) / ROWS;
+    if (c >= nsplit) return;
+    const int j0 = c * ROWS, rows = min(ROWS, count - j0);
+    const int newslot = pos % C;
+    const bool has_new = APPEND && newslot >= j0 && newslot < j0 + rows;
+
+    T* kbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD;
+    T* vbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD;
+
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t bytes = (uint32_t)rows * RB;
+        mbar_expect_tx(&bar[0], bytes);
+        bulk_g2s(sk, kbase + (size_t)j0 * HD, bytes, &bar[0]);
+        mbar_expect_tx(&bar[1], bytes);
+        bulk_g2s(sv, vbase + (size_t)j0 * HD, bytes, &bar[1]);
+    }
+
+    // query (roped here when appending) and, in the chunk holding the new slot,
+    // the new K/V row: written to the ring and kept for the on-chip substitution
+    const float* row = q_in + (size_t)item * q_stride;
+    float2 knew = make_float2(0.f, 0.f), vnew = make_float2(0.f, 0.f);
+    if (tid < 32) {
+        float2 qv = *reinterpret_cast<const float2*>(row + h * HD + 2 * tid);
+        if (APPEND) qv = rope_pair(qv, r.rope[(size_t)pos * 32 + tid]);
+        qs[2 * tid] = qv.x;
+        qs[2 * tid + 1] = qv.y;
+    } else if (has_new && tid < 64) {
+        const int i = tid - 32;
+        const float2 kv = *reinterpret_cast<const float2*>(row + HID + h * HD + 2 * i);
+        const float2 vv = *reinterpret_cast<const float2*>(row + 2 * HID + h * HD + 2 * i);
+        const float2 kr = rope_pair(kv, r.rope[(size_t)pos * 32 + i]);
+        Store<T>::store2(kbase + (size_t)newslot * HD + 2 * i, kr);
+        Store<T>::store2(vbase + (size_t)newslot * HD + 2 * i, vv);
+        knew = Store<T>::round2(kr);
+        vnew = Store<T>::round2(vv);
+    }
+    if (has_new && h == 0 && tid == 64) r.slot_pos[(size_t)s * C + newslot] = pos;
+
+    // liveness of this thread's score slot (kernels-decode.ts:622-623)
+    const int rr = tid / TPR, part = tid % TPR;
+    bool live = false;
+    if (rr < rows) {
+        const int j = j0 + rr;
+        const int stored = (has_new && j == newslot) ? pos : r.slot_pos[(size_t)s * C + j];
+        live = stored >= 0 && pos - stored >= 0 && pos - stored < C;
+    }
+
+    // ---- K chunk landed?  (bounded; a copy that never lands reads as an empty chunk)
+    bool ok = __syncthreads_and(mbar_wait(&bar[0], 0, WAIT_LIMIT));
+    if (!ok) {
+        if (tid == 0) atomicOr(r.err, DERR_TIMEOUT);
+        live = false;
+    }
+    if (ok && has_new && tid >= 32 && tid < 64) {
+        T* dst = reinterpret_cast<T*>(sk + (newslot - j0) * RB) + 2 * (tid - 32);
+        Store<T>::store2(dst, knew);
+    }
+    __syncthreads();
+
+    // ---- scores: slot rr, 128 bytes per thread, 16-byte vectors read in a
+    // per-slot rotated order so the 8 threads of a shared-memory phase hit 8
+    // different bank quads
+    float dot = 0.f;
+    if (live) {
+        const uint4* kp = reinterpret_cast<const uint4*>(sk + rr * RB + part * 128);
+        const float4* q4 = reinterpret_cast<const float4*>(qs);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int v = (k + rr + 4 * part) & 7;
+            const uint4 raw = kp[v];
+            if constexpr (sizeof(T) == 4) {
+                const float4 kf = *reinterpret_cast<const float4*>(&raw);
+                const float4 qf = q4[part * 8 + v];
+                dot = fmaf(kf.x, qf.x, dot);
+                dot = fmaf(kf.y, qf.y, dot);
+                dot = fmaf(kf.z, qf.z, dot);
+                dot = fmaf(kf.w, qf.w, dot);
+            } else {
+                dot = dot8(raw, q4 + 2 * v, dot, static_cast<T*>(nullptr));
+            }
+        }
+    }
+    if (TPR == 2) dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+    const float sc2 = live ? dot * (SCALE * LOG2E) : -INFINITY;  // log2-domain score
+
+    float m = sc2;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wmax[warp] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+    const float p = live ? exp2f(sc2 - m) : 0.f;
+    if (part == 0 && rr < ROWS) ps[rr] = p;
+    float l = (part == 0) ? p : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) wsum[warp] = l;
+
+    // ---- V chunk
+    ok = __syncthreads_and(mbar_wait(&bar[1], 0, WAIT_LIMIT)) && ok;
+    if (!ok && tid == 0) atomicOr(r.err, DERR_TIMEOUT);
+    if (ok && has_new && tid >= 32 && tid < 64) {
+        T* dst = reinterpret_cast<T*>(sv + (newslot - j0) * RB) + 2 * (tid - 32);
+        Store<T>::store2(dst, vnew);
+    }
+    __syncthreads();
+    l = wsum[0] + wsum[1] + wsum[2] + wsum[3];
+
+    // ---- P.V: warp w takes slots w, w+4, ...; lane owns dims 2*lane, 2*lane+1
+    float a0 = 0.f, a1 = 0.f;
+    if (ok) {
+        for (int j = warp; j < rows; j += 4) {
+            const float pj = ps[j];
+            const float2 vv = Store<T>::load2(reinterpret_cast<const T*>(sv + j * RB) + 2 * lane);
+            a0 = fmaf(pj, vv.x, a0);
+            a1 = fmaf(pj, vv.y, a1);
+        }
+    }
+    red[warp][2 * lane] = a0;
+    red[warp][2 * lane + 1] = a1;
+    __syncthreads();
+    float acc = 0.f;
+    if (tid < HD) acc = red[0][tid] + red[1][tid] + red[2][tid] + red[3][tid];
+
+    float* dst = out + (size_t)item * HID + h * HD;
+    if (nsplit == 1) {
+        if (tid < HD) dst[tid] = l > 0.f ? acc / l : 0.f;
+        return;
+    }
+
+    // ---- split-K: publish the partial; the last CTA of (item, head) combines
+    float* mine = sc.part + (((size_t)item * H + h) * sc.max_splits + c) * (2 + HD);
+    if (tid < HD) mine[2 + tid] = acc;
+    if (tid == 0) {
+        mine[0] = m;
+        mine[1] = l;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket = atomicAdd(&sc.counters[(size_t)item * H + h], 1);
+    __syncthreads();
+    if (ticket != nsplit - 1) return;
+    __threadfence();
+    if (tid < HD) {
+        const float* base = sc.part + ((size_t)item * H + h) * sc.max_splits * (2 + HD);
+        float M = -INFINITY;
+        for (int cc = 0; cc < nsplit; cc++) M = fmaxf(M, __ldcg(base + cc * (2 + HD)));
+        float L = 0.f, o = 0.f;
+        for (int cc = 0; cc < nsplit; cc++) {
+            const float mc = __ldcg(base + cc * (2 + HD));
+            if (mc == -INFINITY) continue;
+            const float w = exp2f(mc - M);
+            L = fmaf(__ldcg(base + cc * (2 + HD) + 1), w, L);
+            o = fmaf(__ldcg(base + cc * (2 + HD) + 2 + tid), w, o);
+        }
+        dst[tid] = L > 0.f ? o / L : 0.f;
+    }
+    if (tid == 0) sc.counters[(size_t)item * H + h] = 0;
+}
+
+// ---------------------------------------------------------------- launchers
+
+template <typename T>
+static cudaError_t rope_append_t(const RingView& r, int n, const int32_t* streams, const int32_t* positions,
+                                 float* qkv, cudaStream_t st) {
+    rope_append_kernel<T><<<n, 384, 0, st>>>(r, streams, positions, qkv);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_t* streams,
+                               const int32_t* positions, float* qkv, cudaStream_t st) {
+    switch (dtype) {
+        case MB_F32: return rope_append_t<float>(r, n, streams, positions, qkv, st);
+        case MB_BF16: return rope_append_t<__nv_bfloat16>(r, n, streams, positions, qkv, st);
+        default: return rope_append_t<__half>(r, n, streams, positions, qkv, st);
+    }
+}
+
+template <typename T>
+static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, int n, const int32_t* streams,
+                            const int32_t* positions, const float* q, int q_stride, float* out, cudaStream_t st) {
+    dim3 grid(s.max_splits, r.heads, n);
+    if (append)
+        decode_kernel<T, true><<<grid, 128, 0, st>>>(r, s, streams, positions, q, q_stride, out);
+    else
+        decode_kernel<T, false><<<grid, 128, 0, st>>>(r, s, streams, positions, q, q_stride, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
+                          const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
+                          float* out, cudaStream_t st) {
+    switch (dtype) {
+        case MB_F32: return decode_t<float>(append, r, s, n, streams, positions, q, q_stride, out, st);
+        case MB_BF16: return decode_t<__nv_bfloat16>(append, r, s, n, streams, positions, q, q_stride, out, st);
+        default: return decode_t<__half>(append, r, s, n, streams, positions, q, q_stride, out, st);
+    }
+}
+
+}  // namespace mb

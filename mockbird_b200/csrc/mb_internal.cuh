@@ -1,0 +1,97 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "mockbird_kv.h"
+
+namespace mb {
+
+constexpr int HD = 64;                  // head dim (kernels-decode.ts: 64 lanes per head)
+constexpr float SCALE = 0.125f;         // literal attention scale (docs analysis :846)
+constexpr float LOG2E = 1.4426950408889634f;
+
+// device-side rejection bits, reported by mb_sync
+enum : int32_t {
+    DERR_STREAM = 1,
+    DERR_POSITION = 2,
+    DERR_CAPACITY = 4,
+    DERR_TIMEOUT = 8,
+};
+
+// Everything a kernel needs to address one layer of the rings.
+struct RingView {
+    void* kv;             // base of kv[layer]: [stream][2][head][slot][64]
+    int32_t* slot_pos;    // base of slot_pos[layer]: [stream][slot]
+    const float2* rope;   // [max_position][32] (cos, sin)
+    int32_t* err;         // device rejection bits
+    int32_t streams, heads, capacity, wrap, max_position;
+};
+
+struct Scratch {
+    float* part;          // [max_batch][heads][max_splits][2 + 64]
+    int32_t* counters;    // [max_batch][heads], zero between launches
+    int32_t max_splits;
+};
+
+}  // namespace mb
+
+struct mb_ctx {
+    mb_config cfg;
+    size_t esize = 4;
+    size_t kv_bytes = 0;
+    void* kv = nullptr;
+    int32_t* slot_pos = nullptr;
+    float2* rope = nullptr;
+    int32_t* d_err = nullptr;
+    mb::Scratch scratch{};
+    size_t scratch_bytes = 0;
+    // staging for the host-array entry points
+    int32_t* d_streams = nullptr;
+    int32_t* d_positions = nullptr;
+    float* d_qkv = nullptr;   // [layers][max_batch][3*H*64]
+    float* d_out = nullptr;   // [layers][max_batch][H*64]
+    std::string last_error;
+};
+
+namespace mb {
+
+inline RingView ring_view(const mb_ctx* c, int layer) {
+    RingView v;
+    size_t per_layer = (size_t)c->cfg.streams * 2 * c->cfg.heads * (size_t)c->cfg.capacity * HD;
+    v.kv = (char*)c->kv + per_layer * layer * c->esize;
+    v.slot_pos = c->slot_pos + (size_t)layer * c->cfg.streams * c->cfg.capacity;
+    v.rope = c->rope;
+    v.err = c->d_err;
+    v.streams = c->cfg.streams;
+    v.heads = c->cfg.heads;
+    v.capacity = c->cfg.capacity;
+    v.wrap = c->cfg.wrap;
+    v.max_position = c->cfg.max_position;
+    return v;
+}
+
+// rows of one split-K chunk: 16 KB of K (and 16 KB of V) per chunk
+inline int chunk_rows(int dtype) { return dtype == MB_F32 ? 64 : 128; }
+
+// launchers (mb_decode.cu / mb_prefill.cu); return the launch's cudaError_t
+cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_t* streams,
+                               const int32_t* positions, float* qkv, cudaStream_t st);
+cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
+                          const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
+                          float* out, cudaStream_t st);
+cudaError_t launch_prefill(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
+                           const float* qkv, float* out, void* q_stage, cudaStream_t st);
+size_t prefill_stage_bytes(int dtype, int n, int heads, int rows);
+cudaError_t launch_gather(int dtype, const RingView& r, int stream, int position, void* k_out, void* v_out,
+                          int32_t* slots_out, cudaStream_t st);
+cudaError_t launch_ring_write(int dtype, const RingView& r, int stream, int first, int count, const void* k,
+                              const void* v, cudaStream_t st);
+cudaError_t launch_reset(const mb_ctx* c, int stream, cudaStream_t st);
+
+}  // namespace mb

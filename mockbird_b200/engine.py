@@ -1,0 +1,255 @@
+"""Host-side mirror of the reference engine's KV-ring / attention interface.
+
+The reference (liyu1981/mockbird, src/lib/tts/engine/) dispatches these WGSL
+kernels from its runners; each method here is the same operation behind the
+C ABI of include/mockbird_kv.h, with the same argument meaning and the same
+error behaviour (a thrown error; the ring-overflow message is the one of
+decode.ts:719-724):
+
+    reference                                    here
+    -------------------------------------------  ------------------------------
+    ropeSplitRing / ropeSplitCodec dispatch      KvRing.rope_split_ring
+      (decode.ts:527-535, codec.ts:593-624)
+    attendRing / attendCodec dispatch            KvRing.attend_ring
+      (decode.ts:536-552, codec.ts:626-645)
+    the two in sequence, per layer               KvRing.append_attend  (one launch)
+    DecodeRunner.globalStep's 12-layer loop      KvRing.decode_step (device arrays),
+      (decode.ts:712-775)                          KvRing.decode_step_host (host arrays)
+    PrefillRunner.run's rope/scores/softmax/     KvRing.prefill
+      apply dispatches (prefill.ts:424-462)
+    PrefillRunner.readLayerCache (:644-664)      KvRing.read_layer_cache
+    PrefillRunner.poisonKv (:610-620)            KvRing.poison_kv
+    WgpuTtsEngineImpl.reset / resetRings         KvRing.reset
+      (gpu.ts:237-242, codec.ts:279-282)
+    GpuTtsEngine.dispose (gpu.ts:283-291)        KvRing.dispose
+
+Device tensors are torch CUDA tensors (device memory and streams only; the
+arithmetic is in the CUDA library).  Calls run on torch's current stream of
+the ring's device unless a stream is given.
+"""
+from __future__ import annotations
+
+import ctypes
+import numpy as np
+import torch
+
+from . import _lib
+
+HD = 64
+
+
+class MockbirdError(RuntimeError):
+    """A non-zero mb_status from the library, with its message."""
+
+    def __init__(self, code: int, message: str):
+        self.code = code
+        self.status = _lib.STATUS.get(code, str(code))
+        super().__init__(f"{self.status}: {message}")
+
+
+def _ptr(t) -> ctypes.c_void_p:
+    if isinstance(t, torch.Tensor):
+        return ctypes.c_void_p(t.data_ptr())
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(ctypes.c_void_p)
+    raise TypeError(f"expected a torch tensor or numpy array, got {type(t).__name__}")
+
+
+_TORCH_DTYPE = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+class KvRing:
+    """The rings of `streams` independent synthesis streams on one GPU.
+
+    Geometry (mb_config): kv[layer][stream][K|V][head][slot][64] in `dtype`,
+    slot_pos[layer][stream][slot].  `wrap=False` is the reference's global ring
+    (positions must stay below `capacity`), `wrap=True` its codec ring
+    (slot = position % capacity).
+    """
+
+    def __init__(self, layers: int = 12, heads: int = 12, capacity: int = 570, streams: int = 1,
+                 dtype: str = "f32", wrap: bool = False, max_position: int = 65536,
+                 rope_theta: float = 10000.0, device: int = 0, max_batch: int = 0):
+        self.lib = _lib.load()
+        if dtype not in _lib.DTYPES:
+            raise ValueError(f"dtype must be one of {sorted(_lib.DTYPES)}")
+        cfg = _lib.MbConfig()
+        self.lib.mb_config_default(ctypes.byref(cfg))
+        cfg.layers, cfg.heads, cfg.head_dim, cfg.capacity = layers, heads, HD, capacity
+        cfg.streams, cfg.dtype, cfg.wrap = streams, _lib.DTYPES[dtype], int(bool(wrap))
+        cfg.max_position, cfg.rope_theta, cfg.device, cfg.max_batch = max_position, rope_theta, device, max_batch
+        handle = ctypes.c_void_p()
+        rc = self.lib.mb_create(ctypes.byref(cfg), ctypes.byref(handle))
+        if rc:
+            raise MockbirdError(rc, f"mb_create failed (layers={layers} heads={heads} capacity={capacity} "
+                                    f"streams={streams} dtype={dtype} device={device})")
+        self.ctx = handle
+        self.layers, self.heads, self.capacity, self.streams = layers, heads, capacity, streams
+        self.dtype, self.wrap, self.device = dtype, bool(wrap), torch.device("cuda", device)
+        self.max_position = max_position
+        self.max_batch = max_batch or streams
+        self.hidden = heads * HD
+        self.torch_dtype = _TORCH_DTYPE[dtype]
+
+    # ------------------------------------------------------------ plumbing
+    def _check(self, rc: int) -> None:
+        if rc:
+            raise MockbirdError(rc, self.lib.mb_last_error(self.ctx).decode())
+
+    def _stream(self, stream) -> ctypes.c_void_p:
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        return ctypes.c_void_p(stream.cuda_stream if isinstance(stream, torch.cuda.Stream) else int(stream))
+
+    def _ids(self, values) -> torch.Tensor:
+        if isinstance(values, torch.Tensor) and values.is_cuda:
+            if values.dtype != torch.int32 or not values.is_contiguous():
+                raise TypeError("stream ids / positions must be a contiguous int32 tensor")
+            return values
+        return torch.as_tensor(np.asarray(values, dtype=np.int32), device=self.device)
+
+    def _dev(self, t: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == dtype and t.is_contiguous()):
+            raise TypeError(f"expected a contiguous CUDA {dtype} tensor")
+        return t
+
+    @property
+    def info(self) -> _lib.MbRingInfo:
+        out = _lib.MbRingInfo()
+        self._check(self.lib.mb_ring_info_get(self.ctx, ctypes.byref(out)))
+        return out
+
+    # ------------------------------------------------------------ decode
+    def rope_split_ring(self, layer: int, streams, positions, qkv: torch.Tensor, stream=None) -> torch.Tensor:
+        """ROPE_SPLIT_RING / _CODEC: Q roped in place in `qkv` [n][3*H*64]; K/V appended."""
+        s, p, q = self._ids(streams), self._ids(positions), self._dev(qkv)
+        self._check(self.lib.mb_rope_append(self.ctx, layer, s.numel(), _ptr(s), _ptr(p), _ptr(q),
+                                             self._stream(stream)))
+        return qkv
+
+    def attend_ring(self, layer: int, streams, positions, q: torch.Tensor, out: torch.Tensor | None = None,
+                    q_stride: int | None = None, stream=None) -> torch.Tensor:
+        """ATTEND_RING / _CODEC: roped queries (row stride q_stride) -> context [n][H*64]."""
+        s, p, qq = self._ids(streams), self._ids(positions), self._dev(q)
+        n = s.numel()
+        stride = q_stride if q_stride is not None else qq.shape[-1]
+        if out is None:
+            out = torch.empty(n, self.hidden, dtype=torch.float32, device=self.device)
+        self._check(self.lib.mb_attend(self.ctx, layer, n, _ptr(s), _ptr(p), _ptr(qq), stride, _ptr(self._dev(out)),
+                                       self._stream(stream)))
+        return out
+
+    def append_attend(self, layer: int, streams, positions, qkv: torch.Tensor, out: torch.Tensor | None = None,
+                      stream=None) -> torch.Tensor:
+        """The fused hot path: append + RoPE + attention for n streams of one layer."""
+        s, p, q = self._ids(streams), self._ids(positions), self._dev(qkv)
+        n = s.numel()
+        if out is None:
+            out = torch.empty(n, self.hidden, dtype=torch.float32, device=self.device)
+        self._check(self.lib.mb_append_attend(self.ctx, layer, n, _ptr(s), _ptr(p), _ptr(q), _ptr(self._dev(out)),
+                                              self._stream(stream)))
+        return out
+
+    def decode_step(self, streams, positions, qkv: torch.Tensor, out: torch.Tensor | None = None,
+                    stream=None) -> torch.Tensor:
+        """All layers of one decode step on device: qkv [layers][n][3*H*64] -> [layers][n][H*64]."""
+        s, p, q = self._ids(streams), self._ids(positions), self._dev(qkv)
+        n = s.numel()
+        if out is None:
+            out = torch.empty(self.layers, n, self.hidden, dtype=torch.float32, device=self.device)
+        self._check(self.lib.mb_decode_step(self.ctx, n, _ptr(s), _ptr(p), _ptr(q), _ptr(self._dev(out)),
+                                            self._stream(stream)))
+        return out
+
+    def append_attend_host(self, layer: int, streams, positions, qkv: np.ndarray,
+                           out: np.ndarray | None = None, stream=None) -> np.ndarray:
+        """append_attend on host arrays (validated on the host; blocks until `out` is ready)."""
+        s = np.ascontiguousarray(streams, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        q = np.ascontiguousarray(qkv, np.float32)
+        if out is None:
+            out = np.empty((len(s), self.hidden), np.float32)
+        self._check(self.lib.mb_append_attend_host(self.ctx, layer, len(s), _ptr(s), _ptr(p), _ptr(q), _ptr(out),
+                                                   self._stream(stream)))
+        return out
+
+    def decode_step_host(self, streams, positions, qkv, out=None, stream=None):
+        """All layers of one decode step on host buffers: qkv [layers][n][3*H*64] -> [layers][n][H*64].
+
+        `qkv` / `out` may be numpy arrays or (pinned) CPU torch tensors."""
+        s = np.ascontiguousarray(streams, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        if isinstance(qkv, np.ndarray):
+            qkv = np.ascontiguousarray(qkv, np.float32)
+        if out is None:
+            out = np.empty((self.layers, len(s), self.hidden), np.float32)
+        self._check(self.lib.mb_decode_step_host(self.ctx, len(s), _ptr(s), _ptr(p), _ptr(qkv), _ptr(out),
+                                                 self._stream(stream)))
+        return out
+
+    # ------------------------------------------------------------ prefill
+    def prefill(self, layer: int, streams, qkv: torch.Tensor, out: torch.Tensor | None = None,
+                stream=None) -> torch.Tensor:
+        """Causal prefill of positions 0..rows-1: qkv [n][rows][3*H*64] -> context [n][rows][H*64]."""
+        s, q = self._ids(streams), self._dev(qkv)
+        n, rows = q.shape[0], q.shape[1]
+        if out is None:
+            out = torch.empty(n, rows, self.hidden, dtype=torch.float32, device=self.device)
+        self._check(self.lib.mb_prefill(self.ctx, layer, n, _ptr(s), rows, _ptr(q), _ptr(self._dev(out)),
+                                        self._stream(stream)))
+        return out
+
+    # ------------------------------------------------------------ cache access
+    def gather(self, layer: int, stream_id: int, position: int, stream=None):
+        """Live window in position order: (k [H][W][64], v, slots [W]) device tensors, storage dtype."""
+        W = min(position + 1, self.capacity)
+        k = torch.empty(self.heads, W, HD, dtype=self.torch_dtype, device=self.device)
+        v = torch.empty_like(k)
+        slots = torch.empty(W, dtype=torch.int32, device=self.device)
+        self._check(self.lib.mb_gather(self.ctx, layer, stream_id, position, _ptr(k), _ptr(v), _ptr(slots),
+                                       self._stream(stream)))
+        return k, v, slots
+
+    def read_layer_cache(self, layer: int, stream_id: int, rows: int, stream=None):
+        """PrefillRunner.readLayerCache: K and V of positions 0..rows-1 as [rows][H*64] f32."""
+        k, v, _ = self.gather(layer, stream_id, rows - 1, stream)
+        return (k.float().permute(1, 0, 2).reshape(-1, self.hidden),
+                v.float().permute(1, 0, 2).reshape(-1, self.hidden))
+
+    def ring_write(self, layer: int, stream_id: int, first_position: int, k: torch.Tensor, v: torch.Tensor,
+                   stream=None) -> None:
+        """Write K (already roped) / V rows [H][count][64] (storage dtype) at positions first_position.."""
+        k, v = self._dev(k, self.torch_dtype), self._dev(v, self.torch_dtype)
+        self._check(self.lib.mb_ring_write(self.ctx, layer, stream_id, first_position, k.shape[1], _ptr(k), _ptr(v),
+                                           self._stream(stream)))
+
+    def poison_kv(self, layer: int, stream_id: int, rows: int, value: float = -12345.5, stream=None) -> None:
+        """PrefillRunner.poisonKv: write a sentinel into positions 0..rows-1."""
+        k = torch.full((self.heads, rows, HD), value, dtype=self.torch_dtype, device=self.device)
+        self.ring_write(layer, stream_id, 0, k, k.clone(), stream)
+
+    def reset(self, stream_id: int = -1, stream=None) -> None:
+        """Every slot of `stream_id` (all streams if -1) becomes empty."""
+        self._check(self.lib.mb_reset(self.ctx, stream_id, self._stream(stream)))
+
+    def sync(self, stream=None) -> None:
+        """Wait for the stream and raise on any device-side rejection."""
+        self._check(self.lib.mb_sync(self.ctx, self._stream(stream)))
+
+    def dispose(self) -> None:
+        if getattr(self, "ctx", None):
+            self.lib.mb_destroy(self.ctx)
+            self.ctx = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.dispose()
+
+    def __del__(self):
+        try:
+            self.dispose()
+        except Exception:
+            pass
+

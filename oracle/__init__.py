@@ -1,0 +1,197 @@
+"""CPU oracle for the KV-ring / RoPE / attention path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
+(and its ``--impl reference`` arm) may import this package.  It is the checker
+that the CUDA library is compared against, never a code path of the product;
+``mockbird_b200`` does not import it and has no CPU fallback.
+
+The arithmetic lives in ``oracle.c`` (a C restatement of the reference's WGSL
+kernels, each function citing the reference file:line it follows); this module
+only holds the numpy-side ring state and the ctypes plumbing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+F32, BF16, F16 = 0, 1, 2
+DTYPES = {"f32": F32, "bf16": BF16, "f16": F16}
+HD = 64
+
+
+class Geom(ctypes.Structure):
+    _fields_ = [
+        ("layers", ctypes.c_int32),
+        ("streams", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("capacity", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("wrap", ctypes.c_int32),
+    ]
+
+
+def build() -> None:
+    """Compile oracle.c into liboracle.so (make; system gcc with OpenMP)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.c_void_p
+        i32 = ctypes.c_int32
+        G = ctypes.POINTER(Geom)
+        L.orc_rope_table.argtypes = [i32, ctypes.c_double, P]
+        L.orc_rope_rows.argtypes = [i32, i32, P, i32, P, P, P, i32]
+        L.orc_reset.argtypes = [G, P, i32]
+        L.orc_rope_split_ring.argtypes = [G, P, P, P, i32, i32, P, P, P]
+        L.orc_rope_split_ring.restype = ctypes.c_int
+        L.orc_attend_ring.argtypes = [G, P, P, i32, i32, P, P, P, i32, P, i32]
+        L.orc_append_attend.argtypes = [G, P, P, P, i32, i32, P, P, P, P, i32]
+        L.orc_append_attend.restype = ctypes.c_int
+        L.orc_gather.argtypes = [G, P, P, i32, i32, i32, P, P, P]
+        L.orc_gather.restype = i32
+        L.orc_prefill.argtypes = [G, P, P, P, i32, i32, P, i32, P, P, i32]
+        L.orc_prefill.restype = ctypes.c_int
+        L.orc_round_to.argtypes = [i32, P, P, ctypes.c_size_t]
+        L.orc_xorshift_js.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int64, P]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def rope_table(positions: int, theta: float = 10000.0) -> np.ndarray:
+    """[positions][64] float32: (cos, sin) pairs per frequency, fp64 angles."""
+    tab = np.empty((positions, HD), np.float32)
+    lib().orc_rope_table(positions, theta, _p(tab))
+    return tab
+
+
+def rope_rows(x: np.ndarray, positions, tab: np.ndarray) -> np.ndarray:
+    """RoPE of [rows][heads*64] rows at per-row positions (fp32, no FMA)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, width = x.shape
+    pos = np.ascontiguousarray(positions, np.int32)
+    out = np.empty_like(x)
+    lib().orc_rope_rows(rows, width // HD, _p(x), width, _p(pos), _p(tab), _p(out), width)
+    return out
+
+
+def round_to(dtype: str, x: np.ndarray) -> np.ndarray:
+    """Round fp32 values to the storage dtype (nearest-even) and back."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    lib().orc_round_to(DTYPES[dtype], _p(x), _p(out), x.size)
+    return out
+
+
+class Ring:
+    """Host copy of the ring state: kv[layer][stream][2][head][slot][64] + slot_pos."""
+
+    def __init__(self, layers=12, streams=1, heads=12, capacity=570, dtype="f32", wrap=True,
+                 max_position=None, theta=10000.0):
+        self.g = Geom(layers, streams, heads, capacity, DTYPES[dtype], int(bool(wrap)))
+        self.dtype = dtype
+        self.heads = heads
+        self.capacity = capacity
+        elems = layers * streams * 2 * heads * capacity * HD
+        self.kv = np.zeros(elems, np.float32 if dtype == "f32" else np.uint16)
+        self.slot_pos = np.full((layers, streams, capacity), -1, np.int32)
+        self.tab = rope_table(max_position or max(capacity, 1) * 4, theta)
+
+    def reset(self, stream: int = -1) -> None:
+        lib().orc_reset(ctypes.byref(self.g), _p(self.slot_pos), stream)
+
+    def _check_pos(self, positions):
+        if len(positions) and int(np.max(positions)) >= self.tab.shape[0]:
+            self.tab = rope_table(int(np.max(positions)) * 2 + 1)
+
+    def rope_split(self, layer, streams, positions, qkv: np.ndarray) -> np.ndarray:
+        """ROPE_SPLIT_RING/_CODEC; returns the row block with Q roped in place."""
+        s = np.ascontiguousarray(streams, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        self._check_pos(p)
+        q = np.array(qkv, np.float32, order="C", copy=True)
+        rc = lib().orc_rope_split_ring(ctypes.byref(self.g), _p(self.kv), _p(self.slot_pos), _p(self.tab),
+                                       layer, len(s), _p(s), _p(p), _p(q))
+        if rc:
+            raise ValueError("position does not fit the (non-wrapping) ring")
+        return q
+
+    def attend(self, layer, streams, positions, q_rows: np.ndarray, mode: int = 0) -> np.ndarray:
+        """ATTEND_RING/_CODEC (mode 0, fp32 tile mirror) or ref-decode attend (mode 1, fp64)."""
+        s = np.ascontiguousarray(streams, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        q = np.ascontiguousarray(q_rows, np.float32)
+        ctx = np.zeros((len(s), self.heads * HD), np.float32)
+        lib().orc_attend_ring(ctypes.byref(self.g), _p(self.kv), _p(self.slot_pos), layer, len(s), _p(s), _p(p),
+                              _p(q), q.shape[1], _p(ctx), mode)
+        return ctx
+
+    def append_attend(self, layer, streams, positions, qkv: np.ndarray, mode: int = 0):
+        """rope_split then attend (decode.ts:527-552); returns (ctx, roped qkv)."""
+        q = self.rope_split(layer, streams, positions, qkv)
+        return self.attend(layer, streams, positions, q, mode), q
+
+    def gather(self, layer, stream, position):
+        """Live window in position order: (k [H][W][64], v, slots [W])."""
+        W = min(position + 1, self.capacity)
+        dt = np.float32 if self.dtype == "f32" else np.uint16
+        k = np.zeros((self.heads, W, HD), dt)
+        v = np.zeros((self.heads, W, HD), dt)
+        slots = np.zeros(W, np.int32)
+        lib().orc_gather(ctypes.byref(self.g), _p(self.kv), _p(self.slot_pos), layer, stream, position,
+                         _p(k), _p(v), _p(slots))
+        return k, v, slots
+
+    def prefill(self, layer, streams, qkv: np.ndarray, q_round: bool = False):
+        """ROPE_SPLIT_CACHE + ATTENTION_*; qkv [n][rows][2304] -> (ctx [n][rows][768], roped qkv)."""
+        s = np.ascontiguousarray(streams, np.int32)
+        q = np.array(qkv, np.float32, order="C", copy=True)
+        n, rows = q.shape[0], q.shape[1]
+        self._check_pos(np.array([rows], np.int32))
+        ctx = np.zeros((n, rows, self.heads * HD), np.float32)
+        rc = lib().orc_prefill(ctypes.byref(self.g), _p(self.kv), _p(self.slot_pos), _p(self.tab), layer, n,
+                               _p(s), rows, _p(q), _p(ctx), int(q_round))
+        if rc:
+            raise ValueError("prefill rows exceed the ring capacity")
+        return ctx, q
+
+    def kv_view(self):
+        """kv as [layers][streams][2][heads][capacity][64]."""
+        g = self.g
+        return self.kv.reshape(g.layers, g.streams, 2, g.heads, g.capacity, HD)
+
+
+def xorshift32_stream(seed: int = 0x2F6E2B1):
+    """The PRNG of tests/gpu/kernels.test.mjs:22-30, evaluated as JavaScript does.
+
+    Returns rnd(count) -> float32 draws; rnd(count, keep=False) only advances.
+    """
+    state = ctypes.c_uint32(seed & 0xFFFFFFFF)
+
+    def rnd(count: int, keep: bool = True):
+        if not keep:
+            lib().orc_xorshift_js(ctypes.byref(state), count, None)
+            return None
+        out = np.empty(count, np.float32)
+        lib().orc_xorshift_js(ctypes.byref(state), count, _p(out))
+        return out
+
+    return rnd

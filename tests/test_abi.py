@@ -1,0 +1,80 @@
+"""CPU tests of the C ABI boundary: the library builds, loads without a GPU, and
+exports exactly what include/mockbird_kv.h declares.  No compute calls."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from mockbird_b200 import _lib
+from mockbird_b200.build import LIB, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "mockbird_kv.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"MB_API\s+[\w\s\*]+?\b(mb_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.load()
+
+
+def test_header_declares_the_entry_points():
+    syms = declared_symbols()
+    for name in ["mb_create", "mb_destroy", "mb_reset", "mb_rope_append", "mb_attend", "mb_append_attend",
+                 "mb_prefill", "mb_gather", "mb_sync", "mb_last_error"]:
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (mb_\w+)", out))
+    declared = set(declared_symbols())
+    assert declared <= exported, declared - exported
+    # nothing but the declared C ABI is visible (the rest is hidden)
+    assert {s for s in exported if s.startswith("mb_")} == declared
+
+
+def test_python_bindings_cover_the_header(lib):
+    assert set(_lib.SIGNATURES) == set(declared_symbols())
+    for name in declared_symbols():
+        assert hasattr(lib, name)
+
+
+def test_config_struct_layout_matches_header(lib):
+    cfg = _lib.MbConfig()
+    lib.mb_config_default(ctypes.byref(cfg))
+    assert (cfg.layers, cfg.heads, cfg.head_dim, cfg.capacity) == (12, 12, 64, 570)  # gpu.ts:362 maxSlots
+    assert cfg.dtype == _lib.MB_F32 and cfg.wrap == 0 and abs(cfg.rope_theta - 10000.0) < 1e-3
+    assert ctypes.sizeof(_lib.MbConfig) == 11 * 4
+    assert lib.mb_version().decode().startswith("mockbird-b200")
+
+
+def test_create_reports_missing_device_or_bad_config(lib):
+    cfg = _lib.MbConfig()
+    lib.mb_config_default(ctypes.byref(cfg))
+    cfg.head_dim = 32  # only 64 is supported
+    h = ctypes.c_void_p()
+    assert lib.mb_create(ctypes.byref(cfg), ctypes.byref(h)) == 1  # MB_ERR_ARG
+    assert not h.value
+
+
+def test_null_context_is_an_argument_error(lib):
+    assert lib.mb_destroy(None) == 1
+    assert lib.mb_sync(None, None) == 1
+    assert lib.mb_reset(None, -1, None) == 1
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _lib._lib = None
+        try:
+            _lib.load(str(tmp_path / "libmockbird_kv.so"))
+        finally:
+            _lib._lib = None

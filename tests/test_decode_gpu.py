@@ -1,0 +1,290 @@
+"""GPU parity of the decode path (append + RoPE + flash-decode), through the C ABI,
+against the CPU oracle.  Ring bytes, slot indices and wrap order bit-exact;
+attention within max-abs 2e-3 (fp32 storage) / 1e-2 (fp16, bf16 storage)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import HD, HID, QKV, TOL, H, assert_window_equal, from_np_storage, max_err, randn, to_np_storage
+from mockbird_b200 import KvRing, MockbirdError
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+def test_wrapping_ring_parity(dtype):
+    """Streams appended out of order, two of them starting late, the ring wrapping
+    more than twice, several split-K chunks per window."""
+    L, S, C = 2, 6, 200
+    ring = KvRing(layers=L, streams=S, capacity=C, dtype=dtype, wrap=True)
+    orc = oracle.Ring(layers=L, streams=S, heads=H, capacity=C, dtype=dtype, wrap=True)
+    start = {5: 0, 0: 0, 3: 0, 2: 0, 1: 100, 4: 137}
+    worst = 0.0
+    for step in range(460):
+        items = [s for s in (5, 0, 3, 2, 1, 4) if step >= start[s]]
+        pos = [step - start[s] for s in items]
+        for layer in range(L):
+            qkv = randn((len(items), QKV), seed=step * 10 + layer)
+            out = ring.append_attend(layer, items, pos, torch.from_numpy(qkv).to(DEV))
+            ref, _ = orc.append_attend(layer, items, pos, qkv)
+            worst = max(worst, max_err(out, ref))
+        if step % 97 == 0 or step == 459:
+            ring.sync()
+            for layer in range(L):
+                for s, p in zip(items, pos):
+                    assert_window_equal(ring, orc, layer, s, layer, s, p)
+    ring.sync()
+    assert worst < TOL[dtype], worst
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_fused_equals_rope_then_attend(dtype):
+    """mb_append_attend == mb_rope_append + mb_attend, bit for bit; roped Q bit-exact."""
+    S, C = 4, 300
+    a = KvRing(layers=1, streams=S, capacity=C, dtype=dtype, wrap=True)
+    b = KvRing(layers=1, streams=S, capacity=C, dtype=dtype, wrap=True)
+    tab = oracle.rope_table(1024)
+    for step in range(350):
+        qkv = torch.from_numpy(randn((S, QKV), seed=step)).to(DEV)
+        pos = [step] * S
+        oa = a.append_attend(0, [0, 1, 2, 3], pos, qkv)
+        qb = qkv.clone()
+        b.rope_split_ring(0, [0, 1, 2, 3], pos, qb)
+        ob = b.attend_ring(0, [0, 1, 2, 3], pos, qb, q_stride=QKV)
+        assert torch.equal(oa, ob), step
+        if step in (0, 63, 64, 299, 300, 349):
+            ref_q = oracle.rope_rows(qkv[:, :HID].cpu().numpy(), pos, tab)
+            assert np.array_equal(qb[:, :HID].cpu().numpy(), ref_q)
+            assert torch.equal(qb[:, HID:], qkv[:, HID:])  # K/V part of the row untouched
+    a.sync()
+    b.sync()
+
+
+def test_kat_attention_n512_gpu():
+    """kernels.test.mjs test 4 (N=512, 12 heads) within its own tolerance 1e-5."""
+    kat = np.load(os.path.join(GOLDEN, "kat_attention_n512.npz"))
+    rnd = oracle.xorshift32_stream(0x2F6E2B1)
+    rnd(int(kat["skip"]), keep=False)
+    kv = rnd(2 * 512 * H * HD)
+    k = kv[0::2].reshape(512, H, HD).transpose(1, 0, 2).copy()
+    v = kv[1::2].reshape(512, H, HD).transpose(1, 0, 2).copy()
+    q = rnd(H * HD)
+    ring = KvRing(layers=1, streams=1, capacity=512, dtype="f32", wrap=False)
+    ring.ring_write(0, 0, 0, torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV))
+    out = ring.attend_ring(0, [0], [511], torch.from_numpy(q.reshape(1, -1)).to(DEV))
+    ring.sync()
+    assert max_err(out[0], kat["out"]) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_golden_kv_as_ring_contents(dtype):
+    """The ONNX layer-0 K/V rows as realistic ring contents, wrapped, vs the fp64 oracle."""
+    g = np.load(os.path.join(GOLDEN, "layer0_kv.npz"))
+    k = np.ascontiguousarray(g["k"].transpose(1, 0, 2))  # [12][75][64]
+    v = np.ascontiguousarray(g["v"].transpose(1, 0, 2))
+    C = 48
+    ring = KvRing(layers=1, streams=1, capacity=C, dtype=dtype, wrap=True)
+    orc = oracle.Ring(layers=1, streams=1, heads=H, capacity=C, dtype=dtype, wrap=True)
+    ks = oracle.round_to(dtype, k)
+    vs = oracle.round_to(dtype, v)
+    ring.ring_write(0, 0, 27, from_np_storage(_to_storage(ks[:, 27:], dtype), dtype),
+                    from_np_storage(_to_storage(vs[:, 27:], dtype), dtype))
+    kvv = orc.kv_view()
+    for p in range(27, 75):
+        kvv[0, 0, 0, :, p % C] = _to_storage(ks[:, p], dtype)
+        kvv[0, 0, 1, :, p % C] = _to_storage(vs[:, p], dtype)
+        orc.slot_pos[0, 0, p % C] = p
+    q = randn((1, HID), seed=7)
+    out = ring.attend_ring(0, [0], [74], torch.from_numpy(q).to(DEV))
+    ref = orc.attend(0, [0], [74], q, mode=1)
+    ring.sync()
+    assert_window_equal(ring, orc, 0, 0, 0, 0, 74)
+    assert max_err(out, ref) < TOL[dtype]
+
+
+def _to_storage(x, dtype):
+    if dtype == "f32":
+        return np.ascontiguousarray(x, np.float32)
+    if dtype == "f16":
+        return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return (u >> 16).astype(np.uint16)  # x is already bf16-representable
+
+
+def test_config1_single_stream_step():
+    """1 stream, 12 layers, C=2048, slots 0..299 filled with
+    N(0,1) K/V (seed 0), append + attend at position 300 (RoPE theta 10000)."""
+    ring = KvRing(layers=12, streams=1, capacity=2048, dtype="f32", wrap=False)
+    orc = oracle.Ring(layers=12, streams=1, heads=H, capacity=2048, dtype="f32", wrap=False)
+    rng = np.random.default_rng(0)
+    for layer in range(12):
+        k = rng.standard_normal((H, 300, HD)).astype(np.float32)
+        v = rng.standard_normal((H, 300, HD)).astype(np.float32)
+        ring.ring_write(layer, 0, 0, torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV))
+        orc.kv_view()[layer, 0, 0, :, :300] = k
+        orc.kv_view()[layer, 0, 1, :, :300] = v
+        orc.slot_pos[layer, 0, :300] = np.arange(300)
+    qkv = np.random.default_rng(0).standard_normal((12, 1, QKV)).astype(np.float32)
+    for layer in range(12):
+        out = ring.append_attend(layer, [0], [300], torch.from_numpy(qkv[layer]).to(DEV))
+        ref, _ = orc.append_attend(layer, [0], [300], qkv[layer])
+        ref64 = orc.attend(layer, [0], [300], _, mode=1)
+        assert max_err(out, ref) < TOL["f32"]
+        assert max_err(out, ref64) < TOL["f32"]
+        assert_window_equal(ring, orc, layer, 0, layer, 0, 300)
+    ring.sync()
+
+
+def test_config2_full_size_wrap_properties():
+    """BASELINE config 2 at full size: 64 streams x 12 layers, fp32, C=512, 1500
+    appends (two wraps).  The GPU runs everything; the oracle replays 2 layers x 3
+    streams in lockstep; the final ring order is checked for all streams."""
+    L, S, C, STEPS = 12, 64, 512, 1500
+    ring = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
+    track = [(0, 0), (7, 33), (11, 63)]  # (layer, stream)
+    orc = oracle.Ring(layers=len(track), streams=1, heads=H, capacity=C, dtype="f32", wrap=True)
+    streams = torch.arange(S, dtype=torch.int32, device=DEV)
+    gen = torch.Generator(device=DEV)
+    worst = 0.0
+    check_steps = {0, 1, 511, 512, 513, 1023, 1024, 1499}
+    for step in range(STEPS):
+        gen.manual_seed(step)
+        qkv = torch.randn(L, S, QKV, generator=gen, device=DEV)
+        pos = torch.full((S,), step, dtype=torch.int32, device=DEV)
+        outs = [ring.append_attend(layer, streams, pos, qkv[layer]) for layer in range(L)]
+        sub = [qkv[layer, s].cpu().numpy()[None] for layer, s in track]
+        for t, (layer, s) in enumerate(track):
+            ref, _ = orc.append_attend(t, [0], [step], sub[t])
+            if step in check_steps:
+                worst = max(worst, max_err(outs[layer][s], ref[0]))
+    ring.sync()
+    assert worst < TOL["f32"], worst
+    for t, (layer, s) in enumerate(track):
+        assert_window_equal(ring, orc, layer, s, t, 0, STEPS - 1)
+    expected = np.array([p % C for p in range(STEPS - C, STEPS)], np.int32)
+    for s in range(S):
+        _, _, slots = ring.gather(5, s, STEPS - 1)
+        assert np.array_equal(slots.cpu().numpy(), expected)
+
+
+def test_variable_live_lengths_bf16():
+    """Config-5 style: per-stream live lengths U[1, C] (seeded), bf16, 24 steps of
+    appends (some streams wrap), all streams in one launch."""
+    S, C = 16, 512
+    rng = np.random.default_rng(5)
+    lengths = rng.integers(1, C + 1, size=S)
+    ring = KvRing(layers=1, streams=S, capacity=C, dtype="bf16", wrap=True)
+    orc = oracle.Ring(layers=1, streams=S, heads=H, capacity=C, dtype="bf16", wrap=True)
+    for s in range(S):
+        n = int(lengths[s]) - 1
+        if n == 0:
+            continue
+        k = _to_storage(oracle.round_to("bf16", rng.standard_normal((H, n, HD)).astype(np.float32)), "bf16")
+        v = _to_storage(oracle.round_to("bf16", rng.standard_normal((H, n, HD)).astype(np.float32)), "bf16")
+        ring.ring_write(0, s, 0, from_np_storage(k, "bf16"), from_np_storage(v, "bf16"))
+        orc.kv_view()[0, s, 0, :, :n] = k
+        orc.kv_view()[0, s, 1, :, :n] = v
+        orc.slot_pos[0, s, :n] = np.arange(n)
+    order = list(rng.permutation(S))
+    worst = 0.0
+    for step in range(24):
+        pos = [int(lengths[s]) - 1 + step for s in order]
+        qkv = randn((S, QKV), seed=1000 + step)
+        out = ring.append_attend(0, order, pos, torch.from_numpy(qkv).to(DEV))
+        ref, _ = orc.append_attend(0, order, pos, qkv)
+        worst = max(worst, max_err(out, ref))
+    ring.sync()
+    assert worst < TOL["bf16"], worst
+    for s, p in zip(order, pos):
+        assert_window_equal(ring, orc, 0, s, 0, s, p)
+
+
+def test_host_entry_points_match_device_path():
+    S, C, L = 3, 128, 12
+    a = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
+    b = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
+    c = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
+    for step in range(140):
+        qkv = randn((L, S, QKV), seed=step)
+        pos = [step, step, step]
+        host = a.decode_step_host([2, 0, 1], pos, qkv)
+        for layer in range(L):
+            dev = b.append_attend(layer, [2, 0, 1], pos, torch.from_numpy(qkv[layer]).to(DEV))
+            one = c.append_attend_host(layer, [2, 0, 1], pos, qkv[layer])
+            assert np.array_equal(host[layer], dev.cpu().numpy())
+            assert np.array_equal(one, host[layer])
+
+
+def test_errors_are_reported_and_the_context_survives():
+    ring = KvRing(layers=2, streams=4, capacity=8, dtype="f32", wrap=False, max_batch=4)
+    qkv = randn((1, QKV), seed=0)
+    for p in range(8):
+        ring.append_attend_host(0, [1], [p], qkv)
+    with pytest.raises(MockbirdError, match="exceeds the KV ring") as e:
+        ring.append_attend_host(0, [1], [8], qkv)
+    assert e.value.status == "MB_ERR_CAPACITY"
+    with pytest.raises(MockbirdError) as e:
+        ring.append_attend_host(0, [4], [0], qkv)
+    assert e.value.status == "MB_ERR_STREAM"
+    with pytest.raises(MockbirdError) as e:
+        ring.append_attend_host(0, [1, 1], [0, 0], np.concatenate([qkv, qkv]))
+    assert e.value.status == "MB_ERR_STREAM"
+    with pytest.raises(MockbirdError) as e:
+        ring.append_attend_host(2, [1], [0], qkv)
+    assert e.value.status == "MB_ERR_LAYER"
+    with pytest.raises(MockbirdError) as e:
+        ring.append_attend_host(0, [0], [-1], qkv)
+    assert e.value.status == "MB_ERR_POSITION"
+    with pytest.raises(MockbirdError) as e:
+        ring.append_attend_host(0, [0, 1, 2, 3, 0], [0] * 5, np.repeat(qkv, 5, 0))
+    assert e.value.status == "MB_ERR_ARG"
+    # device-side rejection: the bad item is skipped, the good one is computed
+    good = KvRing(layers=2, streams=4, capacity=8, dtype="f32", wrap=False)
+    q2 = torch.from_numpy(randn((2, QKV), seed=3)).to(DEV)
+    out = ring.append_attend(1, torch.tensor([0, 9], dtype=torch.int32, device=DEV),
+                             torch.tensor([0, 0], dtype=torch.int32, device=DEV), q2)
+    with pytest.raises(MockbirdError) as e:
+        ring.sync()
+    assert e.value.status == "MB_ERR_DEVICE"
+    ref = good.append_attend(1, [0], [0], q2[:1].clone())
+    assert torch.equal(out[0], ref[0])
+    ring.append_attend(1, torch.tensor([2], dtype=torch.int32, device=DEV),
+                       torch.tensor([8], dtype=torch.int32, device=DEV), q2[:1].clone())
+    with pytest.raises(MockbirdError, match="non-wrapping"):
+        ring.sync()
+    ring.sync()  # status cleared
+    # and the context still computes correctly
+    orc = oracle.Ring(layers=2, streams=4, heads=H, capacity=8, dtype="f32", wrap=False)
+    for p in range(8):
+        orc.append_attend(0, [1], [p], qkv)
+    q3 = randn((1, QKV), seed=9)
+    ring.reset(1)
+    orc.reset(1)
+    out = ring.append_attend_host(0, [1], [0], q3)
+    ref, _ = orc.append_attend(0, [1], [0], q3)
+    assert max_err(out, ref) < TOL["f32"]
+
+
+def test_empty_window_reset_and_poison_readback():
+    ring = KvRing(layers=1, streams=2, capacity=16, dtype="f32", wrap=True)
+    q = torch.from_numpy(randn((1, HID), seed=1)).to(DEV)
+    out = ring.attend_ring(0, [1], [5], q)
+    assert torch.count_nonzero(out).item() == 0  # nothing live: zeros, not NaN
+    # the warm-up check of gpu.ts:201-234: poison, read back, then overwrite
+    ring.poison_kv(0, 0, 2)
+    k, v = ring.read_layer_cache(0, 0, 2)
+    assert torch.all(k == -12345.5) and torch.all(v == -12345.5)
+    qkv = torch.from_numpy(randn((2, QKV), seed=2)).to(DEV)
+    ring.append_attend(0, [0], [0], qkv[:1].clone())
+    ring.append_attend(0, [0], [1], qkv[1:].clone())
+    k, v = ring.read_layer_cache(0, 0, 2)
+    assert not torch.any(k == -12345.5)
+    ring.reset()
+    out = ring.attend_ring(0, [0], [1], q)
+    assert torch.count_nonzero(out).item() == 0
+    ring.sync()

@@ -1,0 +1,101 @@
+"""GPU parity of the causal prefill (ROPE_SPLIT_CACHE + causal attention) through
+the C ABI, against the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import HID, QKV, TOL, H, assert_window_equal, max_err, randn
+from mockbird_b200 import KvRing, MockbirdError
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _prefill_both(dtype, streams, rows, capacity, n_streams, seed, scale=1.0, layer=0, layers=1):
+    ring = KvRing(layers=layers, streams=n_streams, capacity=capacity, dtype=dtype, wrap=True)
+    orc = oracle.Ring(layers=layers, streams=n_streams, heads=H, capacity=capacity, dtype=dtype, wrap=True)
+    qkv = randn((len(streams), rows, QKV), seed=seed, scale=scale)
+    out = ring.prefill(layer, streams, torch.from_numpy(qkv).to(DEV))
+    ref, _ = orc.prefill(layer, streams, qkv, q_round=(dtype != "f32"))
+    return ring, orc, out, ref
+
+
+def test_prefill_f32_195_rows():
+    """The golden prompt's shape (195 rows), fp32 ring of 570 slots (gpu.ts:362)."""
+    ring, orc, out, ref = _prefill_both("f32", [1, 0], 195, 570, 2, seed=11)
+    ring.sync()
+    assert max_err(out, ref) < TOL["f32"]
+    for s in (0, 1):
+        assert_window_equal(ring, orc, 0, s, 0, s, 194)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_prefill_16bit_444_rows(dtype):
+    """BASELINE config 3's shape: 188-frame prompt + 256 text = 444 positions,
+    q/k/v ~ N(0, 0.5), 16-bit storage with fp32 accumulation, ring capacity 2048."""
+    ring, orc, out, ref = _prefill_both(dtype, [3, 0, 2], 444, 2048, 4, seed=12, scale=0.5)
+    ring.sync()
+    assert max_err(out, ref) < TOL[dtype]
+    for s in (0, 2, 3):
+        assert_window_equal(ring, orc, 0, s, 0, s, 443)
+
+
+@pytest.mark.parametrize("rows", [1, 2, 63, 64, 65, 128, 257])
+def test_prefill_row_edges(rows):
+    ring, orc, out, ref = _prefill_both("f16", [0], rows, 300, 1, seed=rows, scale=0.5)
+    ring.sync()
+    assert max_err(out, ref) < TOL["f16"]
+    assert_window_equal(ring, orc, 0, 0, 0, 0, rows - 1)
+
+
+def test_prefill_at_full_capacity_then_decode_wraps():
+    ring, orc, out, ref = _prefill_both("f32", [0], 256, 256, 1, seed=5)
+    assert max_err(out, ref) < TOL["f32"]
+    for step in range(256, 300):  # the first decode steps already wrap
+        qkv = randn((1, QKV), seed=step)
+        o = ring.append_attend(0, [0], [step], torch.from_numpy(qkv).to(DEV))
+        r, _ = orc.append_attend(0, [0], [step], qkv)
+        assert max_err(o, r) < TOL["f32"]
+    ring.sync()
+    assert_window_equal(ring, orc, 0, 0, 0, 0, 299)
+
+
+def test_prefill_starts_an_utterance():
+    """A prefill over a used ring marks the old slots empty: the next decode step
+    attends positions 0..rows only (the per-chunk reset of runtime.ts:520-523)."""
+    C = 64
+    ring = KvRing(layers=1, streams=1, capacity=C, dtype="f32", wrap=True)
+    orc = oracle.Ring(layers=1, streams=1, heads=H, capacity=C, dtype="f32", wrap=True)
+    for step in range(100):  # an earlier utterance that wrapped
+        qkv = randn((1, QKV), seed=step)
+        ring.append_attend(0, [0], [step], torch.from_numpy(qkv).to(DEV))
+        orc.append_attend(0, [0], [step], qkv)
+    qkv = randn((1, 20, QKV), seed=500)
+    out = ring.prefill(0, [0], torch.from_numpy(qkv).to(DEV))
+    orc.reset(0)
+    ref, _ = orc.prefill(0, [0], qkv)
+    assert max_err(out, ref) < TOL["f32"]
+    q = randn((1, QKV), seed=501)
+    o = ring.append_attend(0, [0], [20], torch.from_numpy(q).to(DEV))
+    r, _ = orc.append_attend(0, [0], [20], q)
+    ring.sync()
+    assert max_err(o, r) < TOL["f32"]
+    assert_window_equal(ring, orc, 0, 0, 0, 0, 20)
+
+
+def test_prefill_errors():
+    ring = KvRing(layers=2, streams=2, capacity=32, dtype="f16", wrap=True)
+    qkv = torch.zeros(1, 33, QKV, device=DEV)
+    with pytest.raises(MockbirdError) as e:
+        ring.prefill(0, [0], qkv)
+    assert e.value.status == "MB_ERR_CAPACITY"
+    with pytest.raises(MockbirdError) as e:
+        ring.prefill(2, [0], qkv[:, :4].contiguous())
+    assert e.value.status == "MB_ERR_LAYER"
+    out = ring.prefill(1, torch.tensor([5], dtype=torch.int32, device=DEV), qkv[:, :4].contiguous())
+    with pytest.raises(MockbirdError) as e:
+        ring.sync()
+    assert e.value.status == "MB_ERR_DEVICE"
+    del out
+    ring.sync()
