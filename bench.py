@@ -108,7 +108,7 @@ class ClockSampler:
             return None
         mx = max(float(r[2]) for r in rows if len(r) >= 9)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if r[5 + i].strip() == "Active"})
         loaded = [s for s in sm if s > 0.5 * mx] or sm
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons, "samples": len(sm)}
 
