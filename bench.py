@@ -139,6 +139,13 @@ def setup_ours(cfg, rank, world, device):
     if cfg["job_steps"] is not None:  # config 2: everyone at the same position
         lengths0 = None
         shard_ids = partition_streams(n * world, world)[rank].streams
+        if cfg.get("start") is not None:  # steady state: the C positions before `start` are written
+            C = cfg["capacity"]
+            kv = torch.randn(2, H, C, HD, generator=g, device=device).to(ring.torch_dtype)
+            for layer in range(cfg["layers"]):
+                for i in range(n):
+                    ring.ring_write(layer, i, cfg["start"] - C, kv[0], kv[1])
+            torch.cuda.synchronize(device)
     else:  # config 5: per-stream live lengths, length-balanced shards
         total = n * world
         all_len = config5_lengths(max(total, 4096), cfg["capacity"])[:total]
@@ -160,6 +167,8 @@ def setup_ours(cfg, rank, world, device):
 def positions_for(cfg, step, n, lengths0):
     """Host positions of every stream at `step` (a step of the job)."""
     if lengths0 is None:
+        if cfg.get("start") is not None:
+            return np.full(n, cfg["start"] + step, np.int32)
         return np.full(n, step % cfg["job_steps"], np.int32)
     return (lengths0 - 1 + step).astype(np.int32)
 
@@ -179,23 +188,24 @@ def run_ours(args, cfg, rank, world, device):
     es = _esize(cfg["dtype"])
     # positions of every step, staged on the device (warm-up steps first)
     steps_total = W + K
-    pos_host = np.stack([positions_for(cfg, t if lengths0 is not None else t, n, lengths0)
-                         for t in range(steps_total)])
-    if lengths0 is None:  # config 2: warm-up at 0..W-1, then the timed job from position 0
+    pos_host = np.stack([positions_for(cfg, t, n, lengths0) for t in range(steps_total)])
+    if lengths0 is None and cfg.get("start") is None:  # config 2: warm-up 0..W-1, then the job from 0
         pos_host[W:] = np.stack([positions_for(cfg, t, n, None) for t in range(K)])
     pos_dev = torch.from_numpy(pos_host).to(device)
     algo_bytes = sum(float(window_bytes(live_len(pos_host[t].astype(np.int64), C), es, L).sum())
                      for t in range(W, steps_total))
 
+    job = lengths0 is None and cfg.get("start") is None  # the 1500-frame job with resets
+
     def step(t):
-        if lengths0 is None and t >= W and (t - W) % cfg["job_steps"] == 0:
+        if job and t >= W and (t - W) % cfg["job_steps"] == 0:
             ring.reset()  # a new pass of the 1500-frame job starts from an empty ring
         ring.decode_step(streams, pos_dev[t], qkv_pool[t % qkv_pool.shape[0]], out)
 
     for t in range(W):
         step(t)
     ring.sync()
-    if lengths0 is None:
+    if job:
         ring.reset()
     dist = _dist()
     if dist:
@@ -220,7 +230,7 @@ def run_ours(args, cfg, rank, world, device):
 
     # ---- end to end through the host-array C ABI call (pinned buffers), copies timed
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and cfg.get("start") is None:
         sets = 2
         host_qkv = torch.empty(sets, L, n, QKV, dtype=torch.float32).pin_memory()
         for i in range(sets):
@@ -345,8 +355,20 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--start", type=int, default=None,
+                    help="config 2 profiling variant: begin at this position with full windows pre-written "
+                         "(steady state, no resets) instead of the 1500-frame job")
+    ap.add_argument("--streams", type=int, default=None, help="override streams per GPU (small profiling cases)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.streams:
+        cfg["streams"] = args.streams
+        cfg["workload"] += f" [profiling case: {args.streams} streams/GPU]"
+    if args.start is not None:
+        if cfg["job_steps"] is None or args.start < cfg["capacity"]:
+            ap.error("--start applies to config 2 with a position >= capacity")
+        cfg["start"] = args.start
+        cfg["workload"] += f" [steady-state variant: positions from {args.start}, full windows]"
     args.steps = args.steps if args.steps is not None else cfg["steps"]
     args.warmup = args.warmup if args.warmup is not None else cfg["warmup"]
     if args.warmup < 3:
@@ -382,7 +404,7 @@ def main():
     if dist:
         from mockbird_b200.scheduler import gather_reports
         gather_reports({"rank": rank, "value_gpu": result["value"] / world}, device)
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and cfg.get("start") is None:
         result["cpu_baseline"] = run_cpu(cfg, min(args.steps, cfg["job_steps"] or args.steps), 2, sample_streams=4,
                                          budget_s=30.0)
     elif rank == 0:
