@@ -174,6 +174,50 @@ MB_API int mb_ring_write(mb_ctx* ctx, int32_t layer, int32_t stream, int32_t fir
 /* Wait for `cuda_stream` and report device-side rejections (then clear them). */
 MB_API int mb_sync(mb_ctx* ctx, void* cuda_stream);
 
+/* ---------------------------------------------------------------------------
+ * No-allocation entry point.  No counterpart in the reference: the reference
+ * allocates its GPU buffers once per engine and never hands that job to callers.
+ *
+ * Some callers cannot call cudaMalloc: a host application whose device memory
+ * is already owned by another allocator (a framework's caching pool, a game or
+ * audio engine's arena) where an extra cudaMalloc can fail or fragment, or a
+ * real-time audio thread that must not block on the device-wide synchronisation
+ * that cudaMalloc/cudaFree may imply.  Such a caller owns every buffer itself and
+ * describes its ring with an mb_ring_ref; the entry point below allocates
+ * nothing.  The split-K scratch of the decode kernel lives in a fixed,
+ * file-scope device array of MB_NOALLOC_SCRATCH_BYTES that every GPU which
+ * loads this library holds until the process exits.
+ * ------------------------------------------------------------------------- */
+
+/* Maximum scratch of mb_append_attend_noalloc: a call needs
+ * n * heads * ceil(capacity / chunk) * 66 * 4 bytes of partials (chunk = 64 slots
+ * for fp32, 128 for 16-bit storage) plus n * heads * 4 bytes of counters,
+ * each rounded up to 256 bytes; larger calls are rejected with MB_ERR_ARG. */
+#define MB_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* A ring in caller-owned device memory, laid out as a context's (see above). */
+typedef struct mb_ring_ref {
+    void* kv;              /* kv[layers][streams][2][heads][capacity][64], storage dtype, 16-byte aligned */
+    int32_t* slot_pos;     /* slot_pos[layers][streams][capacity], -1 = empty                          */
+    const float* rope;     /* [max_position][32][2]: cos, sin of p * theta^(-2i/64), angle and
+                              cos/sin in fp64, each rounded once to fp32                              */
+    int32_t* status;       /* device int32; kernel rejections are OR-ed in (1 stream, 2 position,
+                              4 beyond a non-wrapping ring, 8 timeout); the caller reads and clears it */
+    int32_t layers, heads, capacity, streams, dtype, wrap, max_position;
+} mb_ring_ref;
+
+/* mb_append_attend on a caller-owned ring, allocating nothing.  Same inputs,
+ * outputs and results as mb_append_attend; scratch comes from the library's
+ * fixed device array.  The first call on each device looks that array up
+ * (cudaGetSymbolAddress, with the caller's current device), so make that first
+ * call before any stream capture.  Every call shares the one array and its
+ * ticket counters are cleared at the start of each call: calls that overlap on
+ * the GPU (other streams, other threads) race and must be serialised by the
+ * caller.  Uses the current CUDA device.  Returns MB_ERR_ARG for bad arguments
+ * or a call that needs more than MB_NOALLOC_SCRATCH_BYTES of scratch. */
+MB_API int mb_append_attend_noalloc(const mb_ring_ref* ring, int32_t layer, int32_t n, const int32_t* streams,
+                                    const int32_t* positions, const float* qkv, float* out, void* cuda_stream);
+
 /* Device addresses and sizes of the context's state. */
 MB_API int mb_ring_info_get(const mb_ctx* ctx, mb_ring_info* out);
 

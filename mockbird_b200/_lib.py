@@ -58,6 +58,23 @@ class MbRingInfo(ctypes.Structure):
     ]
 
 
+class MbRingRef(ctypes.Structure):
+    """A ring in caller-owned device memory (mb_ring_ref)."""
+    _fields_ = [
+        ("kv", ctypes.c_void_p),
+        ("slot_pos", ctypes.c_void_p),
+        ("rope", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("layers", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("capacity", ctypes.c_int32),
+        ("streams", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("wrap", ctypes.c_int32),
+        ("max_position", ctypes.c_int32),
+    ]
+
+
 SIGNATURES = {
     "mb_config_default": (None, [ctypes.POINTER(MbConfig)]),
     "mb_create": (ctypes.c_int, [ctypes.POINTER(MbConfig), ctypes.POINTER(ctypes.c_void_p)]),
@@ -73,6 +90,7 @@ SIGNATURES = {
     "mb_gather": (ctypes.c_int, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "mb_ring_write": (ctypes.c_int, [_P, _I, _I, _I, _I, _P, _P, _P]),
     "mb_sync": (ctypes.c_int, [_P, _P]),
+    "mb_append_attend_noalloc": (ctypes.c_int, [ctypes.POINTER(MbRingRef), _I, _I, _P, _P, _P, _P, _P]),
     "mb_ring_info_get": (ctypes.c_int, [_P, ctypes.POINTER(MbRingInfo)]),
     "mb_last_error": (ctypes.c_char_p, [_P]),
     "mb_version": (ctypes.c_char_p, []),
