@@ -42,6 +42,9 @@ CONFIGS = {
     2: dict(workload="config2: ring wraparound, 64 streams/GPU x 12 layers x 12 heads x 64, fp32 ring capacity "
                      "512, 1500 appends per stream (wraps twice), attention over the last <=512 positions every step",
             streams=64, layers=12, capacity=512, dtype="f32", job_steps=1500, steps=3000, warmup=30),
+    3: dict(workload="config3: causal prefill, 32 streams x (188 prompt + 256 text = 444 positions) x 12 layers "
+                     "x 12 heads x 64, fp16 ring storage (capacity 2048), fp32 accumulation, q/k/v ~ N(0, 0.5)",
+            streams=32, layers=12, capacity=2048, dtype="f16", job_steps=None, steps=20, warmup=3, rows=444),
     5: dict(workload="config5: long-text serving, 512 streams/GPU x 12 layers x 12 heads x 64, bf16 ring capacity "
                      "4096, live lengths U[1,4096] from seed 0, consecutive appends",
             streams=512, layers=12, capacity=4096, dtype="bf16", job_steps=None, steps=200, warmup=5),
@@ -292,6 +295,76 @@ def _dist():
         return None
 
 
+# ------------------------------------------------------------------ config 3: causal prefill
+def prefill_flops(rows, streams, layers=12):
+    """Causal QK^T + PV FLOPs: 4 * 64 * 12 * S(S+1)/2 per layer per stream."""
+    return 4.0 * HD * H * rows * (rows + 1) / 2 * streams * layers
+
+
+def run_prefill(args, cfg, rank, world, device):
+    """A step = the 12-layer prefill of every stream on this GPU (12 mb_prefill calls)."""
+    import torch
+
+    from mockbird_b200 import KvRing
+    from mockbird_b200.scheduler import max_over_ranks
+
+    n, L, C, S = cfg["streams"], cfg["layers"], cfg["capacity"], cfg["rows"]
+    ring = KvRing(layers=L, capacity=C, streams=n, dtype=cfg["dtype"], wrap=True, device=device.index)
+    g = torch.Generator(device=device)
+    g.manual_seed(4321 + rank)
+    qkv = torch.randn(L, n, S, QKV, generator=g, device=device) * 0.5  # 1.57 GB: one step's inputs
+    out = torch.empty(n, S, HID, device=device)
+    streams = torch.arange(n, dtype=torch.int32, device=device)
+    for _ in range(args.warmup):
+        for layer in range(L):
+            ring.prefill(layer, streams, qkv[layer], out)
+    ring.sync()
+    dist = _dist()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        for layer in range(L):
+            ring.prefill(layer, streams, qkv[layer], out)
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ring.sync()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, device if dist else None)
+    flops = prefill_flops(S, n, L) * args.steps
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpeak, tkind = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        tpeak, tkind = 1590.0, "fallback"
+    achieved = flops / (ms / 1e3) / 1e12
+    result = {
+        "metric": "causal prefill attention TFLOP/s (config 3; RoPE+cache write and attention, all 12 layers)",
+        "value": round(world * flops / (ms_max / 1e3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded N(0, 0.5) q/k/v)",
+        "config": {"workload": cfg["workload"], "streams_per_gpu": n, "rows": S, "layers": L,
+                   "l2": "inputs larger than L2: 1.57 GB of qkv per step",
+                   "positions_per_s": round(world * n * S * args.steps / (ms_max / 1e3), 1)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tpeak, "unit": "TFLOP/s",
+                     "frac": round(achieved / tpeak, 4), "traffic": None,
+                     "peak_source": f"{tkind} bf16_tflops (burst)",
+                     "timing": "CUDA events over the whole prefill calls (RoPE/cache kernel + attention kernel); "
+                               "algorithmic FLOPs are the causal QK^T + PV only"},
+        "gpu_launches": 2 * L * args.steps, "clocks": clk, "e2e": None,
+    }
+    return result, ring
+
+
 # ------------------------------------------------------------------ CPU reference (oracle port)
 def run_cpu(cfg, steps, warmup, sample_streams, budget_s=None):
     """The reference algorithm (oracle mirror of the WGSL kernels) on the host cores:
@@ -399,12 +472,15 @@ def main():
     if world > 1:
         from mockbird_b200.scheduler import init_group
         init_group("nccl", timeout_s=300)
-    result, ring = run_ours(args, cfg, rank, world, device)
+    if args.config == 3:
+        result, ring = run_prefill(args, cfg, rank, world, device)
+    else:
+        result, ring = run_ours(args, cfg, rank, world, device)
     dist = _dist()
     if dist:
         from mockbird_b200.scheduler import gather_reports
         gather_reports({"rank": rank, "value_gpu": result["value"] / world}, device)
-    if rank == 0 and world == 1 and not args.no_cpu and cfg.get("start") is None:
+    if rank == 0 and world == 1 and not args.no_cpu and cfg.get("start") is None and args.config != 3:
         result["cpu_baseline"] = run_cpu(cfg, min(args.steps, cfg["job_steps"] or args.steps), 2, sample_streams=4,
                                          budget_s=30.0)
     elif rank == 0:

@@ -12,54 +12,10 @@
 // CTA of an (item, head) to finish folds the partials (online-softmax rescale)
 // and writes the context row.  No tensor cores: one query per head is a GEMV.
 #include "mb_internal.cuh"
+#include "mb_ptx.cuh"
 
 namespace mb {
 
-// ---------------------------------------------------------------- PTX helpers
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void fence_mbar_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
-// dst, src 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-// Bounded wait for `phase` of `bar`; false if the bound ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, long long limit) {
-    const long long t0 = clock64();
-    while (true) {
-        uint32_t done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-            : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(phase)
-            : "memory");
-        if (done) return true;
-        if (clock64() - t0 > limit) return false;
-    }
-}
-
-constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s at 1.9 GHz; a bulk copy takes microseconds
 
 // ---------------------------------------------------------------- storage types
 

@@ -88,6 +88,8 @@ cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scrat
 cudaError_t launch_prefill(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
                            const float* qkv, float* out, void* q_stage, cudaStream_t st);
 size_t prefill_stage_bytes(int dtype, int n, int heads, int rows);
+cudaError_t launch_prefill_attn_tc(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
+                                   const void* q_stage, float* out, cudaStream_t st);
 cudaError_t launch_gather(int dtype, const RingView& r, int stream, int position, void* k_out, void* v_out,
                           int32_t* slots_out, cudaStream_t st);
 cudaError_t launch_ring_write(int dtype, const RingView& r, int stream, int first, int count, const void* k,

@@ -7,6 +7,8 @@
 //      scores and probabilities and applies them with one workgroup per head)
 // Here the three attention passes are one flash-style kernel: scores never leave
 // the chip.
+#include <type_traits>
+
 #include "mb_internal.cuh"
 
 namespace mb {
@@ -76,10 +78,11 @@ __global__ void __launch_bounds__(384) prefill_rope_kernel(RingView r, const int
         for (int j = rows + threadIdx.x; j < C; j += blockDim.x) r.slot_pos[(size_t)s * C + j] = -1;
 }
 
-// Causal flash attention on CUDA cores: grid (ceil(rows/64), heads, n), 128
-// threads = 64 queries x 2 halves of the head dim.  K/V tiles of 64 slots are
-// staged in shared memory as fp32; each query keeps its running max / sum and
-// 32 accumulators.  Used for fp32 rings (the tensor-core kernel covers 16-bit).
+// Causal flash attention on CUDA cores for fp32 rings (kind::f16 tensor cores
+// take 16-bit operands; 16-bit rings use mb_prefill_tc.cu): grid (ceil(rows/64),
+// heads, n), 128 threads = 64 queries x 2 halves of the head dim.  K/V tiles of 64
+// slots are staged in shared memory as fp32; each query keeps its running max /
+// sum and 32 accumulators.
 template <typename T>
 __global__ void __launch_bounds__(128) prefill_attn_simt_kernel(RingView r, const int32_t* __restrict__ streams,
                                                                 int rows, const T* __restrict__ q_stage,
@@ -165,6 +168,9 @@ static cudaError_t prefill_t(const RingView& r, int n, const int32_t* streams, i
     prefill_rope_kernel<T><<<dim3(rows, n), 384, 0, st>>>(r, streams, rows, qkv, reinterpret_cast<T*>(q_stage));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    if constexpr (sizeof(T) == 2)  // 16-bit rings: tensor cores (mb_prefill_tc.cu)
+        return launch_prefill_attn_tc(sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value ? MB_BF16 : MB_F16, r, n,
+                                      streams, rows, q_stage, out, st);
     prefill_attn_simt_kernel<T><<<dim3((rows + 63) / 64, r.heads, n), 128, 0, st>>>(
         r, streams, rows, reinterpret_cast<const T*>(q_stage), out);
     return cudaGetLastError();
