@@ -18,7 +18,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libmockbird_kv.so")
 
-SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_noalloc.cu"]
+SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_decode_persist.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_noalloc.cu"]
 HEADERS = ["mb_internal.cuh", "mb_ptx.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

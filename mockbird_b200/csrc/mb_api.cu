@@ -3,6 +3,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <vector>
@@ -89,6 +90,19 @@ int check_items_host(mb_ctx* c, int n, const int32_t* streams, const int32_t* po
     return MB_OK;
 }
 
+// The decode launch of every context entry point: the per-chunk kernel
+// (mb_decode.cu), or -- when MOCKBIRD_DECODE_KERNEL=persistent and the call fits
+// it -- the persistent stream-K kernel (mb_decode_persist.cu).  Both compute the
+// same thing.  overlap_previous: see launch_decode.
+cudaError_t run_decode(mb_ctx* c, bool append, int layer, int n, const int32_t* streams, const int32_t* positions,
+                       const float* q, int q_stride, float* out, cudaStream_t st, bool overlap_previous = false) {
+    const RingView v = ring_view(c, layer);
+    if (c->persistent && decode_persist_supported(v, n, q_stride))
+        return launch_decode_persist(c->cfg.dtype, append, v, c->scratch, n, streams, positions, q, q_stride, out, st);
+    return launch_decode(c->cfg.dtype, append, v, c->scratch, n, streams, positions, q, q_stride, out, st,
+                         overlap_previous);
+}
+
 }  // namespace
 
 extern "C" {
@@ -127,6 +141,10 @@ MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
 
     mb_ctx* c = new mb_ctx();
     c->cfg = cfg;
+    {  // MOCKBIRD_DECODE_KERNEL=persistent selects the persistent decode kernel (A/B measurements)
+        const char* k = getenv("MOCKBIRD_DECODE_KERNEL");
+        c->persistent = k && strcmp(k, "persistent") == 0;
+    }
     c->esize = cfg.dtype == MB_F32 ? 4 : 2;
     DeviceGuard g(cfg.device);
     auto bail = [&](int rc) {
@@ -162,7 +180,11 @@ MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
     // split-K scratch: one (m, l, acc[64]) partial per chunk and a ticket per (item, head)
     const int rows = chunk_rows(cfg.dtype);
     c->scratch.max_splits = (cfg.capacity + rows - 1) / rows;
-    const size_t part_bytes = (size_t)cfg.max_batch * cfg.heads * c->scratch.max_splits * (2 + HD) * sizeof(float);
+    // (the persistent kernel's units are half a chunk: it may need twice the slots)
+    const int part_slots = c->scratch.max_splits > persist_part_stride(cfg.dtype, cfg.capacity)
+                               ? c->scratch.max_splits
+                               : persist_part_stride(cfg.dtype, cfg.capacity);
+    const size_t part_bytes = (size_t)cfg.max_batch * cfg.heads * part_slots * (2 + HD) * sizeof(float);
     const size_t cnt_bytes = (size_t)cfg.max_batch * cfg.heads * sizeof(int32_t);
     c->scratch_bytes = part_bytes + cnt_bytes;
     if (cudaMalloc(&c->scratch.part, part_bytes) != cudaSuccess) return bail(MB_ERR_OOM);
@@ -233,8 +255,7 @@ MB_API int mb_attend(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams
         (q_stride & 1))
         return fail(c, MB_ERR_ARG, "null/misaligned device pointer or bad q_stride %d", q_stride);
     DeviceGuard g(c->cfg.device);
-    CK(launch_decode(c->cfg.dtype, false, ring_view(c, layer), c->scratch, n, streams, positions, q, q_stride, out,
-                     static_cast<cudaStream_t>(cuda_stream)),
+    CK(run_decode(c, false, layer, n, streams, positions, q, q_stride, out, static_cast<cudaStream_t>(cuda_stream)),
        "attend launch");
     return MB_OK;
 }
@@ -248,8 +269,8 @@ MB_API int mb_append_attend(mb_ctx* c, int32_t layer, int32_t n, const int32_t* 
     if (!streams || !positions || !qkv || !out || !aligned(qkv, 16) || !aligned(out, 16))
         return fail(c, MB_ERR_ARG, "null or misaligned device pointer");
     DeviceGuard g(c->cfg.device);
-    CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, streams, positions, qkv,
-                     3 * c->cfg.heads * HD, out, static_cast<cudaStream_t>(cuda_stream)),
+    CK(run_decode(c, true, layer, n, streams, positions, qkv, 3 * c->cfg.heads * HD, out,
+                  static_cast<cudaStream_t>(cuda_stream)),
        "append_attend launch");
     return MB_OK;
 }
@@ -266,8 +287,8 @@ MB_API int mb_decode_step(mb_ctx* c, int32_t n, const int32_t* streams, const in
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     const size_t hid = (size_t)c->cfg.heads * HD;
     for (int layer = 0; layer < c->cfg.layers; layer++)
-        CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, streams, positions,
-                         qkv + (size_t)layer * n * 3 * hid, 3 * (int)hid, out + (size_t)layer * n * hid, st),
+        CK(run_decode(c, true, layer, n, streams, positions, qkv + (size_t)layer * n * 3 * hid, 3 * (int)hid,
+                      out + (size_t)layer * n * hid, st, layer > 0),
            "append_attend launch");
     return MB_OK;
 }
@@ -302,8 +323,7 @@ MB_API int mb_append_attend_host(mb_ctx* c, int32_t layer, int32_t n, const int3
     CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy streams");
     CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy positions");
     CK(cudaMemcpyAsync(c->d_qkv, qkv, n * 3 * hid * sizeof(float), cudaMemcpyHostToDevice, st), "copy qkv");
-    CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, c->d_streams, c->d_positions, c->d_qkv,
-                     3 * (int)hid, c->d_out, st),
+    CK(run_decode(c, true, layer, n, c->d_streams, c->d_positions, c->d_qkv, 3 * (int)hid, c->d_out, st),
        "append_attend launch");
     CK(cudaMemcpyAsync(out, c->d_out, n * hid * sizeof(float), cudaMemcpyDeviceToHost, st), "copy out");
     return mb_sync(c, cuda_stream);
@@ -324,8 +344,8 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
     CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy positions");
     CK(cudaMemcpyAsync(c->d_qkv, qkv, L * n * 3 * hid * sizeof(float), cudaMemcpyHostToDevice, st), "copy qkv");
     for (int layer = 0; layer < (int)L; layer++)
-        CK(launch_decode(c->cfg.dtype, true, ring_view(c, layer), c->scratch, n, c->d_streams, c->d_positions,
-                         c->d_qkv + (size_t)layer * n * 3 * hid, 3 * (int)hid, c->d_out + (size_t)layer * n * hid, st),
+        CK(run_decode(c, true, layer, n, c->d_streams, c->d_positions, c->d_qkv + (size_t)layer * n * 3 * hid,
+                      3 * (int)hid, c->d_out + (size_t)layer * n * hid, st, layer > 0),
            "append_attend launch");
     CK(cudaMemcpyAsync(out, c->d_out, L * n * hid * sizeof(float), cudaMemcpyDeviceToHost, st), "copy out");
     return mb_sync(c, cuda_stream);

@@ -281,6 +281,12 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     float acc = 0.f;
     if (tid < HD) acc = red[0][tid] + red[1][tid] + red[2][tid] + red[3][tid];
 
+    // Programmatic dependent launch: the split-K scratch is shared by every launch,
+    // so it (and the output) is touched only once the previous launch has
+    // completed; dependents are released only after that, so a chain of launches
+    // never reaches further back than one kernel.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     float* dst = out + (size_t)item * HID + h * HD;
     if (nsplit == 1) {
         if (tid < HD) dst[tid] = l > 0.f ? acc / l : 0.f;
@@ -294,9 +300,11 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         mine[0] = m;
         mine[1] = l;
     }
-    __threadfence();
     __syncthreads();
-    if (tid == 0) ticket = atomicAdd(&sc.counters[(size_t)item * H + h], 1);
+    if (tid == 0) {  // one release for the whole CTA: the barrier orders the other threads' writes before it
+        __threadfence();
+        ticket = atomicAdd(&sc.counters[(size_t)item * H + h], 1);
+    }
     __syncthreads();
     if (ticket != nsplit - 1) return;
     __threadfence();
@@ -337,22 +345,32 @@ cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_
 
 template <typename T>
 static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, int n, const int32_t* streams,
-                            const int32_t* positions, const float* q, int q_stride, float* out, cudaStream_t st) {
-    dim3 grid(s.max_splits, r.heads, n);
-    if (append)
-        decode_kernel<T, true><<<grid, 128, 0, st>>>(r, s, streams, positions, q, q_stride, out);
-    else
-        decode_kernel<T, false><<<grid, 128, 0, st>>>(r, s, streams, positions, q, q_stride, out);
-    return cudaGetLastError();
+                            const int32_t* positions, const float* q, int q_stride, float* out, cudaStream_t st,
+                            bool overlap_previous) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(s.max_splits, r.heads, n);
+    cfg.blockDim = dim3(128);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = overlap_previous ? 1 : 0;
+    if (append) return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out);
+    return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out);
 }
 
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
                           const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
-                          float* out, cudaStream_t st) {
+                          float* out, cudaStream_t st, bool overlap_previous) {
     switch (dtype) {
-        case MB_F32: return decode_t<float>(append, r, s, n, streams, positions, q, q_stride, out, st);
-        case MB_BF16: return decode_t<__nv_bfloat16>(append, r, s, n, streams, positions, q, q_stride, out, st);
-        default: return decode_t<__half>(append, r, s, n, streams, positions, q, q_stride, out, st);
+        case MB_F32:
+            return decode_t<float>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous);
+        case MB_BF16:
+            return decode_t<__nv_bfloat16>(append, r, s, n, streams, positions, q, q_stride, out, st,
+                                           overlap_previous);
+        default:
+            return decode_t<__half>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous);
     }
 }
 

@@ -56,6 +56,7 @@ struct mb_ctx {
     int32_t* d_positions = nullptr;
     float* d_qkv = nullptr;   // [layers][max_batch][3*H*64]
     float* d_out = nullptr;   // [layers][max_batch][H*64]
+    bool persistent = false;  // decode with the persistent stream-K kernel (when it applies) instead
     std::string last_error;
 };
 
@@ -82,9 +83,18 @@ inline int chunk_rows(int dtype) { return dtype == MB_F32 ? 64 : 128; }
 // launchers (mb_decode.cu / mb_prefill.cu); return the launch's cudaError_t
 cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_t* streams,
                                const int32_t* positions, float* qkv, cudaStream_t st);
+// overlap_previous: launch with programmatic dependent launch, allowed only when
+// the previous kernel on the stream is a decode launch of a DIFFERENT layer
+// (consecutive layers of one decode step): this launch's ring reads and append
+// may then run before that kernel has finished.
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
                           const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
-                          float* out, cudaStream_t st);
+                          float* out, cudaStream_t st, bool overlap_previous = false);
+bool decode_persist_supported(const RingView& r, int n, int q_stride);
+int persist_part_stride(int dtype, int capacity);  // split-K partial slots per (item, head)
+cudaError_t launch_decode_persist(int dtype, bool append, const RingView& r, const Scratch& s, int n,
+                                  const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
+                                  float* out, cudaStream_t st);
 cudaError_t launch_prefill(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
                            const float* qkv, float* out, void* q_stage, cudaStream_t st);
 size_t prefill_stage_bytes(int dtype, int n, int heads, int rows);

@@ -2,11 +2,14 @@
 // for 16-bit rings: the ATTENTION_SCORES / _SOFTMAX / _APPLY passes of the
 // reference (kernels-batch.ts:246-350) as one flash-attention kernel.
 //
-// One CTA = 128 queries of one (item, head); 4 warps, thread t owns query row t,
-// which is also its TMEM lane.  Per 128-key tile j (causal: j <= query tile):
+// One CTA = 128 queries of one (item, head); 8 warps: warps w and w+4 read TMEM
+// lanes 32(w%4).. (query rows), w/4 picks the half of the key columns (and of
+// the output dims) a thread owns.  Per 128-key tile j (causal: j <= query tile):
 //   S = Q K^T   tcgen05.mma kind::f16, M=128 N=128 K=64, fp32 into TMEM cols [0,128)
-//   softmax     tcgen05.ld S, online max/sum in registers, P (16-bit) written to
-//               shared memory in the 128-byte-swizzled K-major layout
+//   softmax     tcgen05.ld S into registers, row max across the two halves in
+//               shared memory, exp2 with four independent partial sums, P (16-bit)
+//               written to shared memory in the 128-byte-swizzled K-major layout;
+//               tiles with no masked key skip the mask
 //   O_j = P V   tcgen05.mma, M=128 N=64 K=128 (V as an MN-major operand), TMEM cols [128,192)
 //   O = O*corr + O_j in registers
 // Q, K, V arrive by 3-D TMA tile loads (128-byte swizzle, zero fill past the last
@@ -29,12 +32,14 @@ constexpr int BN = 128;                   // keys per tile
 constexpr int TILE = BM * HD * 2;         // [128][64] 16-bit = 16 KB
 constexpr uint32_t TMEM_COLS = 256;       // S [0,128) | O tile [128,192)
 constexpr uint32_t S_COL = 0, O_COL = 128;
+constexpr int NTHREADS = 256;             // 8 warps: (TMEM lane quarter) x (column half)
 
 struct alignas(1024) TcSmem {
     unsigned char q[TILE];
     unsigned char k[TILE];
     unsigned char v[TILE];
     unsigned char p[2][TILE];             // P: keys [0,64) and [64,128) as two K-major sub-tiles
+    float rmax[2][BM];                    // per column half: row maxima, then row sums
     uint64_t bar_q, bar_k, bar_v, bar_mma;
     uint32_t tmem_base;
 };
@@ -51,8 +56,14 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     }
 }
 
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <bool BF16>
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(NTHREADS, 2)
     prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
                            RingView r, const int32_t* __restrict__ streams, int rows, float* __restrict__ out) {
     extern __shared__ unsigned char smem_raw[];
@@ -81,7 +92,7 @@ __global__ void __launch_bounds__(128, 2)
     const uint32_t tbase = sm.tmem_base;
 
     // issue/complete counts per barrier (identical in every thread: the control flow is uniform)
-    int k_issued = 0, k_done = 0, v_issued = 0, v_done = 0, mma_issued = 0, mma_done = 0;
+    int k_issued = 1, k_done = 0, v_issued = 1, v_done = 0, mma_issued = 0, mma_done = 0;
     if (tid == 0) {
         mbar_expect_tx(&sm.bar_q, TILE);
         tma_load_3d(sm.q, &tq, 0, q0, qplane, &sm.bar_q);
@@ -90,18 +101,19 @@ __global__ void __launch_bounds__(128, 2)
         mbar_expect_tx(&sm.bar_v, TILE);
         tma_load_3d(sm.v, &tkv, 0, 0, vplane, &sm.bar_v);
     }
-    k_issued = v_issued = 1;
 
     constexpr uint32_t IDESC_QK = idesc_f16(BF16 ? 1u : 0u, 0u, BM, BN);
     constexpr uint32_t IDESC_PV = idesc_f16(BF16 ? 1u : 0u, 1u, BM, HD);
     const float scale = SCALE * LOG2E;
-    const int row = warp * 32 + lane;
+    // warps w and w+4 share TMEM lanes 32(w%4).. (query rows); w/4 picks the column half
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;
     const int qg = q0 + row;
-    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
-    float o[HD];
+    const uint32_t lane_addr = tbase + ((uint32_t)(quarter * 32) << 16);
+    float o[HD / 2];
 #pragma unroll
-    for (int d = 0; d < HD; d++) o[d] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
+    for (int d = 0; d < HD / 2; d++) o[d] = 0.f;
+    float m_run = -INFINITY, l_half = 0.f;
 
     bool ok = __syncthreads_and(mbar_wait(&sm.bar_q, 0, WAIT_LIMIT));
     bool q_done = ok;
@@ -131,44 +143,60 @@ __global__ void __launch_bounds__(128, 2)
         if (j + 1 < ntiles) k_issued++;
         tc_fence_after();
 
-        // ---- online softmax of this tile (causal mask key <= query, keys < rows)
-        float mx = -INFINITY;
+        // ---- this thread's 64 scores (keys k0 + 64*half ..), kept in registers
+        float sv[64];
+        tmem_ld32(lane_addr + S_COL + 64 * half, sv);
+        tmem_ld32(lane_addr + S_COL + 64 * half + 32, sv + 32);
+        const int kb = k0 + 64 * half;
+        const bool full = (k0 + BN <= q0) && (k0 + BN <= rows);  // no key of the tile is masked
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            float v[32];
-            tmem_ld32(lane_addr + S_COL + 32 * c, v);
+            for (int i = 0; i < 64; i += 4) {
+                sv[i] *= scale;
+                sv[i + 1] *= scale;
+                sv[i + 2] *= scale;
+                sv[i + 3] *= scale;
+                mx0 = fmaxf(mx0, sv[i]);
+                mx1 = fmaxf(mx1, sv[i + 1]);
+                mx2 = fmaxf(mx2, sv[i + 2]);
+                mx3 = fmaxf(mx3, sv[i + 3]);
+            }
+        } else {  // causal mask key <= query, and keys < rows
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
-                const int key = k0 + 32 * c + i;
-                if (key <= qg && key < rows) mx = fmaxf(mx, v[i] * scale);
+            for (int i = 0; i < 64; i++) {
+                const int key = kb + i;
+                sv[i] = (key <= qg && key < rows) ? sv[i] * scale : -INFINITY;
+            }
+#pragma unroll
+            for (int i = 0; i < 64; i += 4) {
+                mx0 = fmaxf(mx0, sv[i]);
+                mx1 = fmaxf(mx1, sv[i + 1]);
+                mx2 = fmaxf(mx2, sv[i + 2]);
+                mx3 = fmaxf(mx3, sv[i + 3]);
             }
         }
-        const float m_new = fmaxf(m_run, mx);
-        const float corr = exp2f(m_run - m_new);  // 0 on the first tile (m_run = -inf)
-        float lsum = 0.f;
+        sm.rmax[half][row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        __syncthreads();
+        const float m_tile = fmaxf(sm.rmax[0][row], sm.rmax[1][row]);
+        const float m_new = fmaxf(m_run, m_tile);   // finite: key 0 of tile 0 is never masked
+        const float corr = ex2(m_run - m_new);      // 0 on the first tile (m_run = -inf)
+        float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
+        unsigned char* sub = sm.p[half] + row * 128;  // this half's 64 keys = P sub-tile `half`
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            float v[32];
-            tmem_ld32(lane_addr + S_COL + 32 * c, v);
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-                const int key = k0 + 32 * c + i;
-                const float p0 = (key <= qg && key < rows) ? exp2f(v[i] * scale - m_new) : 0.f;
-                const float p1 = (key + 1 <= qg && key + 1 < rows) ? exp2f(v[i + 1] * scale - m_new) : 0.f;
-                lsum += p0 + p1;
-                pk[i >> 1] = pack2<BF16>(p0, p1);
-            }
-            // 32 keys = four 16-byte chunks of this row of sub-tile c/2; 128-byte swizzle
-            unsigned char* sub = sm.p[c >> 1] + row * 128;
-#pragma unroll
-            for (int qd = 0; qd < 4; qd++) {
-                const int chunk = (c & 1) * 4 + qd;
-                *reinterpret_cast<uint4*>(sub + ((chunk ^ (row & 7)) << 4)) =
-                    make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
-            }
+        for (int ch = 0; ch < 8; ch++) {
+            const float p0 = ex2(sv[8 * ch + 0] - m_new), p1 = ex2(sv[8 * ch + 1] - m_new);
+            const float p2 = ex2(sv[8 * ch + 2] - m_new), p3 = ex2(sv[8 * ch + 3] - m_new);
+            const float p4 = ex2(sv[8 * ch + 4] - m_new), p5 = ex2(sv[8 * ch + 5] - m_new);
+            const float p6 = ex2(sv[8 * ch + 6] - m_new), p7 = ex2(sv[8 * ch + 7] - m_new);
+            ls0 += p0 + p4;
+            ls1 += p1 + p5;
+            ls2 += p2 + p6;
+            ls3 += p3 + p7;
+            *reinterpret_cast<uint4*>(sub + ((ch ^ (row & 7)) << 4)) =
+                make_uint4(pack2<BF16>(p0, p1), pack2<BF16>(p2, p3), pack2<BF16>(p4, p5), pack2<BF16>(p6, p7));
         }
-        l_run = l_run * corr + lsum;
+        l_half = l_half * corr + ((ls0 + ls1) + (ls2 + ls3));
         m_run = m_new;
         fence_async_smem();
         tc_fence_before();
@@ -198,23 +226,22 @@ __global__ void __launch_bounds__(128, 2)
         tc_fence_after();
         {
             float v[32];
-            tmem_ld32(lane_addr + O_COL, v);
+            tmem_ld32(lane_addr + O_COL + 32 * half, v);
 #pragma unroll
             for (int i = 0; i < 32; i++) o[i] = fmaf(o[i], corr, v[i]);
-            tmem_ld32(lane_addr + O_COL + 32, v);
-#pragma unroll
-            for (int i = 0; i < 32; i++) o[32 + i] = fmaf(o[32 + i], corr, v[i]);
         }
         tc_fence_before();
         __syncthreads();  // S, the O tile and P are free for the next tile
     }
 
     if (ok) {
+        sm.rmax[half][row] = l_half;  // exchange the two halves' sums
+        __syncthreads();
         if (qg < rows) {
-            const float inv = 1.f / l_run;
-            float* dst = out + ((size_t)item * rows + qg) * H * HD + h * HD;
+            const float inv = 1.f / (sm.rmax[0][row] + sm.rmax[1][row]);
+            float* dst = out + ((size_t)item * rows + qg) * H * HD + h * HD + 32 * half;
 #pragma unroll
-            for (int d = 0; d < HD; d += 4)
+            for (int d = 0; d < 32; d += 4)
                 *reinterpret_cast<float4*>(dst + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv,
                                                                   o[d + 3] * inv);
         }
@@ -284,7 +311,7 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
         attr_set[dev] = true;
     }
     dim3 grid((rows + BM - 1) / BM, r.heads, n);
-    prefill_attn_tc_kernel<BF16><<<grid, 128, SMEM_BYTES, st>>>(tq, tkv, r, streams, rows, out);
+    prefill_attn_tc_kernel<BF16><<<grid, NTHREADS, SMEM_BYTES, st>>>(tq, tkv, r, streams, rows, out);
     return cudaGetLastError();
 }
 

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import oracle
-from gpu_util import HD, HID, QKV, TOL, H, assert_window_equal, from_np_storage, max_err, randn, to_np_storage
+from gpu_util import HD, HID, QKV, TOL, H, assert_window_equal, from_np_storage, max_err, randn, to_np_storage  # noqa: F401
 from mockbird_b200 import KvRing, MockbirdError
 
 pytestmark = pytest.mark.gpu
@@ -288,3 +288,101 @@ def test_empty_window_reset_and_poison_readback():
     out = ring.attend_ring(0, [0], [1], q)
     assert torch.count_nonzero(out).item() == 0
     ring.sync()
+
+
+@pytest.mark.parametrize("dtype,C,items", [("f32", 512, 64), ("bf16", 4096, 3), ("f16", 256, 37)])
+def test_persistent_and_chunked_kernels_agree(dtype, C, items, monkeypatch):
+    """The per-chunk decode kernel (default) and the persistent stream-K kernel
+    (MOCKBIRD_DECODE_KERNEL=persistent) compute the same thing: identical ring bytes, contexts within fp32 rounding, and both
+    within the oracle tolerance.  Windows of varied length, some split across CTAs."""
+    rings = {}
+    for kernel in ("persistent", "chunked"):
+        monkeypatch.setenv("MOCKBIRD_DECODE_KERNEL", kernel)
+        rings[kernel] = KvRing(layers=2, streams=items, capacity=C, dtype=dtype, wrap=True)
+    orc = oracle.Ring(layers=2, streams=items, heads=H, capacity=C, dtype=dtype, wrap=True)
+    rng = np.random.default_rng(11)
+    start = rng.integers(0, 3 * C, size=items)  # streams at different points, some already wrapped
+    for s in range(items):  # jump-start: write the positions before start[s] directly
+        first = max(0, int(start[s]) - C)
+        cnt = int(start[s]) - first
+        if cnt == 0:
+            continue
+        k = oracle.round_to(dtype, rng.standard_normal((H, cnt, HD)).astype(np.float32))
+        v = oracle.round_to(dtype, rng.standard_normal((H, cnt, HD)).astype(np.float32))
+        for ring in rings.values():
+            for layer in range(2):
+                ring.ring_write(layer, s, first, from_np_storage(_to_storage(k, dtype), dtype),
+                                from_np_storage(_to_storage(v, dtype), dtype))
+        for layer in range(2):
+            for w in range(cnt):
+                p = first + w
+                orc.kv_view()[layer, s, 0, :, p % C] = _to_storage(k[:, w], dtype)
+                orc.kv_view()[layer, s, 1, :, p % C] = _to_storage(v[:, w], dtype)
+                orc.slot_pos[layer, s, p % C] = p
+    order = list(rng.permutation(items))
+    worst = {"persistent": 0.0, "chunked": 0.0}
+    for step in range(6):
+        pos = [int(start[s]) + step for s in order]
+        qkv = randn((items, QKV), seed=700 + step)
+        outs = {kname: ring.append_attend(step % 2, order, pos, torch.from_numpy(qkv).to(DEV))
+                for kname, ring in rings.items()}
+        ref, _ = orc.append_attend(step % 2, order, pos, qkv)
+        for kname, o in outs.items():
+            worst[kname] = max(worst[kname], max_err(o, ref))
+        assert max_err(outs["persistent"], outs["chunked"]) < 1e-5
+    for ring in rings.values():
+        ring.sync()
+    for kname in rings:
+        assert worst[kname] < TOL[dtype], (kname, worst)
+    for s, p in zip(order, pos):
+        ka, va, sa = rings["persistent"].gather(1, s, p)
+        kb, vb, sb = rings["chunked"].gather(1, s, p)
+        assert torch.equal(sa, sb) and torch.equal(ka, kb) and torch.equal(va, vb)
+        assert_window_equal(rings["persistent"], orc, 1, s, 1, s, p)
+
+
+def test_many_streams_take_the_chunked_kernel():
+    """More items than the persistent kernel's prologue holds (2048): same results."""
+    S, C = 2100, 8
+    ring = KvRing(layers=1, streams=S, capacity=C, dtype="f32", wrap=True)
+    orc = oracle.Ring(layers=1, streams=S, heads=H, capacity=C, dtype="f32", wrap=True)
+    for step in range(10):
+        qkv = randn((S, QKV), seed=900 + step)
+        out = ring.append_attend(0, np.arange(S), [step] * S, torch.from_numpy(qkv).to(DEV))
+        ref, _ = orc.append_attend(0, np.arange(S), [step] * S, qkv)
+        assert max_err(out, ref) < TOL["f32"]
+    ring.sync()
+
+
+@pytest.mark.parametrize("capacity", [500, 1696, 2480, 3248])
+def test_codec_ring_geometry(capacity):
+    """The codec decoder's rings (codec.ts:1-28, 204-225): d = 256 = 4 heads x 64,
+    wrapping capacities 500 / 1696 / 2480 / 3248, fp32, slot = pos % C with the
+    stored-position mask (ATTEND_RING_CODEC, kernels-decode.ts:590-667)."""
+    heads, L, S = 4, 2, 3
+    ring = KvRing(layers=L, heads=heads, streams=S, capacity=capacity, dtype="f32", wrap=True)
+    orc = oracle.Ring(layers=L, streams=S, heads=heads, capacity=capacity, dtype="f32", wrap=True)
+    w = 3 * heads * HD
+    rng = np.random.default_rng(capacity)
+    # jump close to the wrap, then append across it
+    first = capacity - 40
+    for s in range(S):
+        for layer in range(L):
+            k = rng.standard_normal((heads, first, HD)).astype(np.float32)
+            v = rng.standard_normal((heads, first, HD)).astype(np.float32)
+            ring.ring_write(layer, s, 0, torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV))
+            orc.kv_view()[layer, s, 0, :, :first] = k
+            orc.kv_view()[layer, s, 1, :, :first] = v
+            orc.slot_pos[layer, s, :first] = np.arange(first)
+    worst = 0.0
+    for step in range(first, capacity + 60):
+        qkv = rng.standard_normal((S, w)).astype(np.float32)
+        layer = step % L
+        out = ring.append_attend(layer, [2, 0, 1], [step] * S, torch.from_numpy(qkv).to(DEV))
+        ref, _ = orc.append_attend(layer, [2, 0, 1], [step] * S, qkv)
+        worst = max(worst, max_err(out, ref))
+    ring.sync()
+    assert worst < TOL["f32"], worst
+    last = capacity + 59
+    for s in range(S):
+        assert_window_equal(ring, orc, last % L, s, last % L, s, last)
