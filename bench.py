@@ -503,7 +503,7 @@ def main():
     torch.cuda.set_device(device)
     if world > 1:
         from mockbird_b200.scheduler import init_group
-        init_group("nccl", timeout_s=300)
+        init_group("nccl", timeout_s=300, device=device)
     if args.config == 3:
         result, ring = run_prefill(args, cfg, rank, world, device)
     else:

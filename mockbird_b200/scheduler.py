@@ -69,16 +69,20 @@ def dist_env() -> tuple[int, int, int]:
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
-def init_group(backend: str, timeout_s: float = 120.0):
-    """Initialise the default process group from the environment (127.0.0.1 rendezvous)."""
+def init_group(backend: str, timeout_s: float = 120.0, device=None):
+    """Initialise the default process group from the environment (127.0.0.1 rendezvous).
+
+    `device`: this rank's CUDA device (NCCL binds the group to it)."""
     import torch.distributed as dist
 
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     os.environ.setdefault("MASTER_PORT", "29511")
+    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout for the report line
     rank, world, _ = dist_env()
     if not dist.is_initialized():
+        kw = {"device_id": device} if device is not None else {}
         dist.init_process_group(backend, rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=timeout_s))
+                                timeout=datetime.timedelta(seconds=timeout_s), **kw)
     return dist
 
 
