@@ -175,6 +175,36 @@ MB_API int mb_ring_write(mb_ctx* ctx, int32_t layer, int32_t stream, int32_t fir
 MB_API int mb_sync(mb_ctx* ctx, void* cuda_stream);
 
 /* ---------------------------------------------------------------------------
+ * The decode step around the path: the whole global
+ * transformer layer of DecodeRunner.runLayer (decode.ts:474-620) for n streams
+ * at once -- LN1 -> QKV GEMM -> append + RoPE + attention -> c_proj GEMM +
+ * residual -> LN2 -> fc_in GEMM + GELU(tanh) -> fc_out GEMM + residual -- and
+ * the final LayerNorm, over a context's rings.  The GEMMs are cuBLASLt (bf16
+ * weights, fp32 accumulation); LayerNorm (eps 1e-5), GELU(tanh) and the
+ * attention are this library's kernels.
+ * ------------------------------------------------------------------------- */
+
+typedef struct mb_decoder mb_decoder;
+
+/* Weights as one host array of fp32 in the order of the published graph, per
+ * layer (matrices [K][N] row-major, y = b + x W, docs analysis :651):
+ *   ln1_w[H*64] ln1_b[H*64] c_attn_w[H*64][3*H*64] c_attn_b[3*H*64]
+ *   c_proj_w[H*64][H*64] c_proj_b[H*64] ln2_w[H*64] ln2_b[H*64]
+ *   fc_in_w[H*64][ffn] fc_in_b[ffn] fc_out_w[ffn][H*64] fc_out_b[H*64]
+ * then ln_f_w[H*64] ln_f_b[H*64].  Matrices are stored on the device as bf16.
+ * `count` must equal mb_decoder_weight_count(ctx, ffn). */
+MB_API size_t mb_decoder_weight_count(const mb_ctx* ctx, int32_t ffn);
+MB_API int mb_decoder_create(mb_ctx* ctx, int32_t ffn, const float* host_weights, size_t count, mb_decoder** out);
+MB_API int mb_decoder_destroy(mb_decoder* dec);
+
+/* One global decode step for n streams: hidden [n][H*64] fp32 (device) holds the
+ * embedded rows on entry and ln_f of the last layer on return
+ * (DecodeRunner.globalStep, decode.ts:712-775, without the embedding).  Each
+ * stream appends at its position in every layer's ring. */
+MB_API int mb_decoder_step(mb_decoder* dec, int32_t n, const int32_t* streams, const int32_t* positions,
+                           float* hidden, void* cuda_stream);
+
+/* ---------------------------------------------------------------------------
  * No-allocation entry point.  No counterpart in the reference: the reference
  * allocates its GPU buffers once per engine and never hands that job to callers.
  *

@@ -90,6 +90,10 @@ SIGNATURES = {
     "mb_gather": (ctypes.c_int, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "mb_ring_write": (ctypes.c_int, [_P, _I, _I, _I, _I, _P, _P, _P]),
     "mb_sync": (ctypes.c_int, [_P, _P]),
+    "mb_decoder_weight_count": (ctypes.c_size_t, [_P, _I]),
+    "mb_decoder_create": (ctypes.c_int, [_P, _I, _P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_decoder_destroy": (ctypes.c_int, [_P]),
+    "mb_decoder_step": (ctypes.c_int, [_P, _I, _P, _P, _P, _P]),
     "mb_append_attend_noalloc": (ctypes.c_int, [ctypes.POINTER(MbRingRef), _I, _I, _P, _P, _P, _P, _P]),
     "mb_ring_info_get": (ctypes.c_int, [_P, ctypes.POINTER(MbRingInfo)]),
     "mb_last_error": (ctypes.c_char_p, [_P]),

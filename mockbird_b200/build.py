@@ -18,10 +18,13 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libmockbird_kv.so")
 
-SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_decode_persist.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_noalloc.cu"]
+SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_decode_persist.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_decoder.cu",
+           "mb_noalloc.cu"]
 HEADERS = ["mb_internal.cuh", "mb_ptx.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# cuBLASLt: the plain GEMMs of the decoder step around the path
+LINK = ["-lcublasLt", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
 
 
 def nvcc() -> str:
@@ -52,7 +55,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         return LIB
     cmd = [nvcc(), *host_compiler(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "-I", INCLUDE, "-I", CSRC, "-o", LIB + ".tmp",
-           *(extra or []), *[os.path.join(CSRC, s) for s in SOURCES]]
+           *(extra or []), *[os.path.join(CSRC, s) for s in SOURCES], *LINK]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

@@ -1,0 +1,324 @@
+// The decode step around the KV-ring path: the global
+// transformer layer of DecodeRunner.runLayer (liyu1981/mockbird,
+// src/lib/tts/engine/decode.ts:474-620) for n streams at once, and the final
+// LayerNorm of globalStep (decode.ts:749-772).
+//
+// Per layer: LN1 -> QKV GEMM -> append + RoPE + attention (this library's decode
+// kernel) -> c_proj GEMM + residual -> LN2 -> fc_in GEMM -> GELU(tanh) -> fc_out
+// GEMM + residual.  The four GEMMs are plain library GEMMs (cuBLASLt, bf16
+// weights and activations, fp32 accumulation, bias and residual in the
+// epilogue: y = b + x W, W [K][N] row-major as the published graph stores it);
+// LayerNorm (LAYERNORM_1, kernels-decode.ts:168-200: eps 1e-5, two passes) and
+// GELU (GELU_TANH, kernels-decode.ts:373-390) are kernels here.
+#include <cublasLt.h>
+#include <string.h>
+
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "mb_internal.cuh"
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+// ---------------------------------------------------------------- kernels
+
+// One warp per row: mean, then the mean squared deviation (the two passes of
+// LAYERNORM_1), out = (x - mean) * rsqrt(var + 1e-5) * w + b.  In place is fine:
+// the row is in registers before it is written.
+template <typename TO, int PER>
+__global__ void layernorm_rows(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                               TO* __restrict__ y, int rows, int width) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + (size_t)row * width;
+    float v[PER];
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        v[i] = xr[lane + 32 * i];
+        sum += v[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / (float)width;
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const float d = v[i] - mean;
+        sq += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float inv = rsqrtf(sq / (float)width + 1e-5f);
+    TO* yr = y + (size_t)row * width;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int c = lane + 32 * i;
+        yr[c] = (TO)((v[i] - mean) * inv * w[c] + b[c]);
+    }
+}
+
+// GELU, tanh approximation (GELU_TANH), fp32 in -> bf16 out
+__global__ void gelu_tanh_to_bf16(const float* __restrict__ x, bf16* __restrict__ y, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+        y[i] = __float2bfloat16_rn(0.5f * v * (1.f + tanhf(inner)));
+    }
+}
+
+__global__ void to_bf16(const float* __restrict__ x, bf16* __restrict__ y, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+
+uint16_t f32_to_bf16_bits(float f) {  // round to nearest even
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+}  // namespace
+
+struct mb_decoder {
+    mb_ctx* ctx = nullptr;
+    int hid = 0, ffn = 0, layers = 0;
+    struct Layer {
+        const float *ln1_w, *ln1_b, *b_attn, *b_proj, *ln2_w, *ln2_b, *b_in, *b_out;
+        const bf16 *w_attn, *w_proj, *w_in, *w_out;
+    };
+    std::vector<Layer> L;
+    const float *lnf_w = nullptr, *lnf_b = nullptr;
+    void* wmem = nullptr;      // all weights, one allocation
+    bf16* xb = nullptr;        // [max_batch][max(hid, ffn)] GEMM input
+    float* qkv = nullptr;      // [max_batch][3*hid]
+    float* att = nullptr;      // [max_batch][hid]
+    float* h1 = nullptr;       // [max_batch][ffn]
+    cublasLtHandle_t lt = nullptr;
+    void* workspace = nullptr;
+    size_t ws_bytes = 32u << 20;
+    std::map<std::tuple<int, int, int, int>, cublasLtMatmulAlgo_t> algos;
+};
+
+namespace {
+
+int dfail(mb_decoder* d, int code, const std::string& msg) {
+    if (d && d->ctx) d->ctx->last_error = msg;
+    return code;
+}
+
+// y[M][N] (fp32, row-major) = x[M][K] (bf16) * W[K][N] (bf16) + bias[N] (+ y if accumulate)
+int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const float* bias, float* y,
+         bool accumulate, cudaStream_t st) {
+    // column-major view: y^T [N x M] = W^T [N x K] * x^T [K x M]
+    cublasLtMatmulDesc_t op = nullptr;
+    cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
+    cublasStatus_t s = cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F);
+    cublasLtEpilogue_t epi = CUBLASLT_EPILOGUE_BIAS;
+    cudaDataType_t bias_t = CUDA_R_32F;
+    if (s == CUBLAS_STATUS_SUCCESS)
+        s = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof epi);
+    if (s == CUBLAS_STATUS_SUCCESS)
+        s = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
+    if (s == CUBLAS_STATUS_SUCCESS)
+        s = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bias_t, sizeof bias_t);
+    if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&a, CUDA_R_16BF, N, K, N);
+    if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&b, CUDA_R_16BF, K, M, K);
+    if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&c, CUDA_R_32F, N, M, N);
+    const auto key = std::make_tuple(M, N, K, accumulate ? 1 : 0);
+    auto it = d->algos.find(key);
+    if (s == CUBLAS_STATUS_SUCCESS && it == d->algos.end()) {
+        cublasLtMatmulPreference_t pref = nullptr;
+        s = cublasLtMatmulPreferenceCreate(&pref);
+        if (s == CUBLAS_STATUS_SUCCESS)
+            s = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &d->ws_bytes,
+                                                     sizeof d->ws_bytes);
+        cublasLtMatmulHeuristicResult_t res = {};
+        int found = 0;
+        if (s == CUBLAS_STATUS_SUCCESS)
+            s = cublasLtMatmulAlgoGetHeuristic(d->lt, op, a, b, c, c, pref, 1, &res, &found);
+        if (pref) cublasLtMatmulPreferenceDestroy(pref);
+        if (s == CUBLAS_STATUS_SUCCESS && found == 0) s = CUBLAS_STATUS_NOT_SUPPORTED;
+        if (s == CUBLAS_STATUS_SUCCESS) it = d->algos.emplace(key, res.algo).first;
+    }
+    const float alpha = 1.f, beta = accumulate ? 1.f : 0.f;
+    if (s == CUBLAS_STATUS_SUCCESS)
+        s = cublasLtMatmul(d->lt, op, &alpha, W, a, x, b, &beta, y, c, y, c, &it->second, d->workspace, d->ws_bytes,
+                           st);
+    if (c) cublasLtMatrixLayoutDestroy(c);
+    if (b) cublasLtMatrixLayoutDestroy(b);
+    if (a) cublasLtMatrixLayoutDestroy(a);
+    if (op) cublasLtMatmulDescDestroy(op);
+    if (s != CUBLAS_STATUS_SUCCESS)
+        return dfail(d, MB_ERR_CUDA, std::string("cuBLASLt matmul failed: ") + cublasLtGetStatusString(s));
+    return MB_OK;
+}
+
+template <typename TO>
+cudaError_t layernorm(const float* x, const float* w, const float* b, TO* y, int rows, int width, cudaStream_t st) {
+    const int warps = 4, blocks = (rows + warps - 1) / warps;
+    switch (width / 32) {  // width = heads * 64
+        case 2: layernorm_rows<TO, 2><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
+        case 8: layernorm_rows<TO, 8><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
+        case 24: layernorm_rows<TO, 24><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+MB_API size_t mb_decoder_weight_count(const mb_ctx* c, int32_t ffn) {
+    if (!c || ffn <= 0) return 0;
+    const size_t h = (size_t)c->cfg.heads * mb::HD, f = (size_t)ffn;
+    const size_t per_layer = 2 * h + h * 3 * h + 3 * h + h * h + h + 2 * h + h * f + f + f * h + h;
+    return per_layer * c->cfg.layers + 2 * h;
+}
+
+MB_API int mb_decoder_destroy(mb_decoder* d) {
+    if (!d) return MB_ERR_ARG;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d->ctx->cfg.device);
+    void* ptrs[] = {d->wmem, d->xb, d->qkv, d->att, d->h1, d->workspace};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    if (d->lt) cublasLtDestroy(d->lt);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete d;
+    return MB_OK;
+}
+
+MB_API int mb_decoder_create(mb_ctx* c, int32_t ffn, const float* w, size_t count, mb_decoder** out) {
+    if (!c || !w || !out || ffn <= 0 || ffn % 64) return MB_ERR_ARG;
+    *out = nullptr;
+    const int h = c->cfg.heads * mb::HD;
+    if (h / 32 != 2 && h / 32 != 8 && h / 32 != 24) {
+        c->last_error = "decoder: hidden width must be 64, 256 or 768";
+        return MB_ERR_ARG;
+    }
+    if (count != mb_decoder_weight_count(c, ffn)) {
+        c->last_error = "decoder: weight count does not match layers x (hidden, ffn)";
+        return MB_ERR_ARG;
+    }
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(c->cfg.device) != cudaSuccess) return MB_ERR_CUDA;
+    mb_decoder* d = new mb_decoder();
+    d->ctx = c;
+    d->hid = h;
+    d->ffn = ffn;
+    d->layers = c->cfg.layers;
+    auto bail = [&](int rc, const char* msg) {
+        c->last_error = msg;
+        mb_decoder_destroy(d);
+        if (prev >= 0) cudaSetDevice(prev);
+        return rc;
+    };
+    // device image: fp32 vectors first, then bf16 matrices (each block 256-byte aligned)
+    struct Blk {
+        size_t src, n;
+        bool mat;
+        size_t dst;
+    };
+    std::vector<Blk> blks;
+    size_t src = 0;
+    auto add = [&](size_t n, bool mat) {
+        blks.push_back({src, n, mat, 0});
+        src += n;
+    };
+    for (int l = 0; l < d->layers; l++) {
+        add(h, false), add(h, false);                    // ln1
+        add((size_t)h * 3 * h, true), add(3 * h, false);  // c_attn
+        add((size_t)h * h, true), add(h, false);          // c_proj
+        add(h, false), add(h, false);                    // ln2
+        add((size_t)h * ffn, true), add(ffn, false);      // fc_in
+        add((size_t)ffn * h, true), add(h, false);        // fc_out
+    }
+    add(h, false), add(h, false);  // ln_f
+    size_t bytes = 0;
+    for (auto& b : blks) {
+        b.dst = bytes;
+        bytes += ((b.n * (b.mat ? 2 : 4)) + 255) & ~size_t(255);
+    }
+    std::vector<unsigned char> img(bytes, 0);
+    for (auto& b : blks) {
+        if (b.mat) {
+            uint16_t* o = reinterpret_cast<uint16_t*>(img.data() + b.dst);
+            for (size_t i = 0; i < b.n; i++) o[i] = f32_to_bf16_bits(w[b.src + i]);
+        } else {
+            memcpy(img.data() + b.dst, w + b.src, b.n * 4);
+        }
+    }
+    if (cudaMalloc(&d->wmem, bytes) != cudaSuccess) return bail(MB_ERR_OOM, "decoder: weight allocation failed");
+    if (cudaMemcpy(d->wmem, img.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+        return bail(MB_ERR_CUDA, "decoder: weight upload failed");
+    auto F = [&](size_t i) { return reinterpret_cast<const float*>((char*)d->wmem + blks[i].dst); };
+    auto B = [&](size_t i) { return reinterpret_cast<const bf16*>((char*)d->wmem + blks[i].dst); };
+    for (int l = 0; l < d->layers; l++) {
+        const size_t o = (size_t)l * 12;
+        d->L.push_back({F(o + 0), F(o + 1), F(o + 3), F(o + 5), F(o + 6), F(o + 7), F(o + 9), F(o + 11), B(o + 2),
+                        B(o + 4), B(o + 8), B(o + 10)});
+    }
+    d->lnf_w = F(blks.size() - 2);
+    d->lnf_b = F(blks.size() - 1);
+    const size_t mb = c->cfg.max_batch, wide = (size_t)(ffn > h ? ffn : h);
+    if (cudaMalloc(&d->xb, mb * wide * sizeof(bf16)) != cudaSuccess ||
+        cudaMalloc(&d->qkv, mb * 3 * h * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&d->att, mb * h * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&d->h1, mb * ffn * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&d->workspace, d->ws_bytes) != cudaSuccess)
+        return bail(MB_ERR_OOM, "decoder: activation allocation failed");
+    if (cublasLtCreate(&d->lt) != CUBLAS_STATUS_SUCCESS) return bail(MB_ERR_CUDA, "decoder: cublasLtCreate failed");
+    if (prev >= 0) cudaSetDevice(prev);
+    *out = d;
+    return MB_OK;
+}
+
+MB_API int mb_decoder_step(mb_decoder* d, int32_t n, const int32_t* streams, const int32_t* positions,
+                           float* hidden, void* cuda_stream) {
+    if (!d) return MB_ERR_ARG;
+    mb_ctx* c = d->ctx;
+    if (n < 0 || n > c->cfg.max_batch) return dfail(d, MB_ERR_ARG, "decoder: item count out of range");
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !hidden || (reinterpret_cast<uintptr_t>(hidden) & 15))
+        return dfail(d, MB_ERR_ARG, "decoder: null or misaligned device pointer");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != c->cfg.device && cudaSetDevice(c->cfg.device) != cudaSuccess) return MB_ERR_CUDA;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const int h = d->hid, f = d->ffn;
+    const int cvt_blocks = 2 * 148;
+    int rc = MB_OK;
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < d->layers && rc == MB_OK && e == cudaSuccess; l++) {
+        const auto& W = d->L[l];
+        if ((e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess) break;
+        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, false, st))) break;
+        if ((e = mb::launch_decode(c->cfg.dtype, true, mb::ring_view(c, l), c->scratch, n, streams, positions, d->qkv,
+                                   3 * h, d->att, st)) != cudaSuccess)
+            break;
+        to_bf16<<<cvt_blocks, 256, 0, st>>>(d->att, d->xb, (size_t)n * h);
+        if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, true, st))) break;
+        if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, d->xb, n, h, st)) != cudaSuccess) break;
+        if ((rc = gemm(d, n, f, h, d->xb, W.w_in, W.b_in, d->h1, false, st))) break;
+        gelu_tanh_to_bf16<<<cvt_blocks, 256, 0, st>>>(d->h1, d->xb, (size_t)n * f);
+        if ((rc = gemm(d, n, h, f, d->xb, W.w_out, W.b_out, hidden, true, st))) break;
+        e = cudaGetLastError();
+    }
+    if (rc == MB_OK && e == cudaSuccess) e = layernorm<float>(hidden, d->lnf_w, d->lnf_b, hidden, n, h, st);
+    if (prev >= 0 && prev != c->cfg.device) cudaSetDevice(prev);
+    if (rc) return rc;
+    if (e != cudaSuccess) return dfail(d, MB_ERR_CUDA, std::string("decoder: ") + cudaGetErrorString(e));
+    return MB_OK;
+}
+
+}  // extern "C"
