@@ -45,6 +45,10 @@ CONFIGS = {
     3: dict(workload="config3: causal prefill, 32 streams x (188 prompt + 256 text = 444 positions) x 12 layers "
                      "x 12 heads x 64, fp16 ring storage (capacity 2048), fp32 accumulation, q/k/v ~ N(0, 0.5)",
             streams=32, layers=12, capacity=2048, dtype="f16", job_steps=None, steps=20, warmup=3, rows=444),
+    4: dict(workload="config4: full 0.1B-class decoder decode step, 256 streams/GPU x 12 layers (hidden 768, 12 "
+                     "heads x 64, FFN 3072), bf16 weights ~N(0,0.02) and bf16 ring capacity 2048, positions U[444,2048) "
+                     "from seed 0; LN1 -> QKV GEMM -> append+RoPE+attention -> proj GEMM -> LN2 -> FFN per layer",
+            streams=256, layers=12, capacity=2048, dtype="bf16", job_steps=None, steps=100, warmup=5, ffn=3072),
     5: dict(workload="config5: long-text serving, 512 streams/GPU x 12 layers x 12 heads x 64, bf16 ring capacity "
                      "4096, live lengths U[1,4096] from seed 0, consecutive appends",
             streams=512, layers=12, capacity=4096, dtype="bf16", job_steps=None, steps=200, warmup=5),
@@ -59,6 +63,14 @@ def window_bytes(L, esize, layers=12):
     """Algorithmic bytes of one stream-frame (all layers) at live window L:
     K,V window read 2*L*768*E + K,V append 2*768*E + q,k,v in and ctx out 4*768*4."""
     return layers * (2 * L * HID * esize + 2 * HID * esize + 4 * HID * 4)
+
+
+# DRAM read + write per launch over the algorithmic bytes, from the full ncu capture
+# of the fp32 decode kernel (32 streams, full 512-slot windows: 101.05 MB read +
+# 4.0 MB written for 101.25 MB algorithmic; profiles/decode_kernel_f32_config2.md).
+# Traffic grows with the streams and the window, so a launch's traffic is its
+# algorithmic bytes times this ratio.
+DECODE_TRAFFIC_RATIO = {"f32": (101.05 + 4.0) / 101.25}
 
 
 def peaks():
@@ -263,8 +275,12 @@ def run_ours(args, cfg, rank, world, device):
     value = world * n * K / (ms_max / 1e3)
     peak, peak_kind = peaks()
     achieved = algo_bytes / (ms / 1e3) / 1e9  # this rank's algorithmic bytes over its own device time
+    ratio = DECODE_TRAFFIC_RATIO.get(cfg["dtype"])
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None,
+                "frac": round(achieved / peak, 4),
+                "traffic": round(algo_bytes / launches * ratio) if ratio else None,
+                "traffic_source": "ncu capture of a smaller case scaled by algorithmic bytes per launch "
+                                  "(profiles/decode_kernel_f32_config2.md)" if ratio else None,
                 "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
                 "kernel": "decode_kernel<fused append+RoPE+split-K attention>",
@@ -363,6 +379,150 @@ def run_prefill(args, cfg, rank, world, device):
         "gpu_launches": 2 * L * args.steps, "clocks": clk, "e2e": None,
     }
     return result, ring
+
+
+# ------------------------------------------------------------------ config 4: the full decoder step
+def decoder_weights(layers, h, ffn, seed=0):
+    """N(0, 0.02) weights in the published graph's order, LayerNorm gains 1."""
+    from mockbird_b200.engine import Decoder
+
+    per = 2 * h + h * 3 * h + 3 * h + h * h + h + 2 * h + h * ffn + ffn + ffn * h + h
+    w = (np.random.default_rng(seed).standard_normal(Decoder.weight_count(layers, h, ffn)) * 0.02).astype(np.float32)
+    for l in range(layers):
+        b = l * per
+        w[b:b + h] = 1.0
+        w[b + 2 * h + 3 * h * h + 3 * h + h * h + h: b + 2 * h + 3 * h * h + 3 * h + h * h + 2 * h] = 1.0
+    w[layers * per: layers * per + h] = 1.0
+    return w
+
+
+def config4_positions(n, capacity, seed=0):
+    return np.random.default_rng(seed).integers(444, capacity, size=n)
+
+
+def run_decoder(args, cfg, rank, world, device):
+    import torch
+
+    from mockbird_b200 import KvRing
+    from mockbird_b200.engine import Decoder
+    from mockbird_b200.scheduler import max_over_ranks
+
+    n, L, C, F = cfg["streams"], cfg["layers"], cfg["capacity"], cfg["ffn"]
+    ring = KvRing(layers=L, capacity=C, streams=n, dtype=cfg["dtype"], wrap=True, device=device.index)
+    dec = Decoder(ring, decoder_weights(L, HID, F), F)
+    g = torch.Generator(device=device)
+    g.manual_seed(77 + rank)
+    pos0 = config4_positions(n * world, C)[rank * n:(rank + 1) * n].astype(np.int64)
+    for i, p0 in enumerate(pos0):  # positions 0..p0-1 already in every layer's ring
+        kv = torch.randn(2, H, int(p0), HD, generator=g, device=device).to(ring.torch_dtype)
+        for layer in range(L):
+            ring.ring_write(layer, i, 0, kv[0], kv[1])
+    torch.cuda.synchronize(device)
+    K, W = args.steps, args.warmup
+    pos_dev = torch.from_numpy(np.stack([(pos0 + t).astype(np.int32) for t in range(W + 2 * K)])).to(device)
+    streams = torch.arange(n, dtype=torch.int32, device=device)
+    rows = torch.randn(8, n, HID, generator=g, device=device)  # embedded rows, rotating
+    hidden = torch.empty(n, HID, device=device)
+    for t in range(W):
+        hidden.copy_(rows[t % 8])
+        dec.step(streams, pos_dev[t], hidden)
+    ring.sync()
+    dist = _dist()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for t in range(W, W + K):
+        hidden.copy_(rows[t % 8])
+        dec.step(streams, pos_dev[t], hidden)
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ring.sync()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, device if dist else None)
+    # e2e: embedded rows from pinned host memory in, ln_f rows out, every step
+    host_in = torch.empty(2, n, HID).pin_memory()
+    host_in.copy_(rows[:2].cpu())
+    host_out = torch.empty(n, HID).pin_memory()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for t in range(W + K, W + 2 * K):
+        hidden.copy_(host_in[t % 2], non_blocking=True)
+        dec.step(streams, pos_dev[t], hidden)
+        host_out.copy_(hidden, non_blocking=True)
+        stream.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, device if dist else None)
+    es = _esize(cfg["dtype"])
+    live = np.minimum(pos0[None, :] + np.arange(W, W + K)[:, None] + 1, C)
+    kv_bytes = float((2 * live * HID * es + 2 * HID * es).sum()) * L
+    w_bytes = L * (HID * 3 * HID + HID * HID + 2 * HID * F) * 2.0 * K
+    act_bytes = L * n * K * 4.0 * (4 * HID)
+    algo = kv_bytes + w_bytes + act_bytes
+    peak, peak_kind = peaks()
+    achieved = algo / (ms / 1e3) / 1e9
+    value = world * n * K / (ms_max / 1e3)
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "frames/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_max / K, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1) rows and K/V, N(0,0.02) weights)",
+        "config": {"workload": cfg["workload"], "streams_per_gpu": n, "global_streams": n * world, "layers": L,
+                   "capacity": C, "ffn": F, "parallelism": f"stream-sharded x{world} (no collective on the decode path)",
+                   "l2": f"inputs larger than L2: ~{kv_bytes / K / 1e9:.1f} GB of K/V windows per step",
+                   "value_per_gpu": round(value / world, 1),
+                   "gemms": "cuBLASLt (library GEMMs); LayerNorm, GELU and the attention are this library's kernels"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                     "kernel": "whole decoder step (decode_kernel dominates: K/V windows are ~98% of the bytes)",
+                     "timing": "CUDA events over the timed region; algorithmic bytes = K/V windows + appends + "
+                               "weights + activations"},
+        "e2e": {"value": round(world * n * K / e2e_s, 1), "unit": "frames/s",
+                "h2d_bytes_per_step": n * HID * 4, "d2h_bytes_per_step": n * HID * 4,
+                "api": "mb_decoder_step (C ABI) with the embedded rows copied from pinned host memory and the ln_f "
+                       "rows read back every step"},
+        "gpu_launches": K * (L * 5 + 1),
+        "clocks": clk,
+    }
+    result["gpu_launches_note"] = "5 of this library's kernels per layer (2 LayerNorm, attention, 2 conversions) + ln_f; the 4 GEMMs per layer are cuBLASLt"
+    dec.dispose()
+    return result, ring
+
+
+def run_cpu_decoder(cfg, steps, sample_streams=2, budget_s=None):
+    """The reference's decode step (ref-decode.mjs decodeStep restated by the oracle) on the host cores."""
+    import oracle
+
+    n, L, C, F = sample_streams, cfg["layers"], cfg["capacity"], cfg["ffn"]
+    ring = oracle.Ring(layers=L, streams=n, heads=H, capacity=C, dtype=cfg["dtype"], wrap=True, max_position=4096)
+    w = decoder_weights(L, HID, F)
+    rng = np.random.default_rng(5)
+    pos0 = config4_positions(n, C)
+    kvv = ring.kv_view()
+    for s_ in range(n):
+        p0 = int(pos0[s_])
+        rows = rng.standard_normal((2, H, p0, HD)).astype(np.float32)
+        kvv[:, s_, :, :, :p0] = ((rows.view(np.uint32) >> 16).astype(np.uint16))[None]
+        ring.slot_pos[:, s_, :p0] = np.arange(p0)
+    x = rng.standard_normal((n, HID)).astype(np.float32)
+    t0 = time.perf_counter()
+    done = 0
+    for t in range(steps):
+        oracle.decoder_step(ring, w, F, np.arange(n), (pos0 + t).astype(np.int32), x)
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"value": round(n * done / dt, 3), "unit": "frames/s", "cores": cores, "kind": "port",
+            "sample": f"{n} streams x {done} decode steps of the 12-layer decoder (oracle restatement of "
+                      f"ref-decode.mjs decodeStep: numpy GEMMs, C attention mirror), {dt:.1f} s"}
 
 
 # ------------------------------------------------------------------ CPU reference (oracle port)
@@ -483,6 +643,9 @@ def main():
         if args.config == 3:
             base = run_cpu_prefill(cfg, args.steps, 1, sample_streams=1, budget_s=120.0)
             metric, unit = "causal prefill attention TFLOP/s (config 3; RoPE+cache write and attention, all 12 layers)", "TFLOP/s"
+        elif args.config == 4:
+            base = run_cpu_decoder(cfg, args.steps, sample_streams=2, budget_s=120.0)
+            metric, unit = METRIC, "frames/s"
         else:
             base = run_cpu(cfg, args.steps, args.warmup, sample_streams=4)
             metric, unit = METRIC, "frames/s"
@@ -506,6 +669,8 @@ def main():
         init_group("nccl", timeout_s=300, device=device)
     if args.config == 3:
         result, ring = run_prefill(args, cfg, rank, world, device)
+    elif args.config == 4:
+        result, ring = run_decoder(args, cfg, rank, world, device)
     else:
         result, ring = run_ours(args, cfg, rank, world, device)
     dist = _dist()
@@ -515,6 +680,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu and cfg.get("start") is None:
         if args.config == 3:
             result["cpu_baseline"] = run_cpu_prefill(cfg, 1, 0, sample_streams=1, budget_s=30.0)
+        elif args.config == 4:
+            result["cpu_baseline"] = run_cpu_decoder(cfg, 3, sample_streams=2, budget_s=30.0)
         else:
             result["cpu_baseline"] = run_cpu(cfg, min(args.steps, cfg["job_steps"] or args.steps), 2,
                                              sample_streams=4, budget_s=30.0)

@@ -253,3 +253,47 @@ class KvRing:
         except Exception:
             pass
 
+
+
+class Decoder:
+    """The global decode step around the ring, mirroring
+    DecodeRunner.globalStep (decode.ts:712-775) without the embedding: every layer
+    LN1 -> QKV -> append + RoPE + attention -> c_proj + residual -> LN2 -> fc_in ->
+    GELU(tanh) -> fc_out + residual, then ln_f, for n streams at once.
+
+    `weights`: one fp32 array in the published graph's order (see
+    mb_decoder_weight_count / mb_decoder_create in include/mockbird_kv.h)."""
+
+    def __init__(self, ring: KvRing, weights: np.ndarray, ffn: int = 3072):
+        self.ring, self.lib, self.ffn = ring, ring.lib, ffn
+        w = np.ascontiguousarray(weights, np.float32)
+        want = self.lib.mb_decoder_weight_count(ring.ctx, ffn)
+        if w.size != want:
+            raise ValueError(f"decoder weights: {w.size} values, expected {want}")
+        handle = ctypes.c_void_p()
+        ring._check(self.lib.mb_decoder_create(ring.ctx, ffn, _ptr(w), w.size, ctypes.byref(handle)))
+        self.handle = handle
+
+    @staticmethod
+    def weight_count(layers: int, hidden: int, ffn: int) -> int:
+        h, f = hidden, ffn
+        return layers * (2 * h + h * 3 * h + 3 * h + h * h + h + 2 * h + h * f + f + f * h + h) + 2 * h
+
+    def step(self, streams, positions, hidden: torch.Tensor, stream=None) -> torch.Tensor:
+        """hidden [n][H*64] fp32 (device): embedded rows in, ln_f output out (in place)."""
+        s, p, x = self.ring._ids(streams), self.ring._ids(positions), self.ring._dev(hidden)
+        rc = self.lib.mb_decoder_step(self.handle, s.numel(), _ptr(s), _ptr(p), _ptr(x), self.ring._stream(stream))
+        if rc:
+            raise MockbirdError(rc, self.lib.mb_last_error(self.ring.ctx).decode())
+        return hidden
+
+    def dispose(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.mb_decoder_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.dispose()
+        except Exception:
+            pass

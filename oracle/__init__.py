@@ -195,3 +195,45 @@ def xorshift32_stream(seed: int = 0x2F6E2B1):
         return out
 
     return rnd
+
+
+def decoder_step(ring: "Ring", weights: np.ndarray, ffn: int, streams, positions, hidden: np.ndarray) -> np.ndarray:
+    """The global decode step of tools/onnx-probe/ref-decode.mjs:207-235 (decodeStep)
+    for several streams, with the rounding points of a bf16 GEMM path: matrices and
+    GEMM inputs rounded to bf16, everything else fp32.  LayerNorm eps 1e-5
+    (kernels-decode.ts:168-200), GELU tanh (kernels-decode.ts:373-390), attention
+    through the ring's fp32 mirror.  hidden [n][H*64] in (embedded rows), ln_f out."""
+    h = ring.heads * HD
+    w = np.asarray(weights, np.float32)
+    off = [0]
+
+    def take(count, shape=None, mat=False):
+        a = w[off[0]:off[0] + count]
+        off[0] += count
+        a = round_to("bf16", a) if mat else a
+        return a.reshape(shape) if shape else a
+
+    def ln(x, g, b):
+        mean = x.mean(-1, keepdims=True, dtype=np.float64).astype(np.float32)
+        d = x - mean
+        var = (d.astype(np.float64) ** 2).mean(-1, keepdims=True).astype(np.float32)
+        return (d / np.sqrt(var + np.float32(1e-5)) * g + b).astype(np.float32)
+
+    def gemm(x, W, b):  # bf16 inputs, fp32 accumulation
+        return (round_to("bf16", x).astype(np.float64) @ W.astype(np.float64) + b).astype(np.float32)
+
+    x = np.array(hidden, np.float32, copy=True)
+    for layer in range(ring.g.layers):
+        ln1w, ln1b = take(h), take(h)
+        wa, ba = take(h * 3 * h, (h, 3 * h), True), take(3 * h)
+        wp, bp = take(h * h, (h, h), True), take(h)
+        ln2w, ln2b = take(h), take(h)
+        wi, bi = take(h * ffn, (h, ffn), True), take(ffn)
+        wo, bo = take(ffn * h, (ffn, h), True), take(h)
+        qkv = gemm(ln(x, ln1w, ln1b), wa, ba)
+        ctx, _ = ring.append_attend(layer, streams, positions, qkv)
+        x = x + gemm(ctx, wp, bp)
+        a = gemm(ln(x, ln2w, ln2b), wi, bi)
+        a = (0.5 * a * (1 + np.tanh(0.7978845608028654 * (a + 0.044715 * a * a * a)))).astype(np.float32)
+        x = x + gemm(a, wo, bo)
+    return ln(x, take(h), take(h))

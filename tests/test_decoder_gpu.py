@@ -1,0 +1,58 @@
+"""GPU parity of the decode step around the path (BASELINE config 4 shape):
+LayerNorm, QKV/c_proj/fc_in/fc_out GEMMs (bf16 weights), GELU(tanh), residuals,
+ln_f, and the fused append + attention, against the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import max_err
+from mockbird_b200 import KvRing, MockbirdError
+from mockbird_b200.engine import Decoder
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+TOL = 2e-2  # bf16 weights and GEMM inputs, 12-head attention over bf16 storage, accumulated over the layers
+
+
+def _weights(layers, h, ffn, seed):
+    n = Decoder.weight_count(layers, h, ffn)
+    w = (np.random.default_rng(seed).standard_normal(n) * 0.02).astype(np.float32)
+    # LayerNorm gains at 1 (the published model's LN scales are all ones) and biases small
+    off = 0
+    per = 2 * h + h * 3 * h + 3 * h + h * h + h + 2 * h + h * ffn + ffn + ffn * h + h
+    for l in range(layers):
+        base = l * per
+        w[base:base + h] = 1.0
+        w[base + 2 * h + h * 3 * h + 3 * h + h * h + h: base + 2 * h + h * 3 * h + 3 * h + h * h + 2 * h] = 1.0
+    w[layers * per: layers * per + h] = 1.0
+    return w
+
+
+@pytest.mark.parametrize("dtype,layers,ffn", [("bf16", 2, 3072), ("f32", 1, 1024)])
+def test_decoder_step_matches_oracle(dtype, layers, ffn):
+    h, S, C = 768, 5, 256
+    w = _weights(layers, h, ffn, seed=layers)
+    ring = KvRing(layers=layers, streams=S, capacity=C, dtype=dtype, wrap=True)
+    dec = Decoder(ring, w, ffn)
+    orc = oracle.Ring(layers=layers, streams=S, heads=12, capacity=C, dtype=dtype, wrap=True)
+    rng = np.random.default_rng(3)
+    order = [4, 1, 0, 3]
+    worst = 0.0
+    for step in range(40):
+        x = rng.standard_normal((len(order), h)).astype(np.float32)
+        pos = [step + 7 * i for i in range(len(order))]  # different positions per stream
+        got = dec.step(order, pos, torch.from_numpy(x).to(DEV))
+        ref = oracle.decoder_step(orc, w, ffn, order, pos, x)
+        worst = max(worst, max_err(got, ref))
+    ring.sync()
+    assert worst < TOL, worst
+
+
+def test_decoder_rejects_bad_weights():
+    ring = KvRing(layers=1, streams=2, capacity=64, dtype="bf16", wrap=True)
+    with pytest.raises(ValueError):
+        Decoder(ring, np.zeros(10, np.float32), 3072)
+    dec = Decoder(ring, _weights(1, 768, 1024, 0), 1024)
+    with pytest.raises(MockbirdError):
+        dec.step([0, 1, 0], [0, 0, 0], torch.zeros(3, 768, device=DEV))  # 3 items > max_batch 2
