@@ -103,7 +103,12 @@ struct mb_decoder {
     cublasLtHandle_t lt = nullptr;
     void* workspace = nullptr;
     size_t ws_bytes = 32u << 20;
-    std::map<std::tuple<int, int, int, int>, cublasLtMatmulAlgo_t> algos;
+    struct Plan {  // one GEMM shape: descriptors and the chosen algorithm, built once
+        cublasLtMatmulDesc_t op = nullptr;
+        cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
+        cublasLtMatmulAlgo_t algo{};
+    };
+    std::map<std::tuple<int, int, int>, Plan> plans;
 };
 
 namespace {
@@ -117,44 +122,50 @@ int dfail(mb_decoder* d, int code, const std::string& msg) {
 int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const float* bias, float* y,
          bool accumulate, cudaStream_t st) {
     // column-major view: y^T [N x M] = W^T [N x K] * x^T [K x M]
-    cublasLtMatmulDesc_t op = nullptr;
-    cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
-    cublasStatus_t s = cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F);
-    cublasLtEpilogue_t epi = CUBLASLT_EPILOGUE_BIAS;
-    cudaDataType_t bias_t = CUDA_R_32F;
-    if (s == CUBLAS_STATUS_SUCCESS)
-        s = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof epi);
-    if (s == CUBLAS_STATUS_SUCCESS)
-        s = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
-    if (s == CUBLAS_STATUS_SUCCESS)
-        s = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bias_t, sizeof bias_t);
-    if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&a, CUDA_R_16BF, N, K, N);
-    if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&b, CUDA_R_16BF, K, M, K);
-    if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&c, CUDA_R_32F, N, M, N);
-    const auto key = std::make_tuple(M, N, K, accumulate ? 1 : 0);
-    auto it = d->algos.find(key);
-    if (s == CUBLAS_STATUS_SUCCESS && it == d->algos.end()) {
+    cublasStatus_t s = CUBLAS_STATUS_SUCCESS;
+    const auto key = std::make_tuple(M, N, K);
+    auto it = d->plans.find(key);
+    if (it == d->plans.end()) {
+        mb_decoder::Plan p;
+        cublasLtEpilogue_t epi = CUBLASLT_EPILOGUE_BIAS;
+        cudaDataType_t bias_t = CUDA_R_32F;
+        s = cublasLtMatmulDescCreate(&p.op, CUBLAS_COMPUTE_32F, CUDA_R_32F);
+        if (s == CUBLAS_STATUS_SUCCESS)
+            s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof epi);
+        if (s == CUBLAS_STATUS_SUCCESS)
+            s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bias_t, sizeof bias_t);
+        if (s == CUBLAS_STATUS_SUCCESS)
+            s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
+        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.a, CUDA_R_16BF, N, K, N);
+        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.b, CUDA_R_16BF, K, M, K);
+        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.c, CUDA_R_32F, N, M, N);
         cublasLtMatmulPreference_t pref = nullptr;
-        s = cublasLtMatmulPreferenceCreate(&pref);
+        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatmulPreferenceCreate(&pref);
         if (s == CUBLAS_STATUS_SUCCESS)
             s = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &d->ws_bytes,
                                                      sizeof d->ws_bytes);
         cublasLtMatmulHeuristicResult_t res = {};
         int found = 0;
         if (s == CUBLAS_STATUS_SUCCESS)
-            s = cublasLtMatmulAlgoGetHeuristic(d->lt, op, a, b, c, c, pref, 1, &res, &found);
+            s = cublasLtMatmulAlgoGetHeuristic(d->lt, p.op, p.a, p.b, p.c, p.c, pref, 1, &res, &found);
         if (pref) cublasLtMatmulPreferenceDestroy(pref);
         if (s == CUBLAS_STATUS_SUCCESS && found == 0) s = CUBLAS_STATUS_NOT_SUPPORTED;
-        if (s == CUBLAS_STATUS_SUCCESS) it = d->algos.emplace(key, res.algo).first;
+        if (s != CUBLAS_STATUS_SUCCESS) {
+            if (p.c) cublasLtMatrixLayoutDestroy(p.c);
+            if (p.b) cublasLtMatrixLayoutDestroy(p.b);
+            if (p.a) cublasLtMatrixLayoutDestroy(p.a);
+            if (p.op) cublasLtMatmulDescDestroy(p.op);
+            return dfail(d, MB_ERR_CUDA, std::string("cuBLASLt setup failed: ") + cublasLtGetStatusString(s));
+        }
+        p.algo = res.algo;
+        it = d->plans.emplace(key, p).first;
     }
+    mb_decoder::Plan& p = it->second;
+    s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
     const float alpha = 1.f, beta = accumulate ? 1.f : 0.f;
     if (s == CUBLAS_STATUS_SUCCESS)
-        s = cublasLtMatmul(d->lt, op, &alpha, W, a, x, b, &beta, y, c, y, c, &it->second, d->workspace, d->ws_bytes,
-                           st);
-    if (c) cublasLtMatrixLayoutDestroy(c);
-    if (b) cublasLtMatrixLayoutDestroy(b);
-    if (a) cublasLtMatrixLayoutDestroy(a);
-    if (op) cublasLtMatmulDescDestroy(op);
+        s = cublasLtMatmul(d->lt, p.op, &alpha, W, p.a, x, p.b, &beta, y, p.c, y, p.c, &p.algo, d->workspace,
+                           d->ws_bytes, st);
     if (s != CUBLAS_STATUS_SUCCESS)
         return dfail(d, MB_ERR_CUDA, std::string("cuBLASLt matmul failed: ") + cublasLtGetStatusString(s));
     return MB_OK;
@@ -191,6 +202,12 @@ MB_API int mb_decoder_destroy(mb_decoder* d) {
     void* ptrs[] = {d->wmem, d->xb, d->qkv, d->att, d->h1, d->workspace};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    for (auto& kv : d->plans) {
+        cublasLtMatrixLayoutDestroy(kv.second.c);
+        cublasLtMatrixLayoutDestroy(kv.second.b);
+        cublasLtMatrixLayoutDestroy(kv.second.a);
+        cublasLtMatmulDescDestroy(kv.second.op);
+    }
     if (d->lt) cublasLtDestroy(d->lt);
     if (prev >= 0) cudaSetDevice(prev);
     delete d;

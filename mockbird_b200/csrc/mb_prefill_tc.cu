@@ -14,7 +14,9 @@
 //   O = O*corr + O_j in registers
 // Q, K, V arrive by 3-D TMA tile loads (128-byte swizzle, zero fill past the last
 // row, no multicast).  K of tile j+1 is fetched as soon as the QK^T MMA of tile j
-// has consumed K, V of tile j+1 as soon as the PV MMA has consumed V.  80 KB of
+// has consumed K, V of tile j+1 as soon as the PV MMA has consumed V.  (Issuing
+// S_{j+1} = Q K_{j+1}^T ahead, into a second TMEM buffer, was measured slower on
+// B200: it queues in front of PV_j on the tensor pipe.)  80 KB of
 // shared memory and 256 TMEM columns per CTA: two CTAs share an SM.  Every wait is
 // bounded; a CTA that gives up flags MB_ERR_TIMEOUT, waits (bounded) for its
 // copies and MMAs in flight, and frees its TMEM.
@@ -145,8 +147,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
         // ---- this thread's 64 scores (keys k0 + 64*half ..), kept in registers
         float sv[64];
-        tmem_ld32(lane_addr + S_COL + 64 * half, sv);
-        tmem_ld32(lane_addr + S_COL + 64 * half + 32, sv + 32);
+        tmem_ld64(lane_addr + S_COL + 64 * half, sv);
         const int kb = k0 + 64 * half;
         const bool full = (k0 + BN <= q0) && (k0 + BN <= rows);  // no key of the tile is masked
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
