@@ -52,7 +52,13 @@ CONFIGS = {
     5: dict(workload="config5: long-text serving, 512 streams/GPU x 12 layers x 12 heads x 64, bf16 ring capacity "
                      "4096, live lengths U[1,4096] from seed 0, consecutive appends",
             streams=512, layers=12, capacity=4096, dtype="bf16", job_steps=None, steps=200, warmup=5),
+    6: dict(workload="local head: 256 streams/GPU, one frame = 17 sequential steps (one 768-wide layer, FFN 3072, "
+                     "over a 17-slot ring; ln_f; 16 audio heads 768x1024 with greedy argmax and repetition penalty "
+                     "1.2), bf16 weights ~N(0,0.02), tokens kept on the device",
+            streams=256, layers=1, capacity=17, dtype="bf16", job_steps=None, steps=100, warmup=5, ffn=3072,
+            codes=1024, channels=16),
 }
+LOCAL_METRIC = "local-head frames/sec/GPU (17 steps: layer + ln_f + audio head + penalised argmax)"
 
 
 def _esize(dtype):
@@ -79,6 +85,15 @@ def peaks():
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the measured burst figure, else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
 
 
 # ------------------------------------------------------------------ clocks
@@ -356,11 +371,7 @@ def run_prefill(args, cfg, rank, world, device):
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, device if dist else None)
     flops = prefill_flops(S, n, L) * args.steps
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            tpeak, tkind = float(json.load(f)["bf16_tflops"]), "measured"
-    except Exception:
-        tpeak, tkind = 1590.0, "fallback"
+    tpeak, tkind = tensor_peak()
     achieved = flops / (ms / 1e3) / 1e12
     result = {
         "metric": "causal prefill attention TFLOP/s (config 3; RoPE+cache write and attention, all 12 layers)",
@@ -525,6 +536,154 @@ def run_cpu_decoder(cfg, steps, sample_streams=2, budget_s=None):
                       f"ref-decode.mjs decodeStep: numpy GEMMs, C attention mirror), {dt:.1f} s"}
 
 
+# ------------------------------------------------------------------ the local 17-step head
+def local_weights(h, ffn, codes, channels, seed=0):
+    """N(0, 0.02) weights in mb_local_head_create's order, LayerNorm gains 1,
+    N(0,1) embedding rows, text-head columns N(0, 1/h)."""
+    from mockbird_b200.engine import LocalHead
+
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal(LocalHead.weight_count(h, ffn, codes, channels)) * 0.02).astype(np.float32)
+    per = 2 * h + h * 3 * h + 3 * h + h * h + h + 2 * h + h * ffn + ffn + ffn * h + h
+    w[0:h] = 1.0
+    w[2 * h + 3 * h * h + 3 * h + h * h + h: 2 * h + 3 * h * h + 3 * h + h * h + 2 * h] = 1.0
+    w[per:per + h] = 1.0
+    off = per + 2 * h
+    w[off:off + h] = rng.standard_normal(h)
+    w[off + h:off + 3 * h] = rng.standard_normal(2 * h) / np.sqrt(h)
+    off += 3 * h
+    m = (channels - 1) * codes * h
+    w[off:off + m] = rng.standard_normal(m)
+    return w
+
+
+def local_algo(n, h, ffn, codes, channels):
+    """Algorithmic FLOPs and bytes of one frame for n streams: the layer's four
+    GEMMs at every step, the audio-head GEMM at every step but the first; bytes =
+    the bf16 weights each step reads + the embedding rows + hidden in / tokens out."""
+    steps = channels + 1
+    layer_params = 4 * h * h + 2 * h * ffn
+    head_params = h * codes
+    flops = 2.0 * n * (steps * layer_params + channels * head_params)
+    weight_bytes = 2.0 * (steps * layer_params + channels * head_params)
+    act_bytes = 4.0 * n * ((channels - 1) * h + h + channels + 1)
+    return flops, weight_bytes + act_bytes
+
+
+def run_local(args, cfg, rank, world, device):
+    import torch
+
+    from mockbird_b200 import KvRing, LocalHead
+    from mockbird_b200.scheduler import max_over_ranks
+
+    n, F, codes, ch = cfg["streams"], cfg["ffn"], cfg["codes"], cfg["channels"]
+    ring = KvRing(layers=1, capacity=ch + 1, streams=n, dtype=cfg["dtype"], wrap=False, max_position=ch + 1,
+                  device=device.index)
+    head = LocalHead(ring, local_weights(HID, F, codes, ch), F, codes, ch, 1.2)
+    g = torch.Generator(device=device)
+    g.manual_seed(91 + rank)
+    hidden = torch.randn(8, n, HID, generator=g, device=device)  # global hidden states, rotating
+    streams = torch.arange(n, dtype=torch.int32, device=device)
+    K, W = args.steps, args.warmup
+    for t in range(W):
+        head.frame(streams, hidden[t % 8])
+    ring.sync()
+    dist = _dist()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for t in range(W, W + K):
+        tok, cont, _ = head.frame(streams, hidden[t % 8])
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    ring.sync()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, device if dist else None)
+    # e2e: the hidden states from pinned host memory in, tokens and the stop flags out, every frame
+    host_in = torch.empty(2, n, HID).pin_memory()
+    host_in.copy_(hidden[:2].cpu())
+    host_tok = torch.empty(n, ch, dtype=torch.int32).pin_memory()
+    host_cont = torch.empty(n, dtype=torch.int32).pin_memory()
+    x = torch.empty(n, HID, device=device)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for t in range(K):
+        x.copy_(host_in[t % 2], non_blocking=True)
+        tok, cont, _ = head.frame(streams, x)
+        host_tok.copy_(tok, non_blocking=True)
+        host_cont.copy_(cont, non_blocking=True)
+        stream.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, device if dist else None)
+    flops, byts = local_algo(n, HID, F, codes, ch)
+    tpeak, tkind = tensor_peak()
+    hpeak, hkind = peaks()
+    t_s = ms / 1e3 / K
+    value = world * n * K / (ms_max / 1e3)
+    graph = os.environ.get("MOCKBIRD_LOCAL_GRAPH", "1") != "0"
+    result = {
+        "metric": LOCAL_METRIC, "value": round(value, 1), "unit": "frames/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": round(ms_max / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) weights)",
+        "config": {"workload": cfg["workload"], "streams_per_gpu": n, "global_streams": n * world,
+                   "ffn": F, "codes": codes, "channels": ch,
+                   "parallelism": f"stream-sharded x{world} (no collective)",
+                   "l2": "weights (15.7 MB per step) are re-read every step and may stay in L2; the bound is "
+                         "the tensor pipe at this batch", "cuda_graph": graph,
+                   "value_per_gpu": round(value / world, 1),
+                   "gemms": "cuBLASLt (library GEMMs); embedding, LayerNorm, GELU, attention, text-head decision "
+                            "and argmax are this library's kernels"},
+        "roofline": {"bound": "tensor", "achieved": round(flops / t_s / 1e12, 2), "peak": tpeak,
+                     "unit": "TFLOP/s", "frac": round(flops / t_s / 1e12 / tpeak, 4), "traffic": None,
+                     "peak_source": f"{tkind} bf16_tflops (burst)",
+                     "hbm_achieved_gbs": round(byts / t_s / 1e9, 1), "hbm_peak": hpeak,
+                     "timing": "CUDA events over the timed frames; algorithmic FLOPs = the layer's GEMMs at 17 "
+                               "steps + the audio-head GEMMs at 16 steps"},
+        "e2e": {"value": round(world * n * K / e2e_s, 1), "unit": "frames/s",
+                "h2d_bytes_per_step": n * HID * 4, "d2h_bytes_per_step": n * (ch + 1) * 4,
+                "api": "mb_local_head_frame (C ABI) with the hidden states copied from pinned host memory and the "
+                       "tokens and stop flags read back every frame"},
+        "gpu_launches": K * ((ch + 1) * 7 + ch + 1),
+        "gpu_launches_note": "per step: embedding, 2 LayerNorms, attention, 2 conversions, ln_f, and the text "
+                             "decision (step 0) or the argmax (steps 1-16); the 5 GEMMs per step are cuBLASLt",
+        "clocks": clk,
+    }
+    head.dispose()
+    return result, ring
+
+
+def run_cpu_local(cfg, frames, sample_streams=2, budget_s=None):
+    """The reference's local head (ref-decode.mjs localStep/argmaxPenalty restated by the oracle) on the host."""
+    import oracle
+
+    n, F, codes, ch = sample_streams, cfg["ffn"], cfg["codes"], cfg["channels"]
+    ring = oracle.Ring(layers=1, streams=n, heads=H, capacity=ch + 1, dtype=cfg["dtype"], wrap=False,
+                       max_position=ch + 1)
+    w = local_weights(HID, F, codes, ch)
+    seen = np.zeros((n, ch, codes // 32), np.uint32)
+    x = np.random.default_rng(6).standard_normal((n, HID)).astype(np.float32)
+    t0 = time.perf_counter()
+    done = 0
+    for _ in range(frames):
+        oracle.local_frame(ring, w, F, codes, ch, 1.2, np.arange(n), x, seen)
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"value": round(n * done / dt, 3), "unit": "frames/s", "cores": cores, "kind": "port",
+            "sample": f"{n} streams x {done} local-head frames (oracle restatement of ref-decode.mjs localStep + "
+                      f"argmaxPenalty: numpy GEMMs, C attention mirror), {dt:.1f} s"}
+
+
 # ------------------------------------------------------------------ CPU reference (oracle port)
 def run_cpu(cfg, steps, warmup, sample_streams, budget_s=None):
     """The reference algorithm (oracle mirror of the WGSL kernels) on the host cores:
@@ -611,7 +770,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
-    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
+                    help="2-5: BASELINE configs; 6: the local 17-step head")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -646,6 +806,9 @@ def main():
         elif args.config == 4:
             base = run_cpu_decoder(cfg, args.steps, sample_streams=2, budget_s=120.0)
             metric, unit = METRIC, "frames/s"
+        elif args.config == 6:
+            base = run_cpu_local(cfg, args.steps, sample_streams=2, budget_s=120.0)
+            metric, unit = LOCAL_METRIC, "frames/s"
         else:
             base = run_cpu(cfg, args.steps, args.warmup, sample_streams=4)
             metric, unit = METRIC, "frames/s"
@@ -671,6 +834,8 @@ def main():
         result, ring = run_prefill(args, cfg, rank, world, device)
     elif args.config == 4:
         result, ring = run_decoder(args, cfg, rank, world, device)
+    elif args.config == 6:
+        result, ring = run_local(args, cfg, rank, world, device)
     else:
         result, ring = run_ours(args, cfg, rank, world, device)
     dist = _dist()
@@ -682,6 +847,8 @@ def main():
             result["cpu_baseline"] = run_cpu_prefill(cfg, 1, 0, sample_streams=1, budget_s=30.0)
         elif args.config == 4:
             result["cpu_baseline"] = run_cpu_decoder(cfg, 3, sample_streams=2, budget_s=30.0)
+        elif args.config == 6:
+            result["cpu_baseline"] = run_cpu_local(cfg, 3, sample_streams=2, budget_s=30.0)
         else:
             result["cpu_baseline"] = run_cpu(cfg, min(args.steps, cfg["job_steps"] or args.steps), 2,
                                              sample_streams=4, budget_s=30.0)

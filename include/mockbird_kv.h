@@ -205,6 +205,72 @@ MB_API int mb_decoder_step(mb_decoder* dec, int32_t n, const int32_t* streams, c
                            float* hidden, void* cuda_stream);
 
 /* ---------------------------------------------------------------------------
+ * Local head: the 17 sequential steps that turn one global hidden state into one
+ * frame of 16 audio codes, for n streams at once.  Replaces
+ * DecodeRunner.nextFrame (src/lib/tts/engine/decode.ts:788-939) and its
+ * clearSeen (decode.ts:275-280); the per-step kernels it replaces are
+ * EMBED_ROW_LOCAL, the layer of runLayer, LAYERNORM_1 (ln_f), TEXT_HEAD_DECIDE,
+ * the audio-head GEMV and ARGMAX_PENALTY (kernels-decode.ts:96-124, 428-535).
+ *
+ *   step 0      x = the global hidden state -> continue iff
+ *               ln_f(x)·text_head[:, assistant_slot] >= ln_f(x)·text_head[:, audio_end]
+ *   step 1      x = wte[assistant_slot]     -> token 0 = argmax over audio head 0
+ *   step 2+i    x = audio_emb_i[token i]     -> token i+1 = argmax over audio head i+1
+ *
+ * Each step runs the local transformer's one layer over the local ring at
+ * position = step, then ln_f.  The argmax is greedy with the repetition penalty
+ * over the codes already emitted on that channel since the stream's last clear:
+ * a seen logit s becomes s / penalty when s >= 0 and s * penalty when s < 0;
+ * ties go to the lowest id.  As in the reference's GPU path, all 17 steps run
+ * (and set seen bits) even when the frame says stop.
+ * ------------------------------------------------------------------------- */
+
+typedef struct mb_local_head mb_local_head;
+
+typedef struct mb_local_config {
+    int32_t ffn;              /* FFN width of the local layer (3072) */
+    int32_t codes;            /* codebook size (CODES = 1024, decode.ts:48); a multiple of 32 */
+    int32_t channels;         /* codebooks per frame (n_vq = 16), 1..64; a frame takes channels + 1 steps */
+    float repetition_penalty; /* audio_repetition_penalty (1.2 in the published defaults) */
+} mb_local_config;
+
+/* Weights as one host array of fp32:
+ *   the local layer and ln_f, in mb_decoder_create's order for a one-layer ring
+ *     (mb_decoder_weight_count(local_ring, ffn) values)
+ *   wte_slot[H*64]                  the wte row of audio_assistant_slot_token_id
+ *   text_cols[2][H*64]              text head columns audio_end_token_id, then
+ *                                   audio_assistant_slot_token_id
+ *   audio_emb[channels-1][codes][H*64]   the audio embedding tables 0..channels-2
+ *   audio_head[channels][H*64][codes]    the audio heads ([K][N] row-major, no bias)
+ * `local_ring` must have one layer, capacity and max_position >= channels + 1;
+ * its `streams` are the streams whose seen masks the head keeps, its max_batch
+ * bounds n.  The layer and head matrices are stored on the device as bf16.
+ * mb_local_head_weight_count returns 0 for a ring the head cannot use. */
+MB_API size_t mb_local_head_weight_count(const mb_ctx* local_ring, const mb_local_config* cfg);
+MB_API int mb_local_head_create(mb_ctx* local_ring, const mb_local_config* cfg, const float* host_weights,
+                                size_t count, mb_local_head** out);
+MB_API int mb_local_head_destroy(mb_local_head* head);
+
+/* Zero the seen masks of one stream (or of every stream when stream = -1): a new
+ * utterance starts clean (clearSeen, decode.ts:275-280).  Async on cuda_stream. */
+MB_API int mb_local_head_clear(mb_local_head* head, int32_t stream, void* cuda_stream);
+
+/* One frame for n streams.  Device pointers: streams [n] (distinct ring stream
+ * ids), hidden [n][H*64] fp32 (the global step's ln_f output; not modified),
+ * tokens [n][channels] int32 out, cont [n] int32 out (1 = continue, 0 = the
+ * utterance ends: nextFrame's null), logits [n][channels][codes] fp32 out or NULL
+ * (every channel's logits before the penalty, for tests).  Async on cuda_stream. */
+MB_API int mb_local_head_frame(mb_local_head* head, int32_t n, const int32_t* streams, const float* hidden,
+                               int32_t* tokens, int32_t* cont, float* logits, void* cuda_stream);
+
+/* ARGMAX_PENALTY alone (kernels-decode.ts:428-485), on the current device: for
+ * each of n rows, token = the penalised argmax of logits [n][codes] under the
+ * row's seen mask seen [n][codes/32] (bit j of word j/32), whose bit is then
+ * set.  Device pointers; codes a multiple of 32. */
+MB_API int mb_argmax_penalty(int32_t n, int32_t codes, const float* logits, uint32_t* seen, float penalty,
+                             int32_t* tokens, void* cuda_stream);
+
+/* ---------------------------------------------------------------------------
  * No-allocation entry point.  No counterpart in the reference: the reference
  * allocates its GPU buffers once per engine and never hands that job to callers.
  *

@@ -5,7 +5,7 @@ MOSS-TTS-Nano decoder, behind the C ABI of include/mockbird_kv.h.
     ring = KvRing(capacity=512, streams=64, wrap=True)
     ctx = ring.append_attend(layer, streams, positions, qkv)   # one fused launch
 """
-from .engine import KvRing, MockbirdError  # noqa: F401
+from .engine import Decoder, KvRing, LocalHead, MockbirdError, argmax_penalty  # noqa: F401
 from ._lib import LIB_PATH, load  # noqa: F401
 
-__all__ = ["KvRing", "MockbirdError", "LIB_PATH", "load"]
+__all__ = ["Decoder", "KvRing", "LocalHead", "MockbirdError", "argmax_penalty", "LIB_PATH", "load"]

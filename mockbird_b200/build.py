@@ -18,9 +18,9 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libmockbird_kv.so")
 
-SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_decode_persist.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_decoder.cu",
+SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_decode_persist.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_decoder.cu", "mb_local.cu",
            "mb_noalloc.cu"]
-HEADERS = ["mb_internal.cuh", "mb_ptx.cuh"]
+HEADERS = ["mb_internal.cuh", "mb_ptx.cuh", "mb_decoder.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # cuBLASLt: the plain GEMMs of the decoder step around the path

@@ -10,15 +10,9 @@
 // epilogue: y = b + x W, W [K][N] row-major as the published graph stores it);
 // LayerNorm (LAYERNORM_1, kernels-decode.ts:168-200: eps 1e-5, two passes) and
 // GELU (GELU_TANH, kernels-decode.ts:373-390) are kernels here.
-#include <cublasLt.h>
 #include <string.h>
 
-#include <map>
-#include <string>
-#include <tuple>
-#include <vector>
-
-#include "mb_internal.cuh"
+#include "mb_decoder.cuh"
 
 namespace {
 
@@ -71,12 +65,36 @@ __global__ void gelu_tanh_to_bf16(const float* __restrict__ x, bf16* __restrict_
     }
 }
 
-__global__ void to_bf16(const float* __restrict__ x, bf16* __restrict__ y, size_t n) {
+__global__ void to_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y, size_t n) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         y[i] = __float2bfloat16_rn(x[i]);
 }
 
-uint16_t f32_to_bf16_bits(float f) {  // round to nearest even
+template <typename TO>
+cudaError_t layernorm(const float* x, const float* w, const float* b, TO* y, int rows, int width, cudaStream_t st) {
+    const int warps = 4, blocks = (rows + warps - 1) / warps;
+    switch (width / 32) {  // width = heads * 64
+        case 2: layernorm_rows<TO, 2><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
+        case 8: layernorm_rows<TO, 8><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
+        case 24: layernorm_rows<TO, 24><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+constexpr int CVT_BLOCKS = 2 * 148;
+
+}  // namespace
+
+namespace mb {
+namespace dec {
+
+int fail(mb_decoder* d, int code, const std::string& msg) {
+    if (d && d->ctx) d->ctx->last_error = msg;
+    return code;
+}
+
+uint16_t f32_to_bf16_bits(float f) {
     uint32_t u;
     memcpy(&u, &f, 4);
     if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
@@ -84,57 +102,28 @@ uint16_t f32_to_bf16_bits(float f) {  // round to nearest even
     return (uint16_t)(u >> 16);
 }
 
-}  // namespace
-
-struct mb_decoder {
-    mb_ctx* ctx = nullptr;
-    int hid = 0, ffn = 0, layers = 0;
-    struct Layer {
-        const float *ln1_w, *ln1_b, *b_attn, *b_proj, *ln2_w, *ln2_b, *b_in, *b_out;
-        const bf16 *w_attn, *w_proj, *w_in, *w_out;
-    };
-    std::vector<Layer> L;
-    const float *lnf_w = nullptr, *lnf_b = nullptr;
-    void* wmem = nullptr;      // all weights, one allocation
-    bf16* xb = nullptr;        // [max_batch][max(hid, ffn)] GEMM input
-    float* qkv = nullptr;      // [max_batch][3*hid]
-    float* att = nullptr;      // [max_batch][hid]
-    float* h1 = nullptr;       // [max_batch][ffn]
-    cublasLtHandle_t lt = nullptr;
-    void* workspace = nullptr;
-    size_t ws_bytes = 32u << 20;
-    struct Plan {  // one GEMM shape: descriptors and the chosen algorithm, built once
-        cublasLtMatmulDesc_t op = nullptr;
-        cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
-        cublasLtMatmulAlgo_t algo{};
-    };
-    std::map<std::tuple<int, int, int>, Plan> plans;
-};
-
-namespace {
-
-int dfail(mb_decoder* d, int code, const std::string& msg) {
-    if (d && d->ctx) d->ctx->last_error = msg;
-    return code;
+cudaError_t to_bf16(const float* x, bf16* y, size_t n, cudaStream_t st) {
+    to_bf16_kernel<<<CVT_BLOCKS, 256, 0, st>>>(x, y, n);
+    return cudaGetLastError();
 }
 
-// y[M][N] (fp32, row-major) = x[M][K] (bf16) * W[K][N] (bf16) + bias[N] (+ y if accumulate)
 int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const float* bias, float* y,
          bool accumulate, cudaStream_t st) {
     // column-major view: y^T [N x M] = W^T [N x K] * x^T [K x M]
     cublasStatus_t s = CUBLAS_STATUS_SUCCESS;
-    const auto key = std::make_tuple(M, N, K);
+    const bool has_bias = bias != nullptr;
+    const auto key = std::make_tuple(M, N, K, has_bias ? 1 : 0);
     auto it = d->plans.find(key);
     if (it == d->plans.end()) {
         mb_decoder::Plan p;
-        cublasLtEpilogue_t epi = CUBLASLT_EPILOGUE_BIAS;
+        cublasLtEpilogue_t epi = has_bias ? CUBLASLT_EPILOGUE_BIAS : CUBLASLT_EPILOGUE_DEFAULT;
         cudaDataType_t bias_t = CUDA_R_32F;
         s = cublasLtMatmulDescCreate(&p.op, CUBLAS_COMPUTE_32F, CUDA_R_32F);
         if (s == CUBLAS_STATUS_SUCCESS)
             s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof epi);
-        if (s == CUBLAS_STATUS_SUCCESS)
+        if (s == CUBLAS_STATUS_SUCCESS && has_bias)
             s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bias_t, sizeof bias_t);
-        if (s == CUBLAS_STATUS_SUCCESS)
+        if (s == CUBLAS_STATUS_SUCCESS && has_bias)
             s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
         if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.a, CUDA_R_16BF, N, K, N);
         if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.b, CUDA_R_16BF, K, M, K);
@@ -155,35 +144,53 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const
             if (p.b) cublasLtMatrixLayoutDestroy(p.b);
             if (p.a) cublasLtMatrixLayoutDestroy(p.a);
             if (p.op) cublasLtMatmulDescDestroy(p.op);
-            return dfail(d, MB_ERR_CUDA, std::string("cuBLASLt setup failed: ") + cublasLtGetStatusString(s));
+            return fail(d, MB_ERR_CUDA, std::string("cuBLASLt setup failed: ") + cublasLtGetStatusString(s));
         }
         p.algo = res.algo;
         it = d->plans.emplace(key, p).first;
     }
     mb_decoder::Plan& p = it->second;
-    s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
+    if (has_bias) s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
     const float alpha = 1.f, beta = accumulate ? 1.f : 0.f;
     if (s == CUBLAS_STATUS_SUCCESS)
         s = cublasLtMatmul(d->lt, p.op, &alpha, W, p.a, x, p.b, &beta, y, p.c, y, p.c, &p.algo, d->workspace,
                            d->ws_bytes, st);
     if (s != CUBLAS_STATUS_SUCCESS)
-        return dfail(d, MB_ERR_CUDA, std::string("cuBLASLt matmul failed: ") + cublasLtGetStatusString(s));
+        return fail(d, MB_ERR_CUDA, std::string("cuBLASLt matmul failed: ") + cublasLtGetStatusString(s));
     return MB_OK;
 }
 
-template <typename TO>
-cudaError_t layernorm(const float* x, const float* w, const float* b, TO* y, int rows, int width, cudaStream_t st) {
-    const int warps = 4, blocks = (rows + warps - 1) / warps;
-    switch (width / 32) {  // width = heads * 64
-        case 2: layernorm_rows<TO, 2><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
-        case 8: layernorm_rows<TO, 8><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
-        case 24: layernorm_rows<TO, 24><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
-        default: return cudaErrorInvalidValue;
+int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
+        cudaStream_t st) {
+    mb_ctx* c = d->ctx;
+    const int h = d->hid, f = d->ffn;
+    int rc = MB_OK;
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < d->layers && rc == MB_OK && e == cudaSuccess; l++) {
+        const auto& W = d->L[l];
+        if ((e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess) break;
+        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, false, st))) break;
+        if ((e = mb::launch_decode(c->cfg.dtype, true, mb::ring_view(c, l), c->scratch, n, streams, positions, d->qkv,
+                                   3 * h, d->att, st)) != cudaSuccess)
+            break;
+        if ((e = to_bf16(d->att, d->xb, (size_t)n * h, st)) != cudaSuccess) break;
+        if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, true, st))) break;
+        if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, d->xb, n, h, st)) != cudaSuccess) break;
+        if ((rc = gemm(d, n, f, h, d->xb, W.w_in, W.b_in, d->h1, false, st))) break;
+        gelu_tanh_to_bf16<<<CVT_BLOCKS, 256, 0, st>>>(d->h1, d->xb, (size_t)n * f);
+        if ((rc = gemm(d, n, h, f, d->xb, W.w_out, W.b_out, hidden, true, st))) break;
+        e = cudaGetLastError();
     }
-    return cudaGetLastError();
+    if (rc == MB_OK && e == cudaSuccess)
+        e = lnf_bf16 ? layernorm<bf16>(hidden, d->lnf_w, d->lnf_b, lnf_bf16, n, h, st)
+                     : layernorm<float>(hidden, d->lnf_w, d->lnf_b, hidden, n, h, st);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(d, MB_ERR_CUDA, std::string("decoder: ") + cudaGetErrorString(e));
+    return MB_OK;
 }
 
-}  // namespace
+}  // namespace dec
+}  // namespace mb
 
 extern "C" {
 
@@ -270,7 +277,7 @@ MB_API int mb_decoder_create(mb_ctx* c, int32_t ffn, const float* w, size_t coun
     for (auto& b : blks) {
         if (b.mat) {
             uint16_t* o = reinterpret_cast<uint16_t*>(img.data() + b.dst);
-            for (size_t i = 0; i < b.n; i++) o[i] = f32_to_bf16_bits(w[b.src + i]);
+            for (size_t i = 0; i < b.n; i++) o[i] = mb::dec::f32_to_bf16_bits(w[b.src + i]);
         } else {
             memcpy(img.data() + b.dst, w + b.src, b.n * 4);
         }
@@ -304,38 +311,16 @@ MB_API int mb_decoder_step(mb_decoder* d, int32_t n, const int32_t* streams, con
                            float* hidden, void* cuda_stream) {
     if (!d) return MB_ERR_ARG;
     mb_ctx* c = d->ctx;
-    if (n < 0 || n > c->cfg.max_batch) return dfail(d, MB_ERR_ARG, "decoder: item count out of range");
+    if (n < 0 || n > c->cfg.max_batch) return mb::dec::fail(d, MB_ERR_ARG, "decoder: item count out of range");
     if (n == 0) return MB_OK;
     if (!streams || !positions || !hidden || (reinterpret_cast<uintptr_t>(hidden) & 15))
-        return dfail(d, MB_ERR_ARG, "decoder: null or misaligned device pointer");
+        return mb::dec::fail(d, MB_ERR_ARG, "decoder: null or misaligned device pointer");
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != c->cfg.device && cudaSetDevice(c->cfg.device) != cudaSuccess) return MB_ERR_CUDA;
-    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    const int h = d->hid, f = d->ffn;
-    const int cvt_blocks = 2 * 148;
-    int rc = MB_OK;
-    cudaError_t e = cudaSuccess;
-    for (int l = 0; l < d->layers && rc == MB_OK && e == cudaSuccess; l++) {
-        const auto& W = d->L[l];
-        if ((e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess) break;
-        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, false, st))) break;
-        if ((e = mb::launch_decode(c->cfg.dtype, true, mb::ring_view(c, l), c->scratch, n, streams, positions, d->qkv,
-                                   3 * h, d->att, st)) != cudaSuccess)
-            break;
-        to_bf16<<<cvt_blocks, 256, 0, st>>>(d->att, d->xb, (size_t)n * h);
-        if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, true, st))) break;
-        if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, d->xb, n, h, st)) != cudaSuccess) break;
-        if ((rc = gemm(d, n, f, h, d->xb, W.w_in, W.b_in, d->h1, false, st))) break;
-        gelu_tanh_to_bf16<<<cvt_blocks, 256, 0, st>>>(d->h1, d->xb, (size_t)n * f);
-        if ((rc = gemm(d, n, h, f, d->xb, W.w_out, W.b_out, hidden, true, st))) break;
-        e = cudaGetLastError();
-    }
-    if (rc == MB_OK && e == cudaSuccess) e = layernorm<float>(hidden, d->lnf_w, d->lnf_b, hidden, n, h, st);
+    const int rc = mb::dec::run(d, n, streams, positions, hidden, nullptr, static_cast<cudaStream_t>(cuda_stream));
     if (prev >= 0 && prev != c->cfg.device) cudaSetDevice(prev);
-    if (rc) return rc;
-    if (e != cudaSuccess) return dfail(d, MB_ERR_CUDA, std::string("decoder: ") + cudaGetErrorString(e));
-    return MB_OK;
+    return rc;
 }
 
 }  // extern "C"

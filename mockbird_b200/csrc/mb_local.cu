@@ -1,0 +1,399 @@
+// The local head: the 17 sequential steps that turn one global hidden state into
+// one frame of 16 audio codes (DecodeRunner.nextFrame, liyu1981/mockbird
+// src/lib/tts/engine/decode.ts:788-939; CPU form tools/onnx-probe/ref-decode.mjs
+// :236-283 and :380-410), for n streams at once.
+//
+//   step 0      x = the global hidden state   -> continue/stop from two columns
+//                                                 of the text head (TEXT_HEAD_DECIDE)
+//   step 1      x = wte[assistant_slot]        -> argmax over audio head 0
+//   step 2+i    x = audio_emb_i[token_i]       -> argmax over audio head i+1
+//
+// Every step runs the local transformer's single layer over a 17-slot KV ring at
+// position = step, then ln_f.  The argmax is greedy with the HuggingFace
+// repetition penalty over the codes already emitted on that channel in this
+// utterance (ARGMAX_PENALTY, kernels-decode.ts:428-485): a per-stream,
+// per-channel 1024-bit seen mask kept on the device.  Tokens never leave the
+// device between steps.
+//
+// The layer is the decoder machinery of mb_decoder.cu (cuBLASLt GEMMs with bf16
+// weights and fp32 accumulation, this library's LayerNorm, GELU and fused
+// append + RoPE + attention kernels).  The 16 audio heads [768][1024] are bf16
+// GEMMs without bias (the graph's bare MatMul, decode.ts:875); the embeddings,
+// the two text-head columns and everything between the GEMMs stay fp32.
+//
+// One frame is ~220 launches of small kernels, so by default it is captured once
+// per batch size into a CUDA graph and replayed (MOCKBIRD_LOCAL_GRAPH=0 turns
+// that off); the graph reads and writes only this object's own buffers.
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <utility>
+
+#include "mb_decoder.cuh"
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+// x[i] = the step's input row (EMBED_ROW_LOCAL, kernels-decode.ts:96-124, modes
+// 1 and 2; mode "hidden" is the writeBuffer of decode.ts:792).  Tokens come from
+// argmax_penalty_kernel and are always in [0, codes); the clamp only keeps a
+// corrupted token from addressing outside the table.
+__global__ void local_embed_kernel(int step, int h, int channels, int codes, const float* __restrict__ hin,
+                                   const float* __restrict__ wte_slot, const float* __restrict__ emb,
+                                   const int32_t* __restrict__ tokens, float* __restrict__ x) {
+    const int i = blockIdx.x;
+    const float* src;
+    if (step == 0) {
+        src = hin + (size_t)i * h;
+    } else if (step == 1) {
+        src = wte_slot;
+    } else {
+        const int ch = step - 2;
+        int tok = tokens[(size_t)i * channels + ch];
+        tok = min(max(tok, 0), codes - 1);
+        src = emb + ((size_t)ch * codes + tok) * h;
+    }
+    float4* dst = reinterpret_cast<float4*>(x + (size_t)i * h);
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    for (int d = threadIdx.x; d < h / 4; d += blockDim.x) dst[d] = s4[d];
+}
+
+// TEXT_HEAD_DECIDE (kernels-decode.ts:487-535): the dot products of ln_f(x) with
+// the text head's audio_end and assistant_slot columns; continue iff
+// assistant >= end.  One warp per item.
+__global__ void local_decide_kernel(int n, int h, const float* __restrict__ x, const float* __restrict__ cols,
+                                    int32_t* __restrict__ cont) {
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (i >= n) return;
+    const float* xr = x + (size_t)i * h;
+    float end = 0.f, asst = 0.f;
+    for (int d = lane; d < h; d += 32) {
+        end = fmaf(xr[d], cols[d], end);
+        asst = fmaf(xr[d], cols[h + d], asst);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        end += __shfl_xor_sync(0xffffffffu, end, o);
+        asst += __shfl_xor_sync(0xffffffffu, asst, o);
+    }
+    if (lane == 0) cont[i] = asst >= end ? 1 : 0;
+}
+
+// ARGMAX_PENALTY (kernels-decode.ts:428-485) for one row per warp.  A logit
+// whose bit is set in the row's seen mask becomes s / penalty (s >= 0) or
+// s * penalty (s < 0); the winner is the largest value, ties to the lowest id,
+// starting from (-1e30, id 0) as the reference does; its bit is then set.
+// Each lane scans ids lane, lane+32, ... with a strict >, and the warp reduces
+// under the order (value desc, id asc) -- the same total-order maximum as the
+// reference's strided scan and tree, so the same winner.
+// Row i: logits + i*codes; mask = seen + row_sel(i) * seen_row_words + ch * codes/32
+// (row_sel(i) = streams[i] when `streams` is given, else i; rows whose stream is
+// outside [0, n_seen_rows) get token 0 and leave the masks alone -- the ring's
+// own kernel reports such a stream); token -> tokens[i*tok_stride + ch].
+__global__ void argmax_penalty_kernel(int n, int codes, const float* __restrict__ logits, uint32_t* __restrict__ seen,
+                                      const int32_t* __restrict__ streams, int n_seen_rows, int seen_row_words, int ch,
+                                      float penalty, int32_t* __restrict__ tokens, int tok_stride) {
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (i >= n) return;
+    const int row = streams ? streams[i] : i;
+    const bool ok = row >= 0 && row < n_seen_rows;
+    uint32_t* mask = seen + (size_t)(ok ? row : 0) * seen_row_words + (size_t)ch * (codes >> 5);
+    const float* lg = logits + (size_t)i * codes;
+    float best = -1e30f;
+    int idx = 0;
+    for (int j = lane; j < codes; j += 32) {
+        float s = lg[j];
+        if (ok && ((mask[j >> 5] >> (j & 31)) & 1u)) s = s >= 0.f ? s / penalty : s * penalty;
+        if (s > best) {
+            best = s;
+            idx = j;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    if (lane == 0) {
+        tokens[(size_t)i * tok_stride + ch] = ok ? idx : 0;
+        if (ok) mask[idx >> 5] |= 1u << (idx & 31);
+    }
+}
+
+}  // namespace
+
+struct mb_local_head {
+    mb_ctx* ctx = nullptr;       // the local ring (one layer, >= channels + 1 slots)
+    mb_decoder* dec = nullptr;   // the local transformer layer + ln_f
+    int h = 0, codes = 0, channels = 0, max_batch = 0, seen_words = 0;
+    float penalty = 1.f;
+    void* wmem = nullptr;        // wte_slot [h] | cols [2][h] | emb [(channels-1)][codes][h] (fp32) | heads (bf16)
+    const float *wte_slot = nullptr, *cols = nullptr, *emb = nullptr;
+    const bf16* heads = nullptr; // [channels][h][codes]
+    float* hin = nullptr;        // [max_batch][h] staged global hidden states
+    float* x = nullptr;          // [max_batch][h] the step's residual stream
+    bf16* hb = nullptr;          // [max_batch][h] ln_f output, head GEMM input
+    float* lg = nullptr;         // [max_batch][codes] one channel's logits
+    float* lg_all = nullptr;     // [max_batch][channels][codes] when the caller asks for logits
+    int32_t* tok = nullptr;      // [max_batch][channels]
+    int32_t* cont = nullptr;     // [max_batch]
+    int32_t* ids = nullptr;      // [max_batch] staged stream ids
+    int32_t* pos = nullptr;      // [channels + 1][max_batch], row s all = s
+    uint32_t* seen = nullptr;    // [ring streams][channels][codes / 32]
+    bool use_graph = true;
+    cudaStream_t cap = nullptr;  // capture stream
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (n, logits wanted) -> frame
+};
+
+namespace {
+
+int lfail(mb_local_head* lh, int code, const std::string& msg) {
+    if (lh && lh->ctx) lh->ctx->last_error = msg;
+    return code;
+}
+
+size_t dec_count(const mb_ctx* c, int ffn) { return mb_decoder_weight_count(c, ffn); }
+
+// The whole frame on `st`, over this object's buffers only (graph-capturable).
+int enqueue_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
+    const int h = lh->h, steps = lh->channels + 1;
+    const int warps = 4, wblocks = (n + warps - 1) / warps;
+    for (int step = 0; step < steps; step++) {
+        local_embed_kernel<<<n, 192, 0, st>>>(step, h, lh->channels, lh->codes, lh->hin, lh->wte_slot, lh->emb,
+                                              lh->tok, lh->x);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head: ") + cudaGetErrorString(e));
+        int rc = mb::dec::run(lh->dec, n, lh->ids, lh->pos + (size_t)step * lh->max_batch, lh->x,
+                              step == 0 ? nullptr : lh->hb, st);
+        if (rc) return rc;
+        if (step == 0) {
+            local_decide_kernel<<<wblocks, 32 * warps, 0, st>>>(n, h, lh->x, lh->cols, lh->cont);
+        } else {
+            const int ch = step - 1;
+            rc = mb::dec::gemm(lh->dec, n, lh->codes, h, lh->hb, lh->heads + (size_t)ch * h * lh->codes, nullptr,
+                               lh->lg, false, st);
+            if (rc) return rc;
+            argmax_penalty_kernel<<<wblocks, 32 * warps, 0, st>>>(n, lh->codes, lh->lg, lh->seen, lh->ids,
+                                                                  lh->ctx->cfg.streams, lh->seen_words, ch,
+                                                                  lh->penalty, lh->tok, lh->channels);
+            if (want_logits) {
+                const size_t row = (size_t)lh->codes * sizeof(float);
+                e = cudaMemcpy2DAsync(lh->lg_all + (size_t)ch * lh->codes, row * lh->channels, lh->lg, row, row, n,
+                                      cudaMemcpyDeviceToDevice, st);
+                if (e != cudaSuccess)
+                    return lfail(lh, MB_ERR_CUDA, std::string("local head: ") + cudaGetErrorString(e));
+            }
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head: ") + cudaGetErrorString(e));
+    }
+    return MB_OK;
+}
+
+// Replays the captured frame for (n, want_logits).  The first frame of a key runs
+// directly on `st` (so every kernel module is loaded and every GEMM plan built
+// outside a capture) and is then captured, without running, for the next calls.
+int launch_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
+    const auto key = std::make_pair(n, want_logits ? 1 : 0);
+    auto it = lh->graphs.find(key);
+    if (it == lh->graphs.end()) {
+        int rc = enqueue_frame(lh, n, want_logits, st);
+        if (rc) return rc;
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(lh->cap, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head capture: ") + cudaGetErrorString(e));
+        rc = enqueue_frame(lh, n, want_logits, lh->cap);
+        e = cudaStreamEndCapture(lh->cap, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head capture: ") + cudaGetErrorString(e));
+        cudaGraphExec_t ex = nullptr;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess)
+            return lfail(lh, MB_ERR_CUDA, std::string("local head graph: ") + cudaGetErrorString(e));
+        lh->graphs.emplace(key, ex);
+        return MB_OK;
+    }
+    const cudaError_t e = cudaGraphLaunch(it->second, st);
+    if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head graph: ") + cudaGetErrorString(e));
+    return MB_OK;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+MB_API size_t mb_local_head_weight_count(const mb_ctx* c, const mb_local_config* cfg) {
+    if (!c || !cfg || cfg->ffn <= 0 || cfg->codes <= 0 || cfg->channels <= 0) return 0;
+    const int steps = cfg->channels + 1;
+    if (c->cfg.layers != 1 || c->cfg.capacity < steps || c->cfg.max_position < steps) return 0;
+    const size_t h = (size_t)c->cfg.heads * mb::HD, codes = (size_t)cfg->codes, ch = (size_t)cfg->channels;
+    return dec_count(c, cfg->ffn) + h + 2 * h + (ch - 1) * codes * h + ch * h * codes;
+}
+
+MB_API int mb_local_head_destroy(mb_local_head* lh) {
+    if (!lh) return MB_ERR_ARG;
+    DeviceGuard g(lh->ctx->cfg.device);
+    for (auto& kv : lh->graphs) cudaGraphExecDestroy(kv.second);
+    if (lh->cap) cudaStreamDestroy(lh->cap);
+    void* ptrs[] = {lh->wmem, lh->hin, lh->x, lh->hb, lh->lg, lh->lg_all, lh->tok, lh->cont, lh->ids, lh->pos,
+                    lh->seen};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    if (lh->dec) mb_decoder_destroy(lh->dec);
+    delete lh;
+    return MB_OK;
+}
+
+MB_API int mb_local_head_create(mb_ctx* c, const mb_local_config* cfg, const float* w, size_t count,
+                                mb_local_head** out) {
+    if (!c || !cfg || !w || !out) return MB_ERR_ARG;
+    *out = nullptr;
+    const int steps = cfg->channels + 1;
+    if (cfg->codes <= 0 || cfg->codes % 32 || cfg->channels <= 0 || cfg->channels > 64 ||
+        !(cfg->repetition_penalty > 0.f) || !isfinite(cfg->repetition_penalty)) {
+        c->last_error = "local head: codes must be a positive multiple of 32, channels in [1, 64], penalty > 0";
+        return MB_ERR_ARG;
+    }
+    if (c->cfg.layers != 1 || c->cfg.capacity < steps || c->cfg.max_position < steps) {
+        c->last_error = "local head: the ring must have one layer and at least channels + 1 slots and positions";
+        return MB_ERR_ARG;
+    }
+    if (count != mb_local_head_weight_count(c, cfg)) {
+        c->last_error = "local head: weight count does not match (layer, ffn, codes, channels)";
+        return MB_ERR_ARG;
+    }
+    DeviceGuard g(c->cfg.device);
+    if (!g.ok) return MB_ERR_CUDA;
+    mb_local_head* lh = new mb_local_head();
+    lh->ctx = c;
+    lh->h = c->cfg.heads * mb::HD;
+    lh->codes = cfg->codes;
+    lh->channels = cfg->channels;
+    lh->penalty = cfg->repetition_penalty;
+    lh->max_batch = c->cfg.max_batch;
+    lh->seen_words = cfg->channels * (cfg->codes / 32);
+    {
+        const char* v = getenv("MOCKBIRD_LOCAL_GRAPH");
+        lh->use_graph = !(v && strcmp(v, "0") == 0);
+    }
+    auto bail = [&](int rc, const char* msg) {
+        if (msg) c->last_error = msg;
+        mb_local_head_destroy(lh);
+        return rc;
+    };
+    const size_t nd = dec_count(c, cfg->ffn);
+    int rc = mb_decoder_create(c, cfg->ffn, w, nd, &lh->dec);
+    if (rc) return bail(rc, nullptr);
+    const size_t h = lh->h, codes = lh->codes, ch = lh->channels, mbat = lh->max_batch;
+    // device image: fp32 wte_slot | cols | emb, then the bf16 heads (256-byte aligned)
+    const size_t n_f32 = h + 2 * h + (ch - 1) * codes * h;
+    const size_t f32_bytes = (n_f32 * 4 + 255) & ~size_t(255);
+    const size_t n_heads = ch * h * codes;
+    const size_t bytes = f32_bytes + n_heads * 2;
+    std::vector<unsigned char> img(bytes, 0);
+    memcpy(img.data(), w + nd, n_f32 * 4);
+    uint16_t* hb16 = reinterpret_cast<uint16_t*>(img.data() + f32_bytes);
+    for (size_t i = 0; i < n_heads; i++) hb16[i] = mb::dec::f32_to_bf16_bits(w[nd + n_f32 + i]);
+    if (cudaMalloc(&lh->wmem, bytes) != cudaSuccess) return bail(MB_ERR_OOM, "local head: weight allocation failed");
+    if (cudaMemcpy(lh->wmem, img.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+        return bail(MB_ERR_CUDA, "local head: weight upload failed");
+    lh->wte_slot = reinterpret_cast<const float*>(lh->wmem);
+    lh->cols = lh->wte_slot + h;
+    lh->emb = lh->cols + 2 * h;
+    lh->heads = reinterpret_cast<const bf16*>((char*)lh->wmem + f32_bytes);
+    std::vector<int32_t> pos((size_t)steps * mbat);
+    for (int s = 0; s < steps; s++)
+        for (size_t i = 0; i < mbat; i++) pos[(size_t)s * mbat + i] = s;
+    const size_t seen_bytes = (size_t)c->cfg.streams * lh->seen_words * 4;
+    if (cudaMalloc(&lh->hin, mbat * h * 4) != cudaSuccess || cudaMalloc(&lh->x, mbat * h * 4) != cudaSuccess ||
+        cudaMalloc(&lh->hb, mbat * h * 2) != cudaSuccess || cudaMalloc(&lh->lg, mbat * codes * 4) != cudaSuccess ||
+        cudaMalloc(&lh->tok, mbat * ch * 4) != cudaSuccess || cudaMalloc(&lh->cont, mbat * 4) != cudaSuccess ||
+        cudaMalloc(&lh->ids, mbat * 4) != cudaSuccess || cudaMalloc(&lh->pos, pos.size() * 4) != cudaSuccess ||
+        cudaMalloc(&lh->seen, seen_bytes) != cudaSuccess)
+        return bail(MB_ERR_OOM, "local head: buffer allocation failed");
+    if (cudaMemcpy(lh->pos, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(lh->seen, 0, seen_bytes) != cudaSuccess || cudaMemset(lh->tok, 0, mbat * ch * 4) != cudaSuccess)
+        return bail(MB_ERR_CUDA, "local head: buffer initialisation failed");
+    if (cudaStreamCreateWithFlags(&lh->cap, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(MB_ERR_CUDA, "local head: stream creation failed");
+    *out = lh;
+    return MB_OK;
+}
+
+MB_API int mb_local_head_clear(mb_local_head* lh, int32_t stream, void* cuda_stream) {
+    if (!lh) return MB_ERR_ARG;
+    const int streams = lh->ctx->cfg.streams;
+    if (stream < -1 || stream >= streams) return lfail(lh, MB_ERR_STREAM, "local head: stream out of range");
+    DeviceGuard g(lh->ctx->cfg.device);
+    if (!g.ok) return MB_ERR_CUDA;
+    const size_t row = (size_t)lh->seen_words * 4;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const cudaError_t e = stream < 0 ? cudaMemsetAsync(lh->seen, 0, row * streams, st)
+                                     : cudaMemsetAsync(lh->seen + (size_t)stream * lh->seen_words, 0, row, st);
+    if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head: ") + cudaGetErrorString(e));
+    return MB_OK;
+}
+
+MB_API int mb_local_head_frame(mb_local_head* lh, int32_t n, const int32_t* streams, const float* hidden,
+                               int32_t* tokens, int32_t* cont, float* logits, void* cuda_stream) {
+    if (!lh) return MB_ERR_ARG;
+    if (n < 0 || n > lh->max_batch) return lfail(lh, MB_ERR_ARG, "local head: item count out of range");
+    if (n == 0) return MB_OK;
+    if (!streams || !hidden || !tokens || !cont)
+        return lfail(lh, MB_ERR_ARG, "local head: null device pointer");
+    DeviceGuard g(lh->ctx->cfg.device);
+    if (!g.ok) return MB_ERR_CUDA;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const size_t h = lh->h, ch = lh->channels, codes = lh->codes;
+    if (logits && !lh->lg_all && cudaMalloc(&lh->lg_all, (size_t)lh->max_batch * ch * codes * 4) != cudaSuccess)
+        return lfail(lh, MB_ERR_OOM, "local head: logits buffer allocation failed");
+    cudaError_t e = cudaMemcpyAsync(lh->ids, streams, (size_t)n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(lh->hin, hidden, (size_t)n * h * 4, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head inputs: ") + cudaGetErrorString(e));
+    const int rc = lh->use_graph ? launch_frame(lh, n, logits != nullptr, st) : enqueue_frame(lh, n, logits != nullptr, st);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(tokens, lh->tok, (size_t)n * ch * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(cont, lh->cont, (size_t)n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess && logits)
+        e = cudaMemcpyAsync(logits, lh->lg_all, (size_t)n * ch * codes * 4, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head outputs: ") + cudaGetErrorString(e));
+    return MB_OK;
+}
+
+MB_API int mb_argmax_penalty(int32_t n, int32_t codes, const float* logits, uint32_t* seen, float penalty,
+                             int32_t* tokens, void* cuda_stream) {
+    if (n < 0 || codes <= 0 || codes % 32 || !(penalty > 0.f) || !isfinite(penalty)) return MB_ERR_ARG;
+    if (n == 0) return MB_OK;
+    if (!logits || !seen || !tokens) return MB_ERR_ARG;
+    const int warps = 4;
+    argmax_penalty_kernel<<<(n + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(cuda_stream)>>>(
+        n, codes, logits, seen, nullptr, n, codes / 32, 0, penalty, tokens, 1);
+    return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -297,3 +297,86 @@ class Decoder:
             self.dispose()
         except Exception:
             pass
+
+
+class LocalHead:
+    """The local 17-step head (DecodeRunner.nextFrame, decode.ts:788-939) for n
+    streams at once: one frame of `channels` audio codes per stream plus the
+    continue/stop decision, the repetition-penalty seen masks kept on the device
+    (clearSeen, decode.ts:275-280, is `clear`).
+
+    `ring`: the local ring -- a KvRing with one layer and capacity >= channels + 1.
+    `weights`: one fp32 array in the order of mb_local_head_create
+    (include/mockbird_kv.h); `weight_count` gives its length."""
+
+    def __init__(self, ring: KvRing, weights: np.ndarray, ffn: int = 3072, codes: int = 1024,
+                 channels: int = 16, repetition_penalty: float = 1.2):
+        self.ring, self.lib = ring, ring.lib
+        self.ffn, self.codes, self.channels, self.penalty = ffn, codes, channels, repetition_penalty
+        self.cfg = _lib.MbLocalConfig(ffn, codes, channels, repetition_penalty)
+        w = np.ascontiguousarray(weights, np.float32)
+        want = self.lib.mb_local_head_weight_count(ring.ctx, ctypes.byref(self.cfg))
+        if want and w.size != want:  # 0: the ring does not suit; create reports why
+            raise ValueError(f"local head weights: {w.size} values, expected {want}")
+        handle = ctypes.c_void_p()
+        ring._check(self.lib.mb_local_head_create(ring.ctx, ctypes.byref(self.cfg), _ptr(w), w.size,
+                                                  ctypes.byref(handle)))
+        self.handle = handle
+
+    @staticmethod
+    def weight_count(hidden: int, ffn: int, codes: int, channels: int) -> int:
+        h = hidden
+        return Decoder.weight_count(1, h, ffn) + h + 2 * h + (channels - 1) * codes * h + channels * h * codes
+
+    def clear(self, stream: int = -1, cuda_stream=None) -> None:
+        """Zero the seen masks of `stream` (all streams when -1): a new utterance."""
+        self.ring._check(self.lib.mb_local_head_clear(self.handle, int(stream), self.ring._stream(cuda_stream)))
+
+    def frame(self, streams, hidden: torch.Tensor, logits: bool = False, stream=None):
+        """hidden [n][H*64] fp32 (device): the global step's ln_f output.
+
+        Returns (tokens [n][channels] int32, cont [n] int32 -- 1 continue, 0 stop,
+        logits [n][channels][codes] fp32 before the penalty, or None)."""
+        s, x = self.ring._ids(streams), self.ring._dev(hidden)
+        n = s.numel()
+        tok = torch.empty(n, self.channels, dtype=torch.int32, device=self.ring.device)
+        cont = torch.empty(n, dtype=torch.int32, device=self.ring.device)
+        lg = (torch.empty(n, self.channels, self.codes, dtype=torch.float32, device=self.ring.device)
+              if logits else None)
+        rc = self.lib.mb_local_head_frame(self.handle, n, _ptr(s), _ptr(x), _ptr(tok), _ptr(cont),
+                                          _ptr(lg) if lg is not None else None, self.ring._stream(stream))
+        self.ring._check(rc)
+        return tok, cont, lg
+
+    def dispose(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.mb_local_head_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.dispose()
+        except Exception:
+            pass
+
+
+def argmax_penalty(logits: torch.Tensor, seen: torch.Tensor, penalty: float, stream=None) -> torch.Tensor:
+    """ARGMAX_PENALTY (kernels-decode.ts:428-485) on the device: per row of
+    logits [n][codes] fp32, the penalised argmax under seen [n][codes/32] (int32
+    words holding the mask bits), whose bit is then set in place.  Returns the
+    ids [n] int32."""
+    lib = _lib.load()
+    if not (logits.is_cuda and logits.dtype == torch.float32 and logits.is_contiguous() and logits.dim() == 2):
+        raise TypeError("logits must be a contiguous 2-D CUDA float32 tensor")
+    n, codes = logits.shape
+    if not (seen.is_cuda and seen.dtype == torch.int32 and seen.is_contiguous() and seen.shape == (n, codes // 32)):
+        raise TypeError("seen must be a contiguous CUDA int32 tensor [n][codes/32]")
+    out = torch.empty(n, dtype=torch.int32, device=logits.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(logits.device)
+    with torch.cuda.device(logits.device):
+        rc = lib.mb_argmax_penalty(n, codes, _ptr(logits), _ptr(seen), penalty, _ptr(out),
+                                   ctypes.c_void_p(stream.cuda_stream))
+    if rc:
+        raise MockbirdError(rc, "mb_argmax_penalty: bad arguments or launch failure")
+    return out

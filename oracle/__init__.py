@@ -237,3 +237,96 @@ def decoder_step(ring: "Ring", weights: np.ndarray, ffn: int, streams, positions
         a = (0.5 * a * (1 + np.tanh(0.7978845608028654 * (a + 0.044715 * a * a * a)))).astype(np.float32)
         x = x + gemm(a, wo, bo)
     return ln(x, take(h), take(h))
+
+
+# ---------------------------------------------------------------- local head
+
+def argmax_penalty(logits: np.ndarray, seen_words: np.ndarray, penalty: float) -> int:
+    """Greedy pick with the repetition penalty for one row of logits.
+
+    ARGMAX_PENALTY (src/lib/tts/engine/kernels-decode.ts:428-485) and
+    argmaxPenalty (tools/onnx-probe/ref-decode.mjs:273-284): a logit s whose id
+    has its bit set in `seen_words` (bit j of word j/32) becomes s / penalty when
+    s >= 0 and s * penalty when s < 0 (fp32 arithmetic); the scan starts from
+    (-1e30, id 0) and keeps the first id of a strictly larger value, so ties go
+    to the lowest id and NaNs never win."""
+    s = np.array(logits, np.float32, copy=True)
+    bits = ((np.asarray(seen_words, np.uint32)[np.arange(s.size) >> 5] >> (np.arange(s.size) & 31)) & 1) != 0
+    p = np.float32(penalty)
+    pos = bits & (s >= 0)
+    neg = bits & (s < 0)
+    s[pos] = s[pos] / p
+    s[neg] = s[neg] * p
+    best, idx = np.float32(-1e30), 0
+    valid = ~np.isnan(s)
+    if valid.any():
+        m = s[valid].max()
+        if m > best:
+            idx = int(np.flatnonzero(s == m)[0])
+    return idx
+
+
+def local_weight_count(hidden: int, ffn: int, codes: int, channels: int) -> int:
+    """Length of the local head's fp32 weight array (one layer + ln_f, wte_slot,
+    the two text-head columns, channels-1 audio embeddings, channels audio heads)."""
+    h, f = hidden, ffn
+    layer = 2 * h + h * 3 * h + 3 * h + h * h + h + 2 * h + h * f + f + f * h + h + 2 * h
+    return layer + h + 2 * h + (channels - 1) * codes * h + channels * h * codes
+
+
+def local_frame(ring: "Ring", weights: np.ndarray, ffn: int, codes: int, channels: int, penalty: float,
+                streams, hidden: np.ndarray, seen: np.ndarray, forced=None):
+    """One frame of the local head for n streams (DecodeRunner.nextFrame,
+    src/lib/tts/engine/decode.ts:788-939; CPU form ref-decode.mjs:236-283 and
+    :380-410), with the rounding points of the CUDA path: the layer as in
+    `decoder_step` (bf16 GEMMs), ln_f rounded to bf16 before the bf16 audio-head
+    GEMM (no bias), the text-head decision in fp32 columns.
+
+    `ring`: one layer, capacity >= channels + 1.  `seen` [ring streams][channels]
+    [codes/32] uint32 is updated in place.  `forced` [n][channels]: tokens that
+    drive the chain (embedding and seen bits) instead of this oracle's own picks,
+    so that a kernel's picks can be followed step by step.
+    Returns (tokens [n][channels] int32 -- this oracle's own picks, cont [n] int32,
+    logits [n][channels][codes] fp32 before the penalty, decide [n][2] fp64 --
+    the audio_end and assistant_slot dot products)."""
+    h = ring.heads * HD
+    w = np.asarray(weights, np.float32)
+    nd = local_weight_count(h, ffn, codes, channels) - (h + 2 * h + (channels - 1) * codes * h
+                                                        + channels * h * codes)
+    off = nd
+    wte_slot = w[off:off + h]
+    off += h
+    cols = w[off:off + 2 * h].reshape(2, h)
+    off += 2 * h
+    emb = w[off:off + (channels - 1) * codes * h].reshape(channels - 1, codes, h)
+    off += (channels - 1) * codes * h
+    heads = round_to("bf16", w[off:off + channels * h * codes]).reshape(channels, h, codes)
+    streams = np.asarray(streams, np.int64)
+    n = len(streams)
+    tokens = np.zeros((n, channels), np.int32)
+    used = np.zeros((n, channels), np.int32)
+    cont = np.zeros(n, np.int32)
+    logits = np.zeros((n, channels, codes), np.float32)
+    decide = np.zeros((n, 2), np.float64)
+    for step in range(channels + 1):
+        if step == 0:
+            x = np.array(hidden, np.float32, copy=True)
+        elif step == 1:
+            x = np.repeat(wte_slot[None, :], n, axis=0)
+        else:
+            x = emb[step - 2][used[:, step - 2]].copy()
+        hs = decoder_step(ring, w[:nd], ffn, streams, [step] * n, x)
+        if step == 0:
+            decide = hs.astype(np.float64) @ cols.T.astype(np.float64)
+            cont = (decide[:, 1] >= decide[:, 0]).astype(np.int32)
+            continue
+        ch = step - 1
+        lg = (round_to("bf16", hs).astype(np.float64) @ heads[ch].astype(np.float64)).astype(np.float32)
+        logits[:, ch] = lg
+        for i in range(n):
+            mask = seen[streams[i], ch]
+            tokens[i, ch] = argmax_penalty(lg[i], mask, penalty)
+            t = int(forced[i][ch]) if forced is not None else int(tokens[i, ch])
+            used[i, ch] = t
+            mask[t >> 5] |= np.uint32(1 << (t & 31))
+    return tokens, cont, logits, decide

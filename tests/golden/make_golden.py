@@ -29,6 +29,15 @@ kat_attention_n512.npz
       out      [768] f32   expected context
       skip     int         draws consumed before test 4
       k_sum, v_sum, q_sum  float64 sums of the inputs (regeneration check)
+
+kat_argmax_c1024.npz
+    The known answer of kernels.test.mjs test 5 ("argmax over 1024 logits (tie ->
+    lowest id)", :379-436): 1024 logits drawn from the same stream right after
+    test 4's inputs; the expected id is the test's own JavaScript scan (first id
+    of a strictly larger value), restated below in plain Python.
+      best     int         expected id
+      skip     int         draws consumed before test 5
+      logits_sum           float64 sum of the logits (regeneration check)
 """
 from __future__ import annotations
 
@@ -78,6 +87,19 @@ def kat_expected(k, v, q):
     return out.reshape(-1).astype(np.float32)
 
 
+def kat_argmax():
+    """kernels.test.mjs:381-386: logits[i] = rnd(); best = first id of the max."""
+    skip = SKIP_BEFORE_TEST4 + 2 * N_KAT * H * HD + H * HD
+    rnd = oracle.xorshift32_stream(0x2F6E2B1)
+    rnd(skip, keep=False)
+    logits = rnd(1024)
+    best = 0
+    for i in range(1, 1024):
+        if logits[i] > logits[best]:
+            best = i
+    return logits, best, skip
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference tree")
@@ -100,7 +122,11 @@ def main():
     np.savez_compressed(os.path.join(HERE, "kat_attention_n512.npz"), out=out, skip=np.array(SKIP_BEFORE_TEST4),
                         k_sum=np.array(k.astype(np.float64).sum()), v_sum=np.array(v.astype(np.float64).sum()),
                         q_sum=np.array(q.astype(np.float64).sum()))
-    print("wrote layer0_kv.npz (rows %d, k8_equal=%s) and kat_attention_n512.npz" % (len(rows), k8_equal))
+    logits, best, skip = kat_argmax()
+    np.savez_compressed(os.path.join(HERE, "kat_argmax_c1024.npz"), best=np.array(best), skip=np.array(skip),
+                        logits_sum=np.array(logits.astype(np.float64).sum()))
+    print("wrote layer0_kv.npz (rows %d, k8_equal=%s), kat_attention_n512.npz and kat_argmax_c1024.npz (best %d)"
+          % (len(rows), k8_equal, best))
 
 
 if __name__ == "__main__":

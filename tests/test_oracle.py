@@ -210,3 +210,62 @@ def test_storage_rounding_matches_numpy():
     u = x.view(np.uint32).astype(np.uint64)
     bf = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint32) << 16
     assert np.array_equal(oracle.round_to("bf16", x), bf.astype(np.uint32).view(np.float32))
+
+
+# ---------------------------------------------------------------- local head (ARGMAX_PENALTY, nextFrame)
+
+def test_kat_argmax_c1024_oracle():
+    """kernels.test.mjs test 5: the id of the maximum of 1024 xorshift32 logits."""
+    kat = np.load(os.path.join(os.path.dirname(__file__), "golden", "kat_argmax_c1024.npz"))
+    rnd = oracle.xorshift32_stream(0x2F6E2B1)
+    rnd(int(kat["skip"]), keep=False)
+    logits = rnd(1024)
+    assert abs(logits.astype(np.float64).sum() - float(kat["logits_sum"])) < 1e-9
+    assert oracle.argmax_penalty(logits, np.zeros(32, np.uint32), 1.0) == int(kat["best"])
+    # with its own bit set, the maximum is divided by 1.2 and the runner-up may win
+    seen = np.zeros(32, np.uint32)
+    seen[int(kat["best"]) >> 5] = np.uint32(1 << (int(kat["best"]) & 31))
+    pen = logits.copy()
+    pen[int(kat["best"])] = pen[int(kat["best"])] / np.float32(1.2)
+    assert oracle.argmax_penalty(logits, seen, 1.2) == int(np.argmax(pen))
+
+
+def test_oracle_local_frame_penalty_dynamics():
+    """A small local head whose picks are known in advance: ln_f gain 0.01 and bias
+    u make every step's output ~u; heads 0..1 favour id 3 (10 u/h) over id 7
+    (9 u/h), so a channel picks 3, 7 (10/1.2 < 9), 3, 3; head 2 has all-negative
+    logits -10 (1 + 0.01 j), so frame f picks j = f.  Stream 1 is cleared before
+    frame 2 and starts over."""
+    h, ffn, codes, channels = 64, 64, 64, 3
+    rng = np.random.default_rng(0)
+    n = oracle.local_weight_count(h, ffn, codes, channels)
+    w = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    per = 2 * h + h * 3 * h + 3 * h + h * h + h + 2 * h + h * ffn + ffn + ffn * h + h
+    w[0:h] = 1.0
+    w[2 * h + 3 * h * h + 3 * h + h * h + h: 2 * h + 3 * h * h + 3 * h + h * h + 2 * h] = 1.0
+    u = np.where(rng.standard_normal(h) >= 0, 1.0, -1.0).astype(np.float32)
+    w[per:per + h] = 0.01
+    w[per + h:per + 2 * h] = u
+    off = per + 2 * h + h
+    w[off:off + h] = -u / h
+    w[off + h:off + 2 * h] = u / h
+    off += 2 * h + (channels - 1) * codes * h
+    heads = (rng.standard_normal((channels, h, codes)) * 1e-4).astype(np.float32)
+    heads[:channels - 1, :, 3] = 10.0 * u / h
+    heads[:channels - 1, :, 7] = 9.0 * u / h
+    heads[channels - 1] = -10.0 * (1.0 + 0.01 * np.arange(codes))[None, :] * u[:, None] / h
+    w[off:] = heads.reshape(-1)
+    S = 2
+    ring = oracle.Ring(layers=1, streams=S, heads=1, capacity=channels + 1, dtype="f32", wrap=False,
+                       max_position=channels + 1)
+    seen = np.zeros((S, channels, codes // 32), np.uint32)
+    x = rng.standard_normal((S, h)).astype(np.float32)
+    pattern = [3, 7, 3, 3]
+    for frame in range(4):
+        if frame == 2:
+            seen[1] = 0
+        tok, cont, _, _ = oracle.local_frame(ring, w, ffn, codes, channels, 1.2, [0, 1], x, seen)
+        assert cont.tolist() == [1, 1]
+        for s in range(S):
+            f = frame - 2 if (s == 1 and frame >= 2) else frame
+            assert tok[s].tolist() == [pattern[f]] * (channels - 1) + [f], (frame, s)
