@@ -160,24 +160,30 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     T* kbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD;
     T* vbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD;
 
+    // The K and V chunk go in flight first: the issuing thread initialised the
+    // barriers itself; the others meet them only after the barrier below.  In
+    // the chunk holding the new slot the copies skip that row (rows [0, jn) and
+    // (jn, rows)): the appending threads write it into shared memory themselves,
+    // so it never races the ring store of the same row.
+    const int jn = has_new ? newslot - j0 : -1;  // chunk row of the new slot, or none
     if (tid == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
         fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t bytes = (uint32_t)rows * RB;
+        const uint32_t bytes = (uint32_t)(has_new ? rows - 1 : rows) * RB;
+        const int a = has_new ? jn : rows;          // first segment [0, a)
+        const int b = has_new ? jn + 1 : rows;      // second segment [b, rows)
         mbar_expect_tx(&bar[0], bytes);
-        bulk_g2s(sk, kbase + (size_t)j0 * HD, bytes, &bar[0]);
+        if (a > 0) bulk_g2s(sk, kbase + (size_t)j0 * HD, (uint32_t)a * RB, &bar[0]);
+        if (b < rows) bulk_g2s(sk + b * RB, kbase + (size_t)(j0 + b) * HD, (uint32_t)(rows - b) * RB, &bar[0]);
         mbar_expect_tx(&bar[1], bytes);
-        bulk_g2s(sv, vbase + (size_t)j0 * HD, bytes, &bar[1]);
+        if (a > 0) bulk_g2s(sv, vbase + (size_t)j0 * HD, (uint32_t)a * RB, &bar[1]);
+        if (b < rows) bulk_g2s(sv + b * RB, vbase + (size_t)(j0 + b) * HD, (uint32_t)(rows - b) * RB, &bar[1]);
     }
 
     // query (roped here when appending) and, in the chunk holding the new slot,
-    // the new K/V row: written to the ring and kept for the on-chip substitution
+    // the new K/V row: written to the ring and to its row of the staged chunk
     const float* row = q_in + (size_t)item * q_stride;
-    float2 knew = make_float2(0.f, 0.f), vnew = make_float2(0.f, 0.f);
     if (tid < 32) {
         float2 qv = *reinterpret_cast<const float2*>(row + h * HD + 2 * tid);
         if (APPEND) qv = rope_pair(qv, r.rope[(size_t)pos * 32 + tid]);
@@ -190,8 +196,8 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         const float2 kr = rope_pair(kv, r.rope[(size_t)pos * 32 + i]);
         Store<T>::store2(kbase + (size_t)newslot * HD + 2 * i, kr);
         Store<T>::store2(vbase + (size_t)newslot * HD + 2 * i, vv);
-        knew = Store<T>::round2(kr);
-        vnew = Store<T>::round2(vv);
+        Store<T>::store2(reinterpret_cast<T*>(sk + jn * RB) + 2 * i, kr);
+        Store<T>::store2(reinterpret_cast<T*>(sv + jn * RB) + 2 * i, vv);
     }
     if (has_new && h == 0 && tid == 64) r.slot_pos[(size_t)s * C + newslot] = pos;
 
@@ -204,17 +210,12 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         live = stored >= 0 && pos - stored >= 0 && pos - stored < C;
     }
 
-    // ---- K chunk landed?  (bounded; a copy that never lands reads as an empty chunk)
-    bool ok = __syncthreads_and(mbar_wait(&bar[0], 0, WAIT_LIMIT));
-    if (!ok) {
-        if (tid == 0) atomicOr(r.err, DERR_TIMEOUT);
-        live = false;
-    }
-    if (ok && has_new && tid >= 32 && tid < 64) {
-        T* dst = reinterpret_cast<T*>(sk + (newslot - j0) * RB) + 2 * (tid - 32);
-        Store<T>::store2(dst, knew);
-    }
-    __syncthreads();
+    __syncthreads();  // barriers initialised; qs and the new row written
+
+    // ---- K chunk landed?  Each thread waits for itself (bounded; a copy that
+    // never lands reads as an empty chunk, and the CTA agrees on that below)
+    bool ok = mbar_wait(&bar[0], 0, WAIT_LIMIT);
+    if (!ok) live = false;
 
     // ---- scores: slot rr, 128 bytes per thread, 16-byte vectors read in a
     // per-slot rotated order so the 8 threads of a shared-memory phase hit 8
@@ -246,7 +247,11 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) wmax[warp] = m;
-    __syncthreads();
+    ok = __syncthreads_and(ok);
+    if (!ok) {
+        if (tid == 0) atomicOr(r.err, DERR_TIMEOUT);
+        live = false;
+    }
     m = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
     const float p = live ? exp2f(sc2 - m) : 0.f;
     if (part == 0 && rr < ROWS) ps[rr] = p;
@@ -255,14 +260,10 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
     if (lane == 0) wsum[warp] = l;
 
-    // ---- V chunk
-    ok = __syncthreads_and(mbar_wait(&bar[1], 0, WAIT_LIMIT)) && ok;
-    if (!ok && tid == 0) atomicOr(r.err, DERR_TIMEOUT);
-    if (ok && has_new && tid >= 32 && tid < 64) {
-        T* dst = reinterpret_cast<T*>(sv + (newslot - j0) * RB) + 2 * (tid - 32);
-        Store<T>::store2(dst, vnew);
-    }
-    __syncthreads();
+    // ---- V chunk (this barrier also publishes ps and wsum)
+    const bool okv = __syncthreads_and(mbar_wait(&bar[1], 0, WAIT_LIMIT));
+    if (ok && !okv && tid == 0) atomicOr(r.err, DERR_TIMEOUT);
+    ok = ok && okv;
     l = wsum[0] + wsum[1] + wsum[2] + wsum[3];
 
     // ---- P.V: warp w takes slots w, w+4, ...; lane owns dims 2*lane, 2*lane+1
