@@ -72,11 +72,11 @@ def window_bytes(L, esize, layers=12):
 
 
 # DRAM read + write per launch over the algorithmic bytes, from the full ncu capture
-# of the fp32 decode kernel (32 streams, full 512-slot windows: 101.05 MB read +
-# 4.0 MB written for 101.25 MB algorithmic; profiles/decode_kernel_f32_config2.md).
-# Traffic grows with the streams and the window, so a launch's traffic is its
-# algorithmic bytes times this ratio.
-DECODE_TRAFFIC_RATIO = {"f32": (101.05 + 4.0) / 101.25}
+# of the fp32 decode kernel (32 streams, full 512-slot windows: 100.85 MB read +
+# 5.84 MB written, mean of 3 launches, for 101.25 MB algorithmic;
+# profiles/decode_kernel_f32_config2.md).  Traffic grows with the streams and the
+# window, so a launch's traffic is its algorithmic bytes times this ratio.
+DECODE_TRAFFIC_RATIO = {"f32": (100.85 + 5.84) / 101.25}
 
 
 def peaks():
