@@ -190,14 +190,16 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         qs[2 * tid] = qv.x;
         qs[2 * tid + 1] = qv.y;
     } else if (has_new && tid < 64) {
-        const int i = tid - 32;
-        const float2 kv = *reinterpret_cast<const float2*>(row + HID + h * HD + 2 * i);
-        const float2 vv = *reinterpret_cast<const float2*>(row + 2 * HID + h * HD + 2 * i);
-        const float2 kr = rope_pair(kv, r.rope[(size_t)pos * 32 + i]);
-        Store<T>::store2(kbase + (size_t)newslot * HD + 2 * i, kr);
-        Store<T>::store2(vbase + (size_t)newslot * HD + 2 * i, vv);
-        Store<T>::store2(reinterpret_cast<T*>(sk + jn * RB) + 2 * i, kr);
-        Store<T>::store2(reinterpret_cast<T*>(sv + jn * RB) + 2 * i, vv);
+        if constexpr (APPEND) {  // has_new implies APPEND
+            const int i = tid - 32;
+            const float2 kv = *reinterpret_cast<const float2*>(row + HID + h * HD + 2 * i);
+            const float2 vv = *reinterpret_cast<const float2*>(row + 2 * HID + h * HD + 2 * i);
+            const float2 kr = rope_pair(kv, r.rope[(size_t)pos * 32 + i]);
+            Store<T>::store2(kbase + (size_t)newslot * HD + 2 * i, kr);
+            Store<T>::store2(vbase + (size_t)newslot * HD + 2 * i, vv);
+            Store<T>::store2(reinterpret_cast<T*>(sk + jn * RB) + 2 * i, kr);
+            Store<T>::store2(reinterpret_cast<T*>(sv + jn * RB) + 2 * i, vv);
+        }
     }
     if (has_new && h == 0 && tid == 64) r.slot_pos[(size_t)s * C + newslot] = pos;
 

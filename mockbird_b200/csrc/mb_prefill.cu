@@ -43,39 +43,60 @@ struct P2<__half> {
     __device__ static float2 rnd(float2 v) { return __half22float2(__floats2half2_rn(v.x, v.y)); }
 };
 
+// Four consecutive elements in the storage type from two pairs: one 16-byte
+// (fp32) or 8-byte (16-bit) store.
+template <typename T>
+__device__ __forceinline__ void st4(T* p, float2 a, float2 b) {
+    if constexpr (sizeof(T) == 4) {
+        *reinterpret_cast<float4*>(p) = make_float4(a.x, a.y, b.x, b.y);
+    } else {
+        T tmp[4];
+        P2<T>::st(tmp, a);
+        P2<T>::st(tmp + 2, b);
+        *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(tmp);
+    }
+}
+
 // ---------------------------------------------------------------- prefill
 
-// ROPE_SPLIT_CACHE for all rows of n items: grid (rows, n), one thread per (head,
-// pair).  K roped and V raw go to slot = row; the roped Q goes to the stage
+// ROPE_SPLIT_CACHE for all rows of n items: grid (ceil(rows / ROPE_ROWS), n),
+// heads * 16 threads, each owning 4 consecutive dims (two RoPE pairs) of one head
+// in ROPE_ROWS consecutive rows: 16-byte loads of q, k, v and the (cos, sin) pairs.
+// K roped and V raw go to slot = row; the roped Q goes to the stage
 // [n][heads][rows][64] (rounded to the storage dtype for 16-bit rings: the
-// attention kernel consumes Q in that type).  Row-0 blocks also mark the item's
-// slots >= rows empty: a prefill starts an utterance at position 0.
+// attention kernel consumes Q in that type).  Block 0 of an item also marks the
+// item's slots >= rows empty: a prefill starts an utterance at position 0.
+constexpr int ROPE_ROWS = 4;
+
 template <typename T>
-__global__ void __launch_bounds__(384) prefill_rope_kernel(RingView r, const int32_t* __restrict__ streams, int rows,
-                                                           const float* __restrict__ qkv, T* q_stage) {
-    const int row = blockIdx.x, item = blockIdx.y;
+__global__ void __launch_bounds__(1024) prefill_rope_kernel(RingView r, const int32_t* __restrict__ streams, int rows,
+                                                            const float* __restrict__ qkv, T* q_stage) {
+    const int item = blockIdx.y, r0 = blockIdx.x * ROPE_ROWS;
     const int s = streams[item];
     if (s < 0 || s >= r.streams) {
-        if (threadIdx.x == 0 && row == 0) atomicOr(r.err, DERR_STREAM);
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(r.err, DERR_STREAM);
         return;
     }
     const int H = r.heads, HID = H * HD, C = r.capacity;
-    const float* src = qkv + ((size_t)item * rows + row) * 3 * HID;
-    for (int t = threadIdx.x; t < H * 32; t += blockDim.x) {
-        const int h = t >> 5, i = t & 31;
-        const float2 cs = r.rope[(size_t)row * 32 + i];
-        const float2 q = rope_pair_p(*reinterpret_cast<const float2*>(src + h * HD + 2 * i), cs);
-        const float2 k = rope_pair_p(*reinterpret_cast<const float2*>(src + HID + h * HD + 2 * i), cs);
-        const float2 v = *reinterpret_cast<const float2*>(src + 2 * HID + h * HD + 2 * i);
-        P2<T>::st(q_stage + (((size_t)item * H + h) * rows + row) * HD + 2 * i, q);
-        T* kd = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD + (size_t)row * HD + 2 * i;
-        T* vd = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD + (size_t)row * HD + 2 * i;
-        P2<T>::st(kd, k);
-        P2<T>::st(vd, v);
+    const int t = threadIdx.x, h = t >> 4, d4 = (t & 15) * 4;  // head, first of 4 dims
+    const int rend = min(r0 + ROPE_ROWS, rows);
+    T* kbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD + d4;
+    T* vbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD + d4;
+    T* qbase = q_stage + ((size_t)item * H + h) * rows * HD + d4;
+    for (int row = r0; row < rend; row++) {
+        const float* src = qkv + ((size_t)item * rows + row) * 3 * HID + h * HD + d4;
+        const float4 cs = *reinterpret_cast<const float4*>(r.rope + (size_t)row * 32 + d4 / 2);
+        const float4 q = *reinterpret_cast<const float4*>(src);
+        const float4 k = *reinterpret_cast<const float4*>(src + HID);
+        const float4 v = *reinterpret_cast<const float4*>(src + 2 * HID);
+        const float2 c0 = make_float2(cs.x, cs.y), c1 = make_float2(cs.z, cs.w);
+        st4(qbase + (size_t)row * HD, rope_pair_p(make_float2(q.x, q.y), c0), rope_pair_p(make_float2(q.z, q.w), c1));
+        st4(kbase + (size_t)row * HD, rope_pair_p(make_float2(k.x, k.y), c0), rope_pair_p(make_float2(k.z, k.w), c1));
+        st4(vbase + (size_t)row * HD, make_float2(v.x, v.y), make_float2(v.z, v.w));
     }
-    if (threadIdx.x == 0) r.slot_pos[(size_t)s * C + row] = row;
-    if (row == 0)
-        for (int j = rows + threadIdx.x; j < C; j += blockDim.x) r.slot_pos[(size_t)s * C + j] = -1;
+    if (t < rend - r0) r.slot_pos[(size_t)s * C + r0 + t] = r0 + t;
+    if (blockIdx.x == 0)
+        for (int j = rows + t; j < C; j += blockDim.x) r.slot_pos[(size_t)s * C + j] = -1;
 }
 
 // Causal flash attention on CUDA cores for fp32 rings (kind::f16 tensor cores
@@ -165,7 +186,9 @@ size_t prefill_stage_bytes(int dtype, int n, int heads, int rows) {
 template <typename T>
 static cudaError_t prefill_t(const RingView& r, int n, const int32_t* streams, int rows, const float* qkv,
                              float* out, void* q_stage, cudaStream_t st) {
-    prefill_rope_kernel<T><<<dim3(rows, n), 384, 0, st>>>(r, streams, rows, qkv, reinterpret_cast<T*>(q_stage));
+    if (r.heads * 16 > 1024) return cudaErrorInvalidConfiguration;
+    prefill_rope_kernel<T><<<dim3((rows + ROPE_ROWS - 1) / ROPE_ROWS, n), r.heads * 16, 0, st>>>(
+        r, streams, rows, qkv, reinterpret_cast<T*>(q_stage));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if constexpr (sizeof(T) == 2)  // 16-bit rings: tensor cores (mb_prefill_tc.cu)

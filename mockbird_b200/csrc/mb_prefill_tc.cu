@@ -12,14 +12,19 @@
 //               tiles with no masked key skip the mask
 //   O_j = P V   tcgen05.mma, M=128 N=64 K=128 (V as an MN-major operand), TMEM cols [128,192)
 //   O = O*corr + O_j in registers
-// Q, K, V arrive by 3-D TMA tile loads (128-byte swizzle, zero fill past the last
-// row, no multicast).  K of tile j+1 is fetched as soon as the QK^T MMA of tile j
-// has consumed K, V of tile j+1 as soon as the PV MMA has consumed V.  (Issuing
-// S_{j+1} = Q K_{j+1}^T ahead, into a second TMEM buffer, was measured slower on
-// B200: it queues in front of PV_j on the tensor pipe.)  80 KB of
-// shared memory and 256 TMEM columns per CTA: two CTAs share an SM.  Every wait is
-// bounded; a CTA that gives up flags MB_ERR_TIMEOUT, waits (bounded) for its
-// copies and MMAs in flight, and frees its TMEM.
+// At the end O is normalised, staged in the free P buffers (128-byte swizzle)
+// and written by two TMA tile stores (rows past the last are clipped).
+// The tensor pipe runs the next tile's S behind the current PV: once the softmax
+// of tile j has read S_j and written P_j, one thread issues O_j = P_j V_j and then
+// S_{j+1} = Q K_{j+1}^T into the same TMEM columns, each with its own commit
+// barrier, so S_{j+1} is computed while the CTA reads O_j back.  (Issuing S_{j+1}
+// before the softmax of tile j, into a second TMEM buffer, was measured slower:
+// it queues in front of PV_j.)  Q, K, V arrive by 3-D TMA tile loads (128-byte
+// swizzle, zero fill past the last row, no multicast); K is double-buffered and
+// fetched two tiles ahead, V one tile ahead.  96 KB of shared memory and 256
+// TMEM columns per CTA: two CTAs share an SM.  Every wait is bounded; a CTA that
+// gives up flags MB_ERR_TIMEOUT, waits (bounded) for its copies and MMAs in
+// flight, and frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -38,11 +43,11 @@ constexpr int NTHREADS = 256;             // 8 warps: (TMEM lane quarter) x (col
 
 struct alignas(1024) TcSmem {
     unsigned char q[TILE];
-    unsigned char k[TILE];
+    unsigned char k[2][TILE];             // key tiles j (even j) and j (odd j)
     unsigned char v[TILE];
     unsigned char p[2][TILE];             // P: keys [0,64) and [64,128) as two K-major sub-tiles
     float rmax[2][BM];                    // per column half: row maxima, then row sums
-    uint64_t bar_q, bar_k, bar_v, bar_mma;
+    uint64_t bar_q, bar_k[2], bar_v, bar_s, bar_o;
     uint32_t tmem_base;
 };
 constexpr size_t SMEM_BYTES = sizeof(TcSmem) + 1024;  // + alignment slack of the dynamic base
@@ -64,10 +69,33 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// P = 2^(s - m) for this thread's 64 scores (ex2(-inf) = 0 keeps masked keys at
+// 0), packed to 16 bits into its row of the 128-byte-swizzled P sub-tile; adds
+// to the four partial row sums.  (Computing half of the exponentials on the FMA
+// pipe with a polynomial, to unload MUFU, was measured 1.7 % slower here.)
+template <bool BF16>
+__device__ __forceinline__ void softmax_pack(const float (&sv)[64], float m_new, unsigned char* sub, int row,
+                                             float& ls0, float& ls1, float& ls2, float& ls3) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ch++) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) pv[e] = ex2(sv[8 * ch + e] - m_new);
+        ls0 += pv[0] + pv[4];
+        ls1 += pv[1] + pv[5];
+        ls2 += pv[2] + pv[6];
+        ls3 += pv[3] + pv[7];
+        *reinterpret_cast<uint4*>(sub + ((ch ^ (row & 7)) << 4)) =
+            make_uint4(pack2<BF16>(pv[0], pv[1]), pack2<BF16>(pv[2], pv[3]), pack2<BF16>(pv[4], pv[5]),
+                       pack2<BF16>(pv[6], pv[7]));
+    }
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(NTHREADS, 2)
     prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
-                           RingView r, const int32_t* __restrict__ streams, int rows, float* __restrict__ out) {
+                           const __grid_constant__ CUtensorMap tout, RingView r, const int32_t* __restrict__ streams,
+                           int rows) {
     extern __shared__ unsigned char smem_raw[];
     TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -81,12 +109,15 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     if (warp == 0) tmem_alloc(&sm.tmem_base, TMEM_COLS);
     if (tid == 0) {
         mbar_init(&sm.bar_q, 1);
-        mbar_init(&sm.bar_k, 1);
+        mbar_init(&sm.bar_k[0], 1);
+        mbar_init(&sm.bar_k[1], 1);
         mbar_init(&sm.bar_v, 1);
-        mbar_init(&sm.bar_mma, 1);
+        mbar_init(&sm.bar_s, 1);
+        mbar_init(&sm.bar_o, 1);
         fence_mbar_init();
         prefetch_tmap(&tq);
         prefetch_tmap(&tkv);
+        prefetch_tmap(&tout);
     }
     tc_fence_before();
     __syncthreads();
@@ -94,12 +125,17 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     const uint32_t tbase = sm.tmem_base;
 
     // issue/complete counts per barrier (identical in every thread: the control flow is uniform)
-    int k_issued = 1, k_done = 0, v_issued = 1, v_done = 0, mma_issued = 0, mma_done = 0;
+    int k0_issued = 1, k1_issued = ntiles > 1 ? 1 : 0, k0_done = 0, k1_done = 0;  // per key buffer
+    int v_issued = 1, v_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
     if (tid == 0) {
         mbar_expect_tx(&sm.bar_q, TILE);
         tma_load_3d(sm.q, &tq, 0, q0, qplane, &sm.bar_q);
-        mbar_expect_tx(&sm.bar_k, TILE);
-        tma_load_3d(sm.k, &tkv, 0, 0, kplane, &sm.bar_k);
+        mbar_expect_tx(&sm.bar_k[0], TILE);
+        tma_load_3d(sm.k[0], &tkv, 0, 0, kplane, &sm.bar_k[0]);
+        if (ntiles > 1) {
+            mbar_expect_tx(&sm.bar_k[1], TILE);
+            tma_load_3d(sm.k[1], &tkv, 0, BN, kplane, &sm.bar_k[1]);
+        }
         mbar_expect_tx(&sm.bar_v, TILE);
         tma_load_3d(sm.v, &tkv, 0, 0, vplane, &sm.bar_v);
     }
@@ -117,32 +153,35 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     for (int d = 0; d < HD / 2; d++) o[d] = 0.f;
     float m_run = -INFINITY, l_half = 0.f;
 
-    bool ok = __syncthreads_and(mbar_wait(&sm.bar_q, 0, WAIT_LIMIT));
+    // S_0 = Q K_0^T
+    bool ok = __syncthreads_and(mbar_wait(&sm.bar_q, 0, WAIT_LIMIT) && mbar_wait(&sm.bar_k[0], 0, WAIT_LIMIT));
     bool q_done = ok;
-    for (int j = 0; j < ntiles && ok; j++) {
-        const int k0 = j * BN;
-        // ---- S = Q K^T
-        ok = __syncthreads_and(mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT));
-        if (!ok) break;
-        k_done++;
+    if (ok) {
+        k0_done++;
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t qa = smem_u32(sm.q), ka = smem_u32(sm.k);
+            const uint32_t qa = smem_u32(sm.q), ka = smem_u32(sm.k[0]);
 #pragma unroll
             for (int kk = 0; kk < HD / 16; kk++)
                 umma_f16(tbase + S_COL, sdesc_sw128(qa + 32 * kk, 16, 1024), sdesc_sw128(ka + 32 * kk, 16, 1024),
                          IDESC_QK, kk > 0);
-            umma_commit(&sm.bar_mma);
+            umma_commit(&sm.bar_s);
         }
-        mma_issued++;
-        ok = __syncthreads_and(mbar_wait(&sm.bar_mma, mma_done & 1, WAIT_LIMIT));
+        s_issued++;
+    }
+    for (int j = 0; j < ntiles && ok; j++) {
+        const int k0 = j * BN, kb_ = j & 1;
+        // ---- S_j landed in TMEM: its key buffer is free for tile j + 2
+        ok = __syncthreads_and(mbar_wait(&sm.bar_s, s_done & 1, WAIT_LIMIT));
         if (!ok) break;
-        mma_done++;
-        if (tid == 0 && j + 1 < ntiles) {  // K consumed: fetch the next tile's keys
-            mbar_expect_tx(&sm.bar_k, TILE);
-            tma_load_3d(sm.k, &tkv, 0, k0 + BN, kplane, &sm.bar_k);
+        s_done++;
+        if (j + 2 < ntiles) {
+            if (tid == 0) {
+                mbar_expect_tx(&sm.bar_k[kb_], TILE);
+                tma_load_3d(sm.k[kb_], &tkv, 0, k0 + 2 * BN, kplane, &sm.bar_k[kb_]);
+            }
+            if (kb_) k1_issued++; else k0_issued++;
         }
-        if (j + 1 < ntiles) k_issued++;
         tc_fence_after();
 
         // ---- this thread's 64 scores (keys k0 + 64*half ..), kept in registers
@@ -163,14 +202,14 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                 mx2 = fmaxf(mx2, sv[i + 2]);
                 mx3 = fmaxf(mx3, sv[i + 3]);
             }
-        } else {  // causal mask key <= query, and keys < rows
-#pragma unroll
-            for (int i = 0; i < 64; i++) {
-                const int key = kb + i;
-                sv[i] = (key <= qg && key < rows) ? sv[i] * scale : -INFINITY;
-            }
+        } else {  // causal mask key <= query, and keys < rows: keys kb + i live iff i <= lim
+            const int lim = min(qg, rows - 1) - kb;
 #pragma unroll
             for (int i = 0; i < 64; i += 4) {
+                sv[i] = i <= lim ? sv[i] * scale : -INFINITY;
+                sv[i + 1] = i + 1 <= lim ? sv[i + 1] * scale : -INFINITY;
+                sv[i + 2] = i + 2 <= lim ? sv[i + 2] * scale : -INFINITY;
+                sv[i + 3] = i + 3 <= lim ? sv[i + 3] * scale : -INFINITY;
                 mx0 = fmaxf(mx0, sv[i]);
                 mx1 = fmaxf(mx1, sv[i + 1]);
                 mx2 = fmaxf(mx2, sv[i + 2]);
@@ -184,28 +223,22 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         const float corr = ex2(m_run - m_new);      // 0 on the first tile (m_run = -inf)
         float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
         unsigned char* sub = sm.p[half] + row * 128;  // this half's 64 keys = P sub-tile `half`
-#pragma unroll
-        for (int ch = 0; ch < 8; ch++) {
-            const float p0 = ex2(sv[8 * ch + 0] - m_new), p1 = ex2(sv[8 * ch + 1] - m_new);
-            const float p2 = ex2(sv[8 * ch + 2] - m_new), p3 = ex2(sv[8 * ch + 3] - m_new);
-            const float p4 = ex2(sv[8 * ch + 4] - m_new), p5 = ex2(sv[8 * ch + 5] - m_new);
-            const float p6 = ex2(sv[8 * ch + 6] - m_new), p7 = ex2(sv[8 * ch + 7] - m_new);
-            ls0 += p0 + p4;
-            ls1 += p1 + p5;
-            ls2 += p2 + p6;
-            ls3 += p3 + p7;
-            *reinterpret_cast<uint4*>(sub + ((ch ^ (row & 7)) << 4)) =
-                make_uint4(pack2<BF16>(p0, p1), pack2<BF16>(p2, p3), pack2<BF16>(p4, p5), pack2<BF16>(p6, p7));
-        }
+        softmax_pack<BF16>(sv, m_new, sub, row, ls0, ls1, ls2, ls3);
         l_half = l_half * corr + ((ls0 + ls1) + (ls2 + ls3));
         m_run = m_new;
         fence_async_smem();
         tc_fence_before();
 
-        // ---- O_j = P V
-        ok = __syncthreads_and(mbar_wait(&sm.bar_v, v_done & 1, WAIT_LIMIT));
+        // ---- O_j = P_j V_j, then S_{j+1} = Q K_{j+1}^T behind it on the tensor pipe
+        const bool more = j + 1 < ntiles;
+        const int next_done = kb_ ? k0_done : k1_done;  // completions so far of tile j+1's key buffer
+        ok = __syncthreads_and(mbar_wait(&sm.bar_v, v_done & 1, WAIT_LIMIT) &&
+                               (!more || mbar_wait(&sm.bar_k[kb_ ^ 1], next_done & 1, WAIT_LIMIT)));
         if (!ok) break;
         v_done++;
+        if (more) {
+            if (kb_) k0_done++; else k1_done++;
+        }
         if (tid == 0) {
             tc_fence_after();
             const uint32_t pa = smem_u32(sm.p[0]), pb = smem_u32(sm.p[1]), va = smem_u32(sm.v);
@@ -213,17 +246,28 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             for (int kk = 0; kk < BN / 16; kk++)
                 umma_f16(tbase + O_COL, sdesc_sw128((kk < 4 ? pa : pb) + 32 * (kk & 3), 16, 1024),
                          sdesc_sw128(va + 2048 * kk, TILE, 1024), IDESC_PV, kk > 0);
-            umma_commit(&sm.bar_mma);
+            umma_commit(&sm.bar_o);
+            if (more) {
+                const uint32_t qa = smem_u32(sm.q), ka = smem_u32(sm.k[kb_ ^ 1]);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; kk++)
+                    umma_f16(tbase + S_COL, sdesc_sw128(qa + 32 * kk, 16, 1024),
+                             sdesc_sw128(ka + 32 * kk, 16, 1024), IDESC_QK, kk > 0);
+                umma_commit(&sm.bar_s);
+            }
         }
-        mma_issued++;
-        ok = __syncthreads_and(mbar_wait(&sm.bar_mma, mma_done & 1, WAIT_LIMIT));
+        o_issued++;
+        if (more) s_issued++;
+        ok = __syncthreads_and(mbar_wait(&sm.bar_o, o_done & 1, WAIT_LIMIT));
         if (!ok) break;
-        mma_done++;
-        if (tid == 0 && j + 1 < ntiles) {  // V consumed: fetch the next tile's values
-            mbar_expect_tx(&sm.bar_v, TILE);
-            tma_load_3d(sm.v, &tkv, 0, k0 + BN, vplane, &sm.bar_v);
+        o_done++;
+        if (more) {  // V consumed: fetch the next tile's values
+            if (tid == 0) {
+                mbar_expect_tx(&sm.bar_v, TILE);
+                tma_load_3d(sm.v, &tkv, 0, k0 + BN, vplane, &sm.bar_v);
+            }
+            v_issued++;
         }
-        if (j + 1 < ntiles) v_issued++;
         tc_fence_after();
         {
             float v[32];
@@ -231,29 +275,38 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 #pragma unroll
             for (int i = 0; i < 32; i++) o[i] = fmaf(o[i], corr, v[i]);
         }
-        tc_fence_before();
-        __syncthreads();  // S, the O tile and P are free for the next tile
+        tc_fence_before();  // the next barrier orders this O read before PV_{j+1} overwrites it
     }
 
     if (ok) {
+        // normalise, stage the O tile in the (now free) P buffers -- half `half`
+        // of the 64 output dims in sub-tile `half`, 128-byte swizzled -- and store
+        // it with two TMA tile stores (rows past `rows` are clipped by the map)
         sm.rmax[half][row] = l_half;  // exchange the two halves' sums
         __syncthreads();
-        if (qg < rows) {
-            const float inv = 1.f / (sm.rmax[0][row] + sm.rmax[1][row]);
-            float* dst = out + ((size_t)item * rows + qg) * H * HD + h * HD + 32 * half;
+        const float inv = 1.f / (sm.rmax[0][row] + sm.rmax[1][row]);
+        unsigned char* dsub = sm.p[half] + row * 128;
 #pragma unroll
-            for (int d = 0; d < 32; d += 4)
-                *reinterpret_cast<float4*>(dst + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv,
-                                                                  o[d + 3] * inv);
+        for (int c = 0; c < 8; c++)
+            *reinterpret_cast<float4*>(dsub + ((c ^ (row & 7)) << 4)) =
+                make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tma_store_3d(&tout, sm.p[0], h * HD, q0, item);
+            tma_store_3d(&tout, sm.p[1], h * HD + 32, q0, item);
+            bulk_store_drain();
         }
     } else if (tid == 0) {
         // gave up: record it, then let everything in flight land before the
         // shared memory and TMEM of this CTA are released
         atomicOr(r.err, DERR_TIMEOUT);
         if (!q_done) mbar_wait(&sm.bar_q, 0, WAIT_LIMIT);
-        for (; k_done < k_issued; k_done++) mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT);
+        for (; k0_done < k0_issued; k0_done++) mbar_wait(&sm.bar_k[0], k0_done & 1, WAIT_LIMIT);
+        for (; k1_done < k1_issued; k1_done++) mbar_wait(&sm.bar_k[1], k1_done & 1, WAIT_LIMIT);
         for (; v_done < v_issued; v_done++) mbar_wait(&sm.bar_v, v_done & 1, WAIT_LIMIT);
-        for (; mma_done < mma_issued; mma_done++) mbar_wait(&sm.bar_mma, mma_done & 1, WAIT_LIMIT);
+        for (; s_done < s_issued; s_done++) mbar_wait(&sm.bar_s, s_done & 1, WAIT_LIMIT);
+        for (; o_done < o_issued; o_done++) mbar_wait(&sm.bar_o, o_done & 1, WAIT_LIMIT);
     }
     tc_fence_before();
     __syncthreads();
@@ -293,12 +346,27 @@ bool make_map(CUtensorMap* m, bool bf16, const void* base, int rows, int planes,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D map over the fp32 output [items][rows][heads*64]: box 32 dims x 128 rows
+// (128 bytes wide, the 128-byte swizzle span), one item.
+bool make_out_map(CUtensorMap* m, float* out, int rows, int n, int width) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)width, (cuuint64_t)rows, (cuuint64_t)n};
+    cuuint64_t strides[2] = {(cuuint64_t)width * 4, (cuuint64_t)rows * width * 4};
+    cuuint32_t box[3] = {32, (cuuint32_t)BM, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <bool BF16>
 cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows, const void* q_stage, float* out,
                       cudaStream_t st) {
-    CUtensorMap tq, tkv;
+    CUtensorMap tq, tkv, tout;
     if (!make_map(&tq, BF16, q_stage, rows, n * r.heads, (size_t)rows * HD * 2) ||
-        !make_map(&tkv, BF16, r.kv, rows, r.streams * 2 * r.heads, (size_t)r.capacity * HD * 2))
+        !make_map(&tkv, BF16, r.kv, rows, r.streams * 2 * r.heads, (size_t)r.capacity * HD * 2) ||
+        !make_out_map(&tout, out, rows, n, r.heads * HD))
         return cudaErrorInvalidValue;
     static bool attr_set[64] = {};  // per device
     int dev = 0;
@@ -312,7 +380,7 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
         attr_set[dev] = true;
     }
     dim3 grid((rows + BM - 1) / BM, r.heads, n);
-    prefill_attn_tc_kernel<BF16><<<grid, NTHREADS, SMEM_BYTES, st>>>(tq, tkv, r, streams, rows, out);
+    prefill_attn_tc_kernel<BF16><<<grid, NTHREADS, SMEM_BYTES, st>>>(tq, tkv, tout, r, streams, rows);
     return cudaGetLastError();
 }
 

@@ -67,6 +67,23 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// 3-D tiled store of this CTA's shared memory `src` to `tmap` at (c0, c1, c2),
+// in the bulk async-group of the issuing thread.  c0 * element size must be a
+// multiple of 16 bytes and no coordinate may be negative; rows past the map's
+// extent are clipped.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+                 ::"l"(tmap), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
+// Close the issuing thread's bulk async-group, then wait until every store in
+// it has finished reading shared memory (so the CTA may release it).
+__device__ __forceinline__ void bulk_store_drain() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05 (5th-gen tensor cores, TMEM)
 
 // Allocate `ncols` TMEM columns (power of two >= 32) for this CTA; the base
