@@ -199,6 +199,17 @@ MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
         return bail(MB_ERR_OOM);
     if (cudaMalloc(&c->d_out, (size_t)cfg.layers * cfg.max_batch * hid * sizeof(float)) != cudaSuccess)
         return bail(MB_ERR_OOM);
+    if (cudaStreamCreateWithFlags(&c->cp_in, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->cp_out, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) != cudaSuccess)
+        return bail(MB_ERR_CUDA);
+    c->ev_in.assign(cfg.layers, nullptr);
+    c->ev_done.assign(cfg.layers, nullptr);
+    for (int l = 0; l < cfg.layers; l++)
+        if (cudaEventCreateWithFlags(&c->ev_in[l], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_done[l], cudaEventDisableTiming) != cudaSuccess)
+            return bail(MB_ERR_CUDA);
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(MB_ERR_CUDA);
     *out = c;
     return MB_OK;
@@ -212,6 +223,13 @@ MB_API int mb_destroy(mb_ctx* c) {
                         c->d_streams, c->d_positions, c->d_qkv, c->d_out};
         for (void* p : ptrs)
             if (p) cudaFree(p);
+        for (auto* evs : {&c->ev_in, &c->ev_done})
+            for (cudaEvent_t e : *evs)
+                if (e) cudaEventDestroy(e);
+        if (c->ev_start) cudaEventDestroy(c->ev_start);
+        if (c->ev_end) cudaEventDestroy(c->ev_end);
+        if (c->cp_in) cudaStreamDestroy(c->cp_in);
+        if (c->cp_out) cudaStreamDestroy(c->cp_out);
     }
     delete c;
     return MB_OK;
@@ -340,14 +358,36 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
     DeviceGuard g(c->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     const size_t hid = (size_t)c->cfg.heads * HD, L = c->cfg.layers;
-    CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy streams");
-    CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy positions");
-    CK(cudaMemcpyAsync(c->d_qkv, qkv, L * n * 3 * hid * sizeof(float), cudaMemcpyHostToDevice, st), "copy qkv");
-    for (int layer = 0; layer < (int)L; layer++)
-        CK(run_decode(c, true, layer, n, c->d_streams, c->d_positions, c->d_qkv + (size_t)layer * n * 3 * hid,
-                      3 * (int)hid, c->d_out + (size_t)layer * n * hid, st, layer > 0),
+    const size_t in_l = (size_t)n * 3 * hid, out_l = (size_t)n * hid;  // floats per layer
+    // Per layer: its qkv rows copied in on cp_in, its decode on `st` once they
+    // have landed, its context rows copied out on cp_out once it is done; the
+    // copies of one layer overlap the decode of the others.  Both copy streams
+    // start behind the work already queued on `st`, and `st` ends behind them.
+    CK(cudaEventRecord(c->ev_start, st), "order copies");
+    CK(cudaStreamWaitEvent(c->cp_in, c->ev_start, 0), "order copies");
+    CK(cudaStreamWaitEvent(c->cp_out, c->ev_start, 0), "order copies");
+    CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->cp_in), "copy streams");
+    CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->cp_in),
+       "copy positions");
+    for (size_t l = 0; l < L; l++) {
+        CK(cudaMemcpyAsync(c->d_qkv + l * in_l, qkv + l * in_l, in_l * sizeof(float), cudaMemcpyHostToDevice,
+                           c->cp_in),
+           "copy qkv");
+        CK(cudaEventRecord(c->ev_in[l], c->cp_in), "copy qkv");
+    }
+    for (size_t l = 0; l < L; l++) {
+        CK(cudaStreamWaitEvent(st, c->ev_in[l], 0), "wait qkv");
+        CK(run_decode(c, true, (int)l, n, c->d_streams, c->d_positions, c->d_qkv + l * in_l, 3 * (int)hid,
+                      c->d_out + l * out_l, st, l > 0),
            "append_attend launch");
-    CK(cudaMemcpyAsync(out, c->d_out, L * n * hid * sizeof(float), cudaMemcpyDeviceToHost, st), "copy out");
+        CK(cudaEventRecord(c->ev_done[l], st), "layer done");
+        CK(cudaStreamWaitEvent(c->cp_out, c->ev_done[l], 0), "wait layer");
+        CK(cudaMemcpyAsync(out + l * out_l, c->d_out + l * out_l, out_l * sizeof(float), cudaMemcpyDeviceToHost,
+                           c->cp_out),
+           "copy out");
+    }
+    CK(cudaEventRecord(c->ev_end, c->cp_out), "copies done");
+    CK(cudaStreamWaitEvent(st, c->ev_end, 0), "copies done");
     return mb_sync(c, cuda_stream);
 }
 

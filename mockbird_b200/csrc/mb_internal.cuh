@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "mockbird_kv.h"
 
@@ -56,6 +57,11 @@ struct mb_ctx {
     int32_t* d_positions = nullptr;
     float* d_qkv = nullptr;   // [layers][max_batch][3*H*64]
     float* d_out = nullptr;   // [layers][max_batch][H*64]
+    // mb_decode_step_host's copy pipeline: inputs in and outputs out per layer on
+    // their own streams, so that the copies overlap the decode of other layers
+    cudaStream_t cp_in = nullptr, cp_out = nullptr;
+    std::vector<cudaEvent_t> ev_in, ev_done;  // per layer: inputs landed / layer decoded
+    cudaEvent_t ev_start = nullptr, ev_end = nullptr;
     bool persistent = false;  // decode with the persistent stream-K kernel (when it applies) instead
     std::string last_error;
 };
