@@ -129,11 +129,20 @@ struct DecodeShape {
 // grid (max_splits, heads, n), 128 threads.  APPEND: q_in is the raw qkv row
 // (stride q_stride) and this launch also appends K/V; otherwise q_in holds an
 // already-roped query.
+// One context value of the output row: fp32, or bf16 when the caller feeds it
+// straight into a bf16 GEMM (the decoder step).
+__device__ __forceinline__ void store_ctx(void* out, bool bf16, size_t i, float v) {
+    if (bf16)
+        reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else
+        reinterpret_cast<float*>(out)[i] = v;
+}
+
 template <typename T, bool APPEND>
 __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, const int32_t* __restrict__ streams,
                                                      const int32_t* __restrict__ positions,
-                                                     const float* __restrict__ q_in, int q_stride,
-                                                     float* __restrict__ out) {
+                                                     const float* __restrict__ q_in, int q_stride, void* out,
+                                                     int out_bf16) {
     using S = DecodeShape<T>;
     constexpr int ROWS = S::ROWS, TPR = S::TPR, RB = S::ROW_BYTES;
     __shared__ __align__(128) unsigned char sk[ROWS * RB];
@@ -290,9 +299,9 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     // never reaches further back than one kernel.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    float* dst = out + (size_t)item * HID + h * HD;
+    const size_t dst = (size_t)item * HID + h * HD;
     if (nsplit == 1) {
-        if (tid < HD) dst[tid] = l > 0.f ? acc / l : 0.f;
+        if (tid < HD) store_ctx(out, out_bf16, dst + tid, l > 0.f ? acc / l : 0.f);
         return;
     }
 
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
             L = fmaf(__ldcg(base + cc * (2 + HD) + 1), w, L);
             o = fmaf(__ldcg(base + cc * (2 + HD) + 2 + tid), w, o);
         }
-        dst[tid] = L > 0.f ? o / L : 0.f;
+        store_ctx(out, out_bf16, dst + tid, L > 0.f ? o / L : 0.f);
     }
     if (tid == 0) sc.counters[(size_t)item * H + h] = 0;
 }
@@ -348,8 +357,8 @@ cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_
 
 template <typename T>
 static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, int n, const int32_t* streams,
-                            const int32_t* positions, const float* q, int q_stride, float* out, cudaStream_t st,
-                            bool overlap_previous) {
+                            const int32_t* positions, const float* q, int q_stride, void* out, cudaStream_t st,
+                            bool overlap_previous, bool out_bf16) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(s.max_splits, r.heads, n);
     cfg.blockDim = dim3(128);
@@ -359,21 +368,25 @@ static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, in
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = overlap_previous ? 1 : 0;
-    if (append) return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out);
-    return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out);
+    const int ob = out_bf16 ? 1 : 0;
+    if (append)
+        return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out, ob);
+    return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out, ob);
 }
 
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
                           const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
-                          float* out, cudaStream_t st, bool overlap_previous) {
+                          void* out, cudaStream_t st, bool overlap_previous, bool out_bf16) {
     switch (dtype) {
         case MB_F32:
-            return decode_t<float>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous);
+            return decode_t<float>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous,
+                                   out_bf16);
         case MB_BF16:
             return decode_t<__nv_bfloat16>(append, r, s, n, streams, positions, q, q_stride, out, st,
-                                           overlap_previous);
+                                           overlap_previous, out_bf16);
         default:
-            return decode_t<__half>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous);
+            return decode_t<__half>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous,
+                                    out_bf16);
     }
 }
 

@@ -10,6 +10,7 @@
 // epilogue: y = b + x W, W [K][N] row-major as the published graph stores it);
 // LayerNorm (LAYERNORM_1, kernels-decode.ts:168-200: eps 1e-5, two passes) and
 // GELU (GELU_TANH, kernels-decode.ts:373-390) are kernels here.
+#include <stdlib.h>
 #include <string.h>
 
 #include "mb_decoder.cuh"
@@ -31,10 +32,20 @@ __global__ void layernorm_rows(const float* __restrict__ x, const float* __restr
     const float* xr = x + (size_t)row * width;
     float v[PER];
     float sum = 0.f;
+    if constexpr (PER % 4 == 0) {  // 16-byte loads: lane owns columns 4 lane + 128 k .. + 3
 #pragma unroll
-    for (int i = 0; i < PER; i++) {
-        v[i] = xr[lane + 32 * i];
-        sum += v[i];
+        for (int k = 0; k < PER / 4; k++) {
+            const float4 q = *reinterpret_cast<const float4*>(xr + 4 * lane + 128 * k);
+            v[4 * k] = q.x, v[4 * k + 1] = q.y, v[4 * k + 2] = q.z, v[4 * k + 3] = q.w;
+        }
+#pragma unroll
+        for (int i = 0; i < PER; i++) sum += v[i];
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            v[i] = xr[lane + 32 * i];
+            sum += v[i];
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -51,17 +62,38 @@ __global__ void layernorm_rows(const float* __restrict__ x, const float* __restr
     TO* yr = y + (size_t)row * width;
 #pragma unroll
     for (int i = 0; i < PER; i++) {
-        const int c = lane + 32 * i;
+        const int c = PER % 4 == 0 ? 4 * lane + 128 * (i / 4) + (i % 4) : lane + 32 * i;
         yr[c] = (TO)((v[i] - mean) * inv * w[c] + b[c]);
     }
 }
 
-// GELU, tanh approximation (GELU_TANH), fp32 in -> bf16 out
+// tanh on the MUFU unit (tanh.approx.f32, max relative error about 2^-11): the
+// result is rounded to bf16 (2^-8) right after, so the approximation is below
+// the output's own resolution.
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// GELU, tanh approximation (GELU_TANH), fp32 in -> bf16 out, 4 elements a thread
+// (n a multiple of 4, both pointers 16-byte aligned)
 __global__ void gelu_tanh_to_bf16(const float* __restrict__ x, bf16* __restrict__ y, size_t n) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const float v = x[i];
-        const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-        y[i] = __float2bfloat16_rn(0.5f * v * (1.f + tanhf(inner)));
+    const size_t n4 = n / 4;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        float r[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float a = r[k];
+            const float inner = 0.7978845608028654f * (a + 0.044715f * a * a * a);
+            r[k] = 0.5f * a * (1.f + tanh_fast(inner));
+        }
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(r[0], r[1]), hi = __floats2bfloat162_rn(r[2], r[3]);
+        uint2 packed;
+        packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+        packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+        reinterpret_cast<uint2*>(y)[i] = packed;
     }
 }
 
@@ -72,7 +104,7 @@ __global__ void to_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y
 
 template <typename TO>
 cudaError_t layernorm(const float* x, const float* w, const float* b, TO* y, int rows, int width, cudaStream_t st) {
-    const int warps = 4, blocks = (rows + warps - 1) / warps;
+    const int warps = 2, blocks = (rows + warps - 1) / warps;
     switch (width / 32) {  // width = heads * 64
         case 2: layernorm_rows<TO, 2><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
         case 8: layernorm_rows<TO, 8><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
@@ -170,10 +202,10 @@ int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, 
         const auto& W = d->L[l];
         if ((e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess) break;
         if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, false, st))) break;
+        // the context rows go straight to the bf16 input of the c_proj GEMM
         if ((e = mb::launch_decode(c->cfg.dtype, true, mb::ring_view(c, l), c->scratch, n, streams, positions, d->qkv,
-                                   3 * h, d->att, st)) != cudaSuccess)
+                                   3 * h, d->xb, st, false, true)) != cudaSuccess)
             break;
-        if ((e = to_bf16(d->att, d->xb, (size_t)n * h, st)) != cudaSuccess) break;
         if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, true, st))) break;
         if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, d->xb, n, h, st)) != cudaSuccess) break;
         if ((rc = gemm(d, n, f, h, d->xb, W.w_in, W.b_in, d->h1, false, st))) break;
@@ -206,7 +238,9 @@ MB_API int mb_decoder_destroy(mb_decoder* d) {
     int prev = -1;
     cudaGetDevice(&prev);
     cudaSetDevice(d->ctx->cfg.device);
-    void* ptrs[] = {d->wmem, d->xb, d->qkv, d->att, d->h1, d->workspace};
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    if (d->cap) cudaStreamDestroy(d->cap);
+    void* ptrs[] = {d->wmem, d->xb, d->qkv, d->h1, d->workspace, d->g_streams, d->g_positions, d->g_hidden};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (auto& kv : d->plans) {
@@ -297,11 +331,18 @@ MB_API int mb_decoder_create(mb_ctx* c, int32_t ffn, const float* w, size_t coun
     const size_t mb = c->cfg.max_batch, wide = (size_t)(ffn > h ? ffn : h);
     if (cudaMalloc(&d->xb, mb * wide * sizeof(bf16)) != cudaSuccess ||
         cudaMalloc(&d->qkv, mb * 3 * h * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&d->att, mb * h * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&d->h1, mb * ffn * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&d->workspace, d->ws_bytes) != cudaSuccess)
+        cudaMalloc(&d->workspace, d->ws_bytes) != cudaSuccess || cudaMalloc(&d->g_streams, mb * 4) != cudaSuccess ||
+        cudaMalloc(&d->g_positions, mb * 4) != cudaSuccess ||
+        cudaMalloc(&d->g_hidden, mb * h * sizeof(float)) != cudaSuccess)
         return bail(MB_ERR_OOM, "decoder: activation allocation failed");
     if (cublasLtCreate(&d->lt) != CUBLAS_STATUS_SUCCESS) return bail(MB_ERR_CUDA, "decoder: cublasLtCreate failed");
+    if (cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(MB_ERR_CUDA, "decoder: stream creation failed");
+    {
+        const char* v = getenv("MOCKBIRD_DECODER_GRAPH");
+        d->use_graph = !(v && strcmp(v, "0") == 0);
+    }
     if (prev >= 0) cudaSetDevice(prev);
     *out = d;
     return MB_OK;
@@ -318,7 +359,46 @@ MB_API int mb_decoder_step(mb_decoder* d, int32_t n, const int32_t* streams, con
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != c->cfg.device && cudaSetDevice(c->cfg.device) != cudaSuccess) return MB_ERR_CUDA;
-    const int rc = mb::dec::run(d, n, streams, positions, hidden, nullptr, static_cast<cudaStream_t>(cuda_stream));
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    int rc = MB_OK;
+    if (!d->use_graph) {
+        rc = mb::dec::run(d, n, streams, positions, hidden, nullptr, st);
+    } else {
+        // One captured step per item count, over inputs staged into this object's
+        // buffers; the first step of a count runs directly (kernel modules loaded,
+        // GEMM plans built outside any capture) and is then captured for the next.
+        const size_t hb = (size_t)n * d->hid * sizeof(float);
+        cudaError_t e = cudaMemcpyAsync(d->g_streams, streams, n * 4, cudaMemcpyDeviceToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_positions, positions, n * 4, cudaMemcpyDeviceToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_hidden, hidden, hb, cudaMemcpyDeviceToDevice, st);
+        auto it = d->graphs.find(n);
+        if (e != cudaSuccess) {
+            rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder inputs: ") + cudaGetErrorString(e));
+        } else if (it != d->graphs.end()) {
+            e = cudaGraphLaunch(it->second, st);
+            if (e != cudaSuccess) rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder graph: ") + cudaGetErrorString(e));
+        } else {
+            rc = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st);
+            cudaGraph_t g = nullptr;
+            if (rc == MB_OK && (e = cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+                rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
+            if (rc == MB_OK) {
+                const int rc2 = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, d->cap);
+                e = cudaStreamEndCapture(d->cap, &g);
+                cudaGraphExec_t ex = nullptr;
+                if (rc2 == MB_OK && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+                if (g) cudaGraphDestroy(g);
+                if (rc2 != MB_OK)
+                    rc = rc2;
+                else if (e != cudaSuccess)
+                    rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
+                else
+                    d->graphs.emplace(n, ex);
+            }
+        }
+        if (rc == MB_OK && (e = cudaMemcpyAsync(hidden, d->g_hidden, hb, cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+            rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder output: ") + cudaGetErrorString(e));
+    }
     if (prev >= 0 && prev != c->cfg.device) cudaSetDevice(prev);
     return rc;
 }

@@ -26,7 +26,6 @@ struct mb_decoder {
     void* wmem = nullptr;      // all weights, one allocation
     bf16* xb = nullptr;        // [max_batch][max(hid, ffn)] GEMM input
     float* qkv = nullptr;      // [max_batch][3*hid]
-    float* att = nullptr;      // [max_batch][hid]
     float* h1 = nullptr;       // [max_batch][ffn]
     cublasLtHandle_t lt = nullptr;
     void* workspace = nullptr;
@@ -37,6 +36,12 @@ struct mb_decoder {
         cublasLtMatmulAlgo_t algo{};
     };
     std::map<std::tuple<int, int, int, int>, Plan> plans;  // (M, N, K, has bias)
+    // mb_decoder_step replays one captured step per item count over staged inputs
+    bool use_graph = true;
+    cudaStream_t cap = nullptr;
+    int32_t *g_streams = nullptr, *g_positions = nullptr;  // [max_batch]
+    float* g_hidden = nullptr;                              // [max_batch][hid]
+    std::map<int, cudaGraphExec_t> graphs;
 };
 
 namespace mb {

@@ -93,9 +93,10 @@ cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_
 // the previous kernel on the stream is a decode launch of a DIFFERENT layer
 // (consecutive layers of one decode step): this launch's ring reads and append
 // may then run before that kernel has finished.
+// out_bf16: write the context rows as bf16 (out then points to __nv_bfloat16).
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
                           const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
-                          float* out, cudaStream_t st, bool overlap_previous = false);
+                          void* out, cudaStream_t st, bool overlap_previous = false, bool out_bf16 = false);
 bool decode_persist_supported(const RingView& r, int n, int q_stride);
 int persist_part_stride(int dtype, int capacity);  // split-K partial slots per (item, head)
 cudaError_t launch_decode_persist(int dtype, bool append, const RingView& r, const Scratch& s, int n,
