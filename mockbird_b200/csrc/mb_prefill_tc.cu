@@ -73,14 +73,16 @@ __device__ __forceinline__ float ex2(float x) {
 // 0), packed to 16 bits into its row of the 128-byte-swizzled P sub-tile; adds
 // to the four partial row sums.  (Computing half of the exponentials on the FMA
 // pipe with a polynomial, to unload MUFU, was measured 1.7 % slower here.)
+// Scores are raw (unscaled); the scale goes into the exponent's argument, one
+// FFMA per score: p = 2^(s * scale - m), m in the scaled (log2) domain.
 template <bool BF16>
-__device__ __forceinline__ void softmax_pack(const float (&sv)[64], float m_new, unsigned char* sub, int row,
-                                             float& ls0, float& ls1, float& ls2, float& ls3) {
+__device__ __forceinline__ void softmax_pack(const float (&sv)[64], float scale, float m_new, unsigned char* sub,
+                                             int row, float& ls0, float& ls1, float& ls2, float& ls3) {
 #pragma unroll
     for (int ch = 0; ch < 8; ch++) {
         float pv[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) pv[e] = ex2(sv[8 * ch + e] - m_new);
+        for (int e = 0; e < 8; e++) pv[e] = ex2(fmaf(sv[8 * ch + e], scale, -m_new));
         ls0 += pv[0] + pv[4];
         ls1 += pv[1] + pv[5];
         ls2 += pv[2] + pv[6];
@@ -190,13 +192,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         const int kb = k0 + 64 * half;
         const bool full = (k0 + BN <= q0) && (k0 + BN <= rows);  // no key of the tile is masked
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        // row maximum of the raw scores (the scale is positive, so it commutes)
         if (full) {
 #pragma unroll
             for (int i = 0; i < 64; i += 4) {
-                sv[i] *= scale;
-                sv[i + 1] *= scale;
-                sv[i + 2] *= scale;
-                sv[i + 3] *= scale;
                 mx0 = fmaxf(mx0, sv[i]);
                 mx1 = fmaxf(mx1, sv[i + 1]);
                 mx2 = fmaxf(mx2, sv[i + 2]);
@@ -206,10 +205,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             const int lim = min(qg, rows - 1) - kb;
 #pragma unroll
             for (int i = 0; i < 64; i += 4) {
-                sv[i] = i <= lim ? sv[i] * scale : -INFINITY;
-                sv[i + 1] = i + 1 <= lim ? sv[i + 1] * scale : -INFINITY;
-                sv[i + 2] = i + 2 <= lim ? sv[i + 2] * scale : -INFINITY;
-                sv[i + 3] = i + 3 <= lim ? sv[i + 3] * scale : -INFINITY;
+                sv[i] = i <= lim ? sv[i] : -INFINITY;
+                sv[i + 1] = i + 1 <= lim ? sv[i + 1] : -INFINITY;
+                sv[i + 2] = i + 2 <= lim ? sv[i + 2] : -INFINITY;
+                sv[i + 3] = i + 3 <= lim ? sv[i + 3] : -INFINITY;
                 mx0 = fmaxf(mx0, sv[i]);
                 mx1 = fmaxf(mx1, sv[i + 1]);
                 mx2 = fmaxf(mx2, sv[i + 2]);
@@ -218,12 +217,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         }
         sm.rmax[half][row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
         __syncthreads();
-        const float m_tile = fmaxf(sm.rmax[0][row], sm.rmax[1][row]);
+        const float m_tile = fmaxf(sm.rmax[0][row], sm.rmax[1][row]) * scale;
         const float m_new = fmaxf(m_run, m_tile);   // finite: key 0 of tile 0 is never masked
         const float corr = ex2(m_run - m_new);      // 0 on the first tile (m_run = -inf)
         float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
         unsigned char* sub = sm.p[half] + row * 128;  // this half's 64 keys = P sub-tile `half`
-        softmax_pack<BF16>(sv, m_new, sub, row, ls0, ls1, ls2, ls3);
+        softmax_pack<BF16>(sv, scale, m_new, sub, row, ls0, ls1, ls2, ls3);
         l_half = l_half * corr + ((ls0 + ls1) + (ls2 + ls3));
         m_run = m_new;
         fence_async_smem();
