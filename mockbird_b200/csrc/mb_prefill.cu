@@ -192,8 +192,8 @@ static cudaError_t prefill_t(const RingView& r, int n, const int32_t* streams, i
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if constexpr (sizeof(T) == 2)  // 16-bit rings: tensor cores (mb_prefill_tc.cu)
-        return launch_prefill_attn_tc(sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value ? MB_BF16 : MB_F16, r, n,
-                                      streams, rows, q_stage, out, st);
+        return launch_prefill_attn_tc(std::is_same<T, __nv_bfloat16>::value ? MB_BF16 : MB_F16, r, n, streams, rows,
+                                      q_stage, out, st);
     prefill_attn_simt_kernel<T><<<dim3((rows + 63) / 64, r.heads, n), 128, 0, st>>>(
         r, streams, rows, reinterpret_cast<const T*>(q_stage), out);
     return cudaGetLastError();
