@@ -99,3 +99,29 @@ def test_prefill_errors():
     assert e.value.status == "MB_ERR_DEVICE"
     del out
     ring.sync()
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_prefill_rising_scores_rescale_every_tile(dtype):
+    """Scores that rise along the keys, so that every row's running maximum jumps
+    by more than 2^8 (log2 units) on every 64-key tile: the tensor-core kernel
+    then rescales the row's O in tensor memory on every tile.  Q and K put their
+    energy into the last RoPE pair of each head (frequency 10000^(-62/64): it
+    turns by less than 0.2 rad over the 1000 positions), K growing with the
+    position, so q.k grows by ~9 per tile after the 0.125 * log2(e) scale.
+    1000 rows: 8 query tiles of 128, up to 16 key tiles.  Also the longest
+    prefill of the suite.  Random V."""
+    rows, C = 1000, 1024
+    ring = KvRing(layers=1, streams=1, capacity=C, dtype=dtype, wrap=True)
+    orc = oracle.Ring(layers=1, streams=1, heads=H, capacity=C, dtype=dtype, wrap=True)
+    rng = np.random.default_rng(31)
+    qkv = np.zeros((1, rows, QKV), np.float32)
+    for h in range(H):
+        qkv[0, :, h * 64 + 62: h * 64 + 64] = 4.0                                  # q
+        qkv[0, :, HID + h * 64 + 62: HID + h * 64 + 64] = (0.1 * np.arange(rows))[:, None]  # k
+    qkv[0, :, 2 * HID:] = rng.standard_normal((rows, HID)).astype(np.float32)      # v
+    out = ring.prefill(0, [0], torch.from_numpy(qkv).to(DEV))
+    ref, _ = orc.prefill(0, [0], qkv, q_round=True)
+    ring.sync()
+    assert max_err(out, ref) < TOL[dtype]
+    assert_window_equal(ring, orc, 0, 0, 0, 0, rows - 1)
