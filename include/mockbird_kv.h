@@ -229,7 +229,7 @@ typedef struct mb_local_head mb_local_head;
 
 typedef struct mb_local_config {
     int32_t ffn;              /* FFN width of the local layer (3072) */
-    int32_t codes;            /* codebook size (CODES = 1024, decode.ts:48); a multiple of 32 */
+    int32_t codes;            /* codebook size (CODES = 1024, decode.ts:48): 128, 256, 512, 1024 or 2048 */
     int32_t channels;         /* codebooks per frame (n_vq = 16), 1..64; a frame takes channels + 1 steps */
     float repetition_penalty; /* audio_repetition_penalty (1.2 in the published defaults) */
 } mb_local_config;
@@ -266,7 +266,8 @@ MB_API int mb_local_head_frame(mb_local_head* head, int32_t n, const int32_t* st
 /* ARGMAX_PENALTY alone (kernels-decode.ts:428-485), on the current device: for
  * each of n rows, token = the penalised argmax of logits [n][codes] under the
  * row's seen mask seen [n][codes/32] (bit j of word j/32), whose bit is then
- * set.  Device pointers; codes a multiple of 32. */
+ * set.  Device pointers, logits 16-byte aligned; codes 128, 256, 512, 1024 or
+ * 2048. */
 MB_API int mb_argmax_penalty(int32_t n, int32_t codes, const float* logits, uint32_t* seen, float penalty,
                              int32_t* tokens, void* cuda_stream);
 

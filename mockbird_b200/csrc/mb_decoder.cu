@@ -60,10 +60,29 @@ __global__ void layernorm_rows(const float* __restrict__ x, const float* __restr
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     const float inv = rsqrtf(sq / (float)width + 1e-5f);
     TO* yr = y + (size_t)row * width;
+    if constexpr (PER % 4 == 0) {  // 16-byte weight/bias loads, 4-element stores
 #pragma unroll
-    for (int i = 0; i < PER; i++) {
-        const int c = PER % 4 == 0 ? 4 * lane + 128 * (i / 4) + (i % 4) : lane + 32 * i;
-        yr[c] = (TO)((v[i] - mean) * inv * w[c] + b[c]);
+        for (int k = 0; k < PER / 4; k++) {
+            const int c = 4 * lane + 128 * k;
+            const float4 wk = *reinterpret_cast<const float4*>(w + c), bk = *reinterpret_cast<const float4*>(b + c);
+            const float r0 = (v[4 * k] - mean) * inv * wk.x + bk.x, r1 = (v[4 * k + 1] - mean) * inv * wk.y + bk.y;
+            const float r2 = (v[4 * k + 2] - mean) * inv * wk.z + bk.z, r3 = (v[4 * k + 3] - mean) * inv * wk.w + bk.w;
+            if constexpr (sizeof(TO) == 4) {
+                *reinterpret_cast<float4*>(yr + c) = make_float4(r0, r1, r2, r3);
+            } else {
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(r0, r1), hi = __floats2bfloat162_rn(r2, r3);
+                uint2 u;
+                u.x = *reinterpret_cast<const uint32_t*>(&lo);
+                u.y = *reinterpret_cast<const uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(yr + c) = u;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int c = lane + 32 * i;
+            yr[c] = (TO)((v[i] - mean) * inv * w[c] + b[c]);
+        }
     }
 }
 

@@ -86,13 +86,15 @@ __global__ void local_decide_kernel(int n, int h, const float* __restrict__ x, c
 // whose bit is set in the row's seen mask becomes s / penalty (s >= 0) or
 // s * penalty (s < 0); the winner is the largest value, ties to the lowest id,
 // starting from (-1e30, id 0) as the reference does; its bit is then set.
-// Each lane scans ids lane, lane+32, ... with a strict >, and the warp reduces
-// under the order (value desc, id asc) -- the same total-order maximum as the
-// reference's strided scan and tree, so the same winner.
+// Lane l scans its contiguous ids [l*codes/32, (l+1)*codes/32) in order with a
+// strict > (all of its loads issued up front), and the warp reduces under the
+// order (value desc, id asc) -- the same total-order maximum as the reference's
+// strided scan and tree, so the same winner.
 // Row i: logits + i*codes; mask = seen + row_sel(i) * seen_row_words + ch * codes/32
 // (row_sel(i) = streams[i] when `streams` is given, else i; rows whose stream is
 // outside [0, n_seen_rows) get token 0 and leave the masks alone -- the ring's
 // own kernel reports such a stream); token -> tokens[i*tok_stride + ch].
+template <int PER>  // ids per lane = codes / 32, a multiple of 4
 __global__ void argmax_penalty_kernel(int n, int codes, const float* __restrict__ logits, uint32_t* __restrict__ seen,
                                       const int32_t* __restrict__ streams, int n_seen_rows, int seen_row_words, int ch,
                                       float penalty, int32_t* __restrict__ tokens, int tok_stride) {
@@ -101,15 +103,29 @@ __global__ void argmax_penalty_kernel(int n, int codes, const float* __restrict_
     const int row = streams ? streams[i] : i;
     const bool ok = row >= 0 && row < n_seen_rows;
     uint32_t* mask = seen + (size_t)(ok ? row : 0) * seen_row_words + (size_t)ch * (codes >> 5);
-    const float* lg = logits + (size_t)i * codes;
+    const float4* lg = reinterpret_cast<const float4*>(logits + (size_t)i * codes + lane * PER);
+    float v[PER];
+#pragma unroll
+    for (int k = 0; k < PER / 4; k++) {
+        const float4 q = lg[k];
+        v[4 * k] = q.x, v[4 * k + 1] = q.y, v[4 * k + 2] = q.z, v[4 * k + 3] = q.w;
+    }
+    const int j0 = lane * PER;
     float best = -1e30f;
     int idx = 0;
-    for (int j = lane; j < codes; j += 32) {
-        float s = lg[j];
-        if (ok && ((mask[j >> 5] >> (j & 31)) & 1u)) s = s >= 0.f ? s / penalty : s * penalty;
-        if (s > best) {
-            best = s;
-            idx = j;
+#pragma unroll
+    for (int w = 0; w < PER / 32 + (PER % 32 != 0); w++) {
+        const int jw = j0 + 32 * w;  // this lane's ids jw .. jw+31 share one mask word when PER >= 32
+        const uint32_t bits = ok ? mask[jw >> 5] : 0u;
+#pragma unroll
+        for (int e = 0; e < (PER < 32 ? PER : 32); e++) {
+            const int j = jw + e;
+            float s = v[32 * w + e];
+            if ((bits >> (j & 31)) & 1u) s = s >= 0.f ? s / penalty : s * penalty;
+            if (s > best) {
+                best = s;
+                idx = j;
+            }
         }
     }
 #pragma unroll
@@ -125,6 +141,27 @@ __global__ void argmax_penalty_kernel(int n, int codes, const float* __restrict_
         tokens[(size_t)i * tok_stride + ch] = ok ? idx : 0;
         if (ok) mask[idx >> 5] |= 1u << (idx & 31);
     }
+}
+
+// Launches the argmax for `codes` in {128, 256, 512, 1024, 2048} (ids per lane a
+// multiple of 4); other sizes are rejected by the callers' checks.
+cudaError_t launch_argmax(int n, int codes, const float* logits, uint32_t* seen, const int32_t* streams,
+                          int n_seen_rows, int seen_row_words, int ch, float penalty, int32_t* tokens, int tok_stride,
+                          cudaStream_t st) {
+    const int warps = 2, blocks = (n + warps - 1) / warps;
+#define MB_ARGMAX(PER)                                                                                          \
+    argmax_penalty_kernel<PER><<<blocks, 32 * warps, 0, st>>>(n, codes, logits, seen, streams, n_seen_rows,    \
+                                                                seen_row_words, ch, penalty, tokens, tok_stride)
+    switch (codes) {
+        case 128: MB_ARGMAX(4); break;
+        case 256: MB_ARGMAX(8); break;
+        case 512: MB_ARGMAX(16); break;
+        case 1024: MB_ARGMAX(32); break;
+        case 2048: MB_ARGMAX(64); break;
+        default: return cudaErrorInvalidValue;
+    }
+#undef MB_ARGMAX
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -180,9 +217,10 @@ int enqueue_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
             rc = mb::dec::gemm(lh->dec, n, lh->codes, h, lh->hb, lh->heads + (size_t)ch * h * lh->codes, nullptr,
                                lh->lg, false, st);
             if (rc) return rc;
-            argmax_penalty_kernel<<<wblocks, 32 * warps, 0, st>>>(n, lh->codes, lh->lg, lh->seen, lh->ids,
-                                                                  lh->ctx->cfg.streams, lh->seen_words, ch,
-                                                                  lh->penalty, lh->tok, lh->channels);
+            e = launch_argmax(n, lh->codes, lh->lg, lh->seen, lh->ids, lh->ctx->cfg.streams, lh->seen_words, ch,
+                              lh->penalty, lh->tok, lh->channels, st);
+            if (e != cudaSuccess)
+                return lfail(lh, MB_ERR_CUDA, std::string("local head argmax: ") + cudaGetErrorString(e));
             if (want_logits) {
                 const size_t row = (size_t)lh->codes * sizeof(float);
                 e = cudaMemcpy2DAsync(lh->lg_all + (size_t)ch * lh->codes, row * lh->channels, lh->lg, row, row, n,
@@ -274,9 +312,10 @@ MB_API int mb_local_head_create(mb_ctx* c, const mb_local_config* cfg, const flo
     if (!c || !cfg || !w || !out) return MB_ERR_ARG;
     *out = nullptr;
     const int steps = cfg->channels + 1;
-    if (cfg->codes <= 0 || cfg->codes % 32 || cfg->channels <= 0 || cfg->channels > 64 ||
+    if (!(cfg->codes == 128 || cfg->codes == 256 || cfg->codes == 512 || cfg->codes == 1024 || cfg->codes == 2048) ||
+        cfg->channels <= 0 || cfg->channels > 64 ||
         !(cfg->repetition_penalty > 0.f) || !isfinite(cfg->repetition_penalty)) {
-        c->last_error = "local head: codes must be a positive multiple of 32, channels in [1, 64], penalty > 0";
+        c->last_error = "local head: codes must be 128, 256, 512, 1024 or 2048, channels in [1, 64], penalty > 0";
         return MB_ERR_ARG;
     }
     if (c->cfg.layers != 1 || c->cfg.capacity < steps || c->cfg.max_position < steps) {
@@ -387,13 +426,15 @@ MB_API int mb_local_head_frame(mb_local_head* lh, int32_t n, const int32_t* stre
 
 MB_API int mb_argmax_penalty(int32_t n, int32_t codes, const float* logits, uint32_t* seen, float penalty,
                              int32_t* tokens, void* cuda_stream) {
-    if (n < 0 || codes <= 0 || codes % 32 || !(penalty > 0.f) || !isfinite(penalty)) return MB_ERR_ARG;
+    if (n < 0 || !(codes == 128 || codes == 256 || codes == 512 || codes == 1024 || codes == 2048) ||
+        !(penalty > 0.f) || !isfinite(penalty))
+        return MB_ERR_ARG;
     if (n == 0) return MB_OK;
-    if (!logits || !seen || !tokens) return MB_ERR_ARG;
-    const int warps = 4;
-    argmax_penalty_kernel<<<(n + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(cuda_stream)>>>(
-        n, codes, logits, seen, nullptr, n, codes / 32, 0, penalty, tokens, 1);
-    return cudaGetLastError() == cudaSuccess ? MB_OK : MB_ERR_CUDA;
+    if (!logits || !seen || !tokens || (reinterpret_cast<uintptr_t>(logits) & 15)) return MB_ERR_ARG;
+    return launch_argmax(n, codes, logits, seen, nullptr, n, codes / 32, 0, penalty, tokens, 1,
+                         static_cast<cudaStream_t>(cuda_stream)) == cudaSuccess
+               ? MB_OK
+               : MB_ERR_CUDA;
 }
 
 }  // extern "C"
