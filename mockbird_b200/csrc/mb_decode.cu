@@ -337,6 +337,101 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     if (tid == 0) sc.counters[(size_t)item * H + h] = 0;
 }
 
+// ---------------------------------------------------------------- small rings (capacity <= 32)
+
+// The same computation for rings of at most 32 slots (the local head's 17-slot
+// ring): one warp per (item, head), lane j scores slot j, warp shuffles for the
+// softmax, lane l owns dims 2l, 2l+1 of the query, the new row and the context.
+// No staging in shared memory and no split-K: a window is at most 32 slots.
+// grid (ceil(heads / 4), n), 128 threads.
+template <typename T, bool APPEND>
+__global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int32_t* __restrict__ streams,
+                                                           const int32_t* __restrict__ positions,
+                                                           const float* __restrict__ q_in, int q_stride, void* out,
+                                                           int out_bf16) {
+    __shared__ __align__(16) float qs[4][HD];  // the warp's roped query
+    __shared__ __align__(16) float kn[4][HD];  // the warp's new K row (storage-rounded)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x * 4 + warp, item = blockIdx.y;
+    const int s = streams[item], pos = positions[item];
+    if (!item_ok(r, s, pos)) return;  // uniform over the CTA
+    const int C = r.capacity, H = r.heads, HID = H * HD;
+    const bool head_ok = h < H;
+    const int count = min(pos + 1, C), newslot = pos % C;
+    const float* row = q_in + (size_t)item * q_stride;
+    const T* kbase = reinterpret_cast<const T*>(r.kv) + (((size_t)s * 2 + 0) * H + (head_ok ? h : 0)) * (size_t)C * HD;
+    const T* vbase = reinterpret_cast<const T*>(r.kv) + (((size_t)s * 2 + 1) * H + (head_ok ? h : 0)) * (size_t)C * HD;
+
+    float2 vnew = make_float2(0.f, 0.f);
+    if (head_ok) {
+        float2 qv = *reinterpret_cast<const float2*>(row + h * HD + 2 * lane);
+        if (APPEND) {
+            const float2 cs = r.rope[(size_t)pos * 32 + lane];
+            qv = rope_pair(qv, cs);
+            const float2 kr = rope_pair(*reinterpret_cast<const float2*>(row + HID + h * HD + 2 * lane), cs);
+            const float2 vv = *reinterpret_cast<const float2*>(row + 2 * HID + h * HD + 2 * lane);
+            Store<T>::store2(const_cast<T*>(kbase) + (size_t)newslot * HD + 2 * lane, kr);
+            Store<T>::store2(const_cast<T*>(vbase) + (size_t)newslot * HD + 2 * lane, vv);
+            const float2 kq = Store<T>::round2(kr);
+            kn[warp][2 * lane] = kq.x;
+            kn[warp][2 * lane + 1] = kq.y;
+            vnew = Store<T>::round2(vv);
+            if (h == 0 && lane == 0) r.slot_pos[(size_t)s * C + newslot] = pos;
+        }
+        qs[warp][2 * lane] = qv.x;
+        qs[warp][2 * lane + 1] = qv.y;
+    }
+    __syncwarp();
+
+    // ---- lane j: the score of slot j (kernels-decode.ts:622-623 liveness)
+    float sc = -INFINITY;
+    if (head_ok && lane < count) {
+        const int stored = (APPEND && lane == newslot) ? pos : r.slot_pos[(size_t)s * C + lane];
+        if (stored >= 0 && pos - stored >= 0 && pos - stored < C) {
+            float dot = 0.f;
+            if (APPEND && lane == newslot) {
+#pragma unroll 16
+                for (int d = 0; d < HD; d++) dot = fmaf(kn[warp][d], qs[warp][d], dot);
+            } else {
+                const T* kr = kbase + (size_t)lane * HD;
+#pragma unroll 8
+                for (int d = 0; d < HD; d += 2) {
+                    const float2 kv = Store<T>::load2(kr + d);
+                    dot = fmaf(kv.x, qs[warp][d], dot);
+                    dot = fmaf(kv.y, qs[warp][d + 1], dot);
+                }
+            }
+            sc = dot * (SCALE * LOG2E);
+        }
+    }
+    float m = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float p = sc == -INFINITY ? 0.f : exp2f(sc - m);
+    float l = p;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+
+    // ---- P.V: lane owns dims 2 lane, 2 lane + 1
+    float a0 = 0.f, a1 = 0.f;
+    for (int j = 0; j < count; j++) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        if (pj == 0.f || !head_ok) continue;  // warp-uniform
+        const float2 vv = (APPEND && j == newslot) ? vnew : Store<T>::load2(vbase + (size_t)j * HD + 2 * lane);
+        a0 = fmaf(pj, vv.x, a0);
+        a1 = fmaf(pj, vv.y, a1);
+    }
+    // outputs only once the previous launch (programmatic dependent launch) has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (head_ok) {
+        const size_t dst = (size_t)item * HID + h * HD + 2 * lane;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        store_ctx(out, out_bf16, dst, a0 * inv);
+        store_ctx(out, out_bf16, dst + 1, a1 * inv);
+    }
+}
+
 // ---------------------------------------------------------------- launchers
 
 template <typename T>
@@ -363,12 +458,23 @@ static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, in
     cfg.gridDim = dim3(s.max_splits, r.heads, n);
     cfg.blockDim = dim3(128);
     cfg.stream = st;
+    const int ob = out_bf16 ? 1 : 0;
+    if (r.capacity <= 32) {  // a window fits one warp
+        cfg.gridDim = dim3((r.heads + 3) / 4, n);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = overlap_previous ? 1 : 0;
+        if (append)
+            return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, true>, r, streams, positions, q, q_stride, out, ob);
+        return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, false>, r, streams, positions, q, q_stride, out, ob);
+    }
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = overlap_previous ? 1 : 0;
-    const int ob = out_bf16 ? 1 : 0;
     if (append)
         return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out, ob);
     return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out, ob);

@@ -386,3 +386,77 @@ def test_codec_ring_geometry(capacity):
     last = capacity + 59
     for s in range(S):
         assert_window_equal(ring, orc, last % L, s, last % L, s, last)
+
+
+@pytest.mark.parametrize("dtype,C,heads,wrap", [("f32", 17, 12, True), ("bf16", 32, 5, True), ("f16", 17, 5, True),
+                                                ("bf16", 17, 12, False)])
+def test_small_ring_parity(dtype, C, heads, wrap):
+    """Rings of at most 32 slots (the local head's is 17) take the warp-per-head
+    kernel: ring bytes and slot order bit-exact against the oracle, contexts
+    within tolerance, fused == RoPE then attend bit for bit.  Streams at
+    different positions, the ring wrapping several times; 5 heads leave idle
+    warps in a CTA."""
+    S, L = 3, 2
+    qkv_w = 3 * heads * 64
+    a = KvRing(layers=L, heads=heads, streams=S, capacity=C, dtype=dtype, wrap=wrap, max_position=256)
+    b = KvRing(layers=L, heads=heads, streams=S, capacity=C, dtype=dtype, wrap=wrap, max_position=256)
+    orc = oracle.Ring(layers=L, streams=S, heads=heads, capacity=C, dtype=dtype, wrap=wrap, max_position=256)
+    start = [0, 3, 11]
+    steps = 50 if wrap else C - max(start)
+    worst = 0.0
+    for step in range(steps):
+        items = [2, 0, 1]
+        pos = [step + start[s] for s in items]
+        for layer in range(L):
+            qkv = randn((S, qkv_w), seed=300 + step * 10 + layer)
+            x = torch.from_numpy(qkv).to(DEV)
+            oa = a.append_attend(layer, items, pos, x)
+            qb = x.clone()
+            b.rope_split_ring(layer, items, pos, qb)
+            ob = b.attend_ring(layer, items, pos, qb, q_stride=qkv_w)
+            assert torch.equal(oa, ob), (step, layer)
+            ref, _ = orc.append_attend(layer, items, pos, qkv)
+            worst = max(worst, max_err(oa, ref))
+    a.sync()
+    b.sync()
+    assert worst < TOL[dtype], worst
+    for layer in range(L):
+        for s, p in zip(items, pos):
+            assert_window_equal(a, orc, layer, s, layer, s, p)
+
+
+@pytest.mark.parametrize("C", [17, 300])
+def test_decode_on_a_capturing_stream(C):
+    """Every launch goes to the caller's stream: append + attention captured into
+    a CUDA graph on torch's capture stream and replayed (positions and rows
+    updated in place between replays) gives, bit for bit, what the same calls
+    give run directly -- for the small-ring kernel (C = 17) and the general one."""
+    S = 3
+    a = KvRing(layers=1, streams=S, capacity=C, dtype="bf16", wrap=True)
+    b = KvRing(layers=1, streams=S, capacity=C, dtype="bf16", wrap=True)
+    ids = torch.tensor([2, 0, 1], dtype=torch.int32, device=DEV)
+    pos = torch.zeros(S, dtype=torch.int32, device=DEV)
+    qkv = torch.zeros(S, QKV, device=DEV)
+    out = torch.zeros(S, HID, device=DEV)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # one direct call before capturing (module loading)
+        a.append_attend(0, ids, pos, qkv, out)
+    torch.cuda.current_stream().wait_stream(side)
+    a.reset()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        a.append_attend(0, ids, pos, qkv, out)
+    for step in range(40):
+        p = torch.tensor([step, step + 5, step + 9], dtype=torch.int32, device=DEV)
+        x = torch.from_numpy(randn((S, QKV), seed=500 + step)).to(DEV)
+        pos.copy_(p)
+        qkv.copy_(x)
+        g.replay()
+        want = b.append_attend(0, ids, p, x)
+        assert torch.equal(out, want), step
+    torch.cuda.synchronize()
+    a.sync()
+    b.sync()
+    del g
