@@ -383,9 +383,16 @@ __global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int
     }
     __syncwarp();
 
-    // ---- lane j: the score of slot j (kernels-decode.ts:622-623 liveness)
+    // ---- lane j: the score of slot j (kernels-decode.ts:622-623 liveness).  The
+    // slot's position and its K row (16-byte loads) are read together; the row
+    // of the new slot is read too but replaced by the on-chip one.
     float sc = -INFINITY;
     if (head_ok && lane < count) {
+        constexpr int NV = HD * (int)sizeof(T) / 16;  // 16-byte pieces of a row
+        uint4 raw[NV];
+        const uint4* kp = reinterpret_cast<const uint4*>(kbase + (size_t)lane * HD);
+#pragma unroll
+        for (int v = 0; v < NV; v++) raw[v] = kp[v];
         const int stored = (APPEND && lane == newslot) ? pos : r.slot_pos[(size_t)s * C + lane];
         if (stored >= 0 && pos - stored >= 0 && pos - stored < C) {
             float dot = 0.f;
@@ -393,12 +400,19 @@ __global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int
 #pragma unroll 16
                 for (int d = 0; d < HD; d++) dot = fmaf(kn[warp][d], qs[warp][d], dot);
             } else {
-                const T* kr = kbase + (size_t)lane * HD;
-#pragma unroll 8
-                for (int d = 0; d < HD; d += 2) {
-                    const float2 kv = Store<T>::load2(kr + d);
-                    dot = fmaf(kv.x, qs[warp][d], dot);
-                    dot = fmaf(kv.y, qs[warp][d + 1], dot);
+                const float4* q4 = reinterpret_cast<const float4*>(qs[warp]);
+#pragma unroll
+                for (int v = 0; v < NV; v++) {
+                    if constexpr (sizeof(T) == 4) {
+                        const float4 kf = *reinterpret_cast<const float4*>(&raw[v]);
+                        const float4 qf = q4[v];
+                        dot = fmaf(kf.x, qf.x, dot);
+                        dot = fmaf(kf.y, qf.y, dot);
+                        dot = fmaf(kf.z, qf.z, dot);
+                        dot = fmaf(kf.w, qf.w, dot);
+                    } else {
+                        dot = dot8(raw[v], q4 + 2 * v, dot, static_cast<T*>(nullptr));
+                    }
                 }
             }
             sc = dot * (SCALE * LOG2E);
@@ -412,11 +426,12 @@ __global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
 
-    // ---- P.V: lane owns dims 2 lane, 2 lane + 1
+    // ---- P.V: lane owns dims 2 lane, 2 lane + 1 (rows of dead slots have p = 0;
+    // every row read is inside the ring, so the loads need no guard)
     float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
     for (int j = 0; j < count; j++) {
         const float pj = __shfl_sync(0xffffffffu, p, j);
-        if (pj == 0.f || !head_ok) continue;  // warp-uniform
         const float2 vv = (APPEND && j == newslot) ? vnew : Store<T>::load2(vbase + (size_t)j * HD + 2 * lane);
         a0 = fmaf(pj, vv.x, a0);
         a1 = fmaf(pj, vv.y, a1);
