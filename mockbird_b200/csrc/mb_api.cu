@@ -204,6 +204,7 @@ MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
         cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) != cudaSuccess)
         return bail(MB_ERR_CUDA);
+    if (cudaMallocHost(&c->h_err, sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
     c->ev_in.assign(cfg.layers, nullptr);
     c->ev_done.assign(cfg.layers, nullptr);
     for (int l = 0; l < cfg.layers; l++)
@@ -228,6 +229,7 @@ MB_API int mb_destroy(mb_ctx* c) {
                 if (e) cudaEventDestroy(e);
         if (c->ev_start) cudaEventDestroy(c->ev_start);
         if (c->ev_end) cudaEventDestroy(c->ev_end);
+        if (c->h_err) cudaFreeHost(c->h_err);
         if (c->cp_in) cudaStreamDestroy(c->cp_in);
         if (c->cp_out) cudaStreamDestroy(c->cp_out);
     }
@@ -311,13 +313,8 @@ MB_API int mb_decode_step(mb_ctx* c, int32_t n, const int32_t* streams, const in
     return MB_OK;
 }
 
-MB_API int mb_sync(mb_ctx* c, void* cuda_stream) {
-    if (!c) return MB_ERR_ARG;
-    DeviceGuard g(c->cfg.device);
-    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    CK(cudaStreamSynchronize(st), "synchronize");
-    int32_t bits = 0;
-    CK(cudaMemcpy(&bits, c->d_err, sizeof bits, cudaMemcpyDeviceToHost), "read device status");
+// The status of device rejection bits read back (clearing them on the device).
+static int report_bits(mb_ctx* c, int32_t bits) {
     if (!bits) return MB_OK;
     CK(cudaMemset(c->d_err, 0, sizeof(int32_t)), "clear device status");
     if (bits & DERR_TIMEOUT)
@@ -325,6 +322,29 @@ MB_API int mb_sync(mb_ctx* c, void* cuda_stream) {
     return fail(c, MB_ERR_DEVICE, "a kernel rejected an item:%s%s%s", (bits & DERR_STREAM) ? " stream out of range" : "",
                 (bits & DERR_POSITION) ? " position out of range" : "",
                 (bits & DERR_CAPACITY) ? " position beyond a non-wrapping ring" : "");
+}
+
+MB_API int mb_sync(mb_ctx* c, void* cuda_stream) {
+    if (!c) return MB_ERR_ARG;
+    DeviceGuard g(c->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    CK(cudaStreamSynchronize(st), "synchronize");
+    int32_t bits = 0;
+    CK(cudaMemcpy(&bits, c->d_err, sizeof bits, cudaMemcpyDeviceToHost), "read device status");
+    return report_bits(c, bits);
+}
+
+// The end of a host-array call: the status word rides behind the outputs on
+// `copy_st` into pinned memory, so one synchronisation of `st` (which waits for
+// `copy_st`) returns both.
+static int finish_host_call(mb_ctx* c, cudaStream_t st, cudaStream_t copy_st) {
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, copy_st), "read device status");
+    if (copy_st != st) {
+        CK(cudaEventRecord(c->ev_end, copy_st), "copies done");
+        CK(cudaStreamWaitEvent(st, c->ev_end, 0), "copies done");
+    }
+    CK(cudaStreamSynchronize(st), "synchronize");
+    return report_bits(c, *c->h_err);
 }
 
 MB_API int mb_append_attend_host(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams,
@@ -344,7 +364,7 @@ MB_API int mb_append_attend_host(mb_ctx* c, int32_t layer, int32_t n, const int3
     CK(run_decode(c, true, layer, n, c->d_streams, c->d_positions, c->d_qkv, 3 * (int)hid, c->d_out, st),
        "append_attend launch");
     CK(cudaMemcpyAsync(out, c->d_out, n * hid * sizeof(float), cudaMemcpyDeviceToHost, st), "copy out");
-    return mb_sync(c, cuda_stream);
+    return finish_host_call(c, st, st);
 }
 
 MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, const int32_t* positions,
@@ -386,9 +406,7 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
                            c->cp_out),
            "copy out");
     }
-    CK(cudaEventRecord(c->ev_end, c->cp_out), "copies done");
-    CK(cudaStreamWaitEvent(st, c->ev_end, 0), "copies done");
-    return mb_sync(c, cuda_stream);
+    return finish_host_call(c, st, c->cp_out);
 }
 
 MB_API int mb_prefill(mb_ctx* c, int32_t layer, int32_t n, const int32_t* streams, int32_t rows, const float* qkv,

@@ -62,6 +62,7 @@ struct mb_ctx {
     cudaStream_t cp_in = nullptr, cp_out = nullptr;
     std::vector<cudaEvent_t> ev_in, ev_done;  // per layer: inputs landed / layer decoded
     cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+    int32_t* h_err = nullptr;  // pinned copy of d_err, read by the host-array entry points
     bool persistent = false;  // decode with the persistent stream-K kernel (when it applies) instead
     std::string last_error;
 };
