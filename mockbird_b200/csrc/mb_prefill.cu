@@ -150,21 +150,40 @@ __global__ void __launch_bounds__(128) prefill_attn_simt_kernel(RingView r, cons
             vs[j][d + 1] = vv.y;
         }
         __syncthreads();
-        // uniform trip count (the pair shuffle needs the whole warp); the
-        // causal mask key <= query is applied per thread
+        // groups of 8 keys: 8 scores, one rescale of the accumulators, then 8
+        // exponentials and P.V.  Uniform trip counts (the pair shuffle needs the
+        // whole warp); the causal mask key <= query is applied per thread.
         const int jend = min(64, last_key - k0);
-        for (int j = 0; j < jend; j++) {
-            float sdot = 0.f;
+        for (int j0 = 0; j0 < jend; j0 += 8) {
+            float sc[8];
+            float gmax = -INFINITY;
 #pragma unroll
-            for (int d = 0; d < 32; d++) sdot = fmaf(q[d], ks[j][half * 32 + d], sdot);
-            sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
-            if (active && k0 + j <= qi) {
-                const float mn = fmaxf(m, sdot);
-                const float corr = exp2f(m - mn);
-                const float p = exp2f(sdot - mn);
-                l = l * corr + p;
+            for (int u = 0; u < 8; u++) {
+                const int j = j0 + u;
+                float sdot = 0.f;
+                if (j < jend) {
 #pragma unroll
-                for (int d = 0; d < 32; d++) acc[d] = fmaf(p, vs[j][half * 32 + d], acc[d] * corr);
+                    for (int d = 0; d < 32; d++) sdot = fmaf(q[d], ks[j][half * 32 + d], sdot);
+                }
+                sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+                sc[u] = (active && j < jend && k0 + j <= qi) ? sdot : -INFINITY;
+                gmax = fmaxf(gmax, sc[u]);
+            }
+            if (gmax != -INFINITY) {
+                const float mn = fmaxf(m, gmax);
+                const float corr = exp2f(m - mn);  // 0 on the first live group (m = -inf)
+                l *= corr;
+#pragma unroll
+                for (int d = 0; d < 32; d++) acc[d] *= corr;
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const float p = exp2f(sc[u] - mn);  // 0 for masked keys
+                    l += p;
+                    if (j0 + u < jend) {
+#pragma unroll
+                        for (int d = 0; d < 32; d++) acc[d] = fmaf(p, vs[j0 + u][half * 32 + d], acc[d]);
+                    }
+                }
                 m = mn;
             }
         }
