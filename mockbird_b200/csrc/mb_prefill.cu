@@ -100,101 +100,152 @@ __global__ void __launch_bounds__(1024) prefill_rope_kernel(RingView r, const in
 }
 
 // Causal flash attention on CUDA cores for fp32 rings (kind::f16 tensor cores
-// take 16-bit operands; 16-bit rings use mb_prefill_tc.cu): grid (ceil(rows/64),
-// heads, n), 128 threads = 64 queries x 2 halves of the head dim.  K/V tiles of 64
-// slots are staged in shared memory as fp32; each query keeps its running max /
-// sum and 32 accumulators.
-template <typename T>
-__global__ void __launch_bounds__(128) prefill_attn_simt_kernel(RingView r, const int32_t* __restrict__ streams,
-                                                                int rows, const T* __restrict__ q_stage,
+// take 16-bit operands, and tf32 would not meet the fp32 tolerance), blocked the
+// way a CUDA-core GEMM is: grid (ceil(rows/64), heads, n), 256 threads; thread
+// (tq, tk) = (t / 16, t % 16) owns a 4 x 4 block of the 64 x 64 score tile (query
+// rows 4tq.., key columns 4tk..) and a 4 x 4 block of the 64 x 64 output (query
+// rows 4tq.., dims 4tk..).  Q and K are staged transposed ([dim][row]) and V
+// as rows, so each dimension (key) step of QK^T (PV) is two 16-byte shared
+// loads and 16 FMAs.  Row maxima and sums reduce over the 16 threads of a
+// half-warp; P goes through shared memory transposed ([key][query]).
+namespace simt {
+constexpr int BQ = 64, BK = 64, LD = 68;  // tile rows; padded row length (floats)
+struct Smem {
+    float q[HD][LD];   // Q^T, pre-scaled by 0.125 * log2(e)
+    float k[HD][LD];   // K^T of the key tile
+    float v[BK][LD];   // V rows of the key tile
+    float p[BK][LD];   // P^T
+};
+}  // namespace simt
+
+__global__ void __launch_bounds__(256) prefill_attn_simt_kernel(RingView r, const int32_t* __restrict__ streams,
+                                                                int rows, const float* __restrict__ q_stage,
                                                                 float* __restrict__ out) {
-    __shared__ __align__(16) float ks[64][HD];
-    __shared__ __align__(16) float vs[64][HD];
-    const int qt = blockIdx.x, h = blockIdx.y, item = blockIdx.z, tid = threadIdx.x;
+    using namespace simt;
+    extern __shared__ __align__(16) unsigned char simt_raw[];
+    Smem& sm = *reinterpret_cast<Smem*>(simt_raw);
+    const int qt = blockIdx.x, h = blockIdx.y, item = blockIdx.z, t = threadIdx.x;
     const int s = streams[item];
     if (s < 0 || s >= r.streams) return;
-    const int H = r.heads, C = r.capacity;
-    const int qi = qt * 64 + (tid >> 1), half = tid & 1;
-    const bool active = qi < rows;
-    float q[32];
-#pragma unroll
-    for (int d = 0; d < 32; d++) q[d] = 0.f;
-    if (active) {
-        const T* qp = q_stage + (((size_t)item * H + h) * rows + qi) * HD + half * 32;
-#pragma unroll
-        for (int d = 0; d < 32; d += 2) {
-            float2 v = P2<T>::ld(qp + d);
-            q[d] = v.x * (SCALE * LOG2E);
-            q[d + 1] = v.y * (SCALE * LOG2E);
-        }
+    const int H = r.heads, C = r.capacity, q0 = qt * BQ;
+    const int tq = t >> 4, tk = t & 15;
+    const float* qg = q_stage + ((size_t)item * H + h) * rows * HD;
+    const float* kb = reinterpret_cast<const float*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD;
+    const float* vb = reinterpret_cast<const float*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD;
+
+    // Q^T, scaled (rows past `rows` read as 0).  A warp covers 8 rows x 4 chunks
+    // of 16 bytes: 64-byte global segments, 2-way conflicts on the transposed stores.
+    for (int e = t; e < BQ * HD / 4; e += 256) {
+        const int row = ((e >> 5) & 7) * 8 + (e & 7), d = (((e >> 8) * 4) + ((e >> 3) & 3)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q0 + row < rows) v = *reinterpret_cast<const float4*>(qg + (size_t)(q0 + row) * HD + d);
+        const float sc = SCALE * LOG2E;
+        sm.q[d][row] = v.x * sc;
+        sm.q[d + 1][row] = v.y * sc;
+        sm.q[d + 2][row] = v.z * sc;
+        sm.q[d + 3][row] = v.w * sc;
     }
-    float acc[32];
+    float o[4][4], m[4], l[4];
 #pragma unroll
-    for (int d = 0; d < 32; d++) acc[d] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    const T* kb = reinterpret_cast<const T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD;
-    const T* vb = reinterpret_cast<const T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD;
-    const int last_key = min(rows, qt * 64 + 64);  // keys [0, last_key) are needed by this tile
-    for (int k0 = 0; k0 < last_key; k0 += 64) {
-        __syncthreads();
-        for (int e = tid * 2; e < 64 * HD; e += 256) {
-            const int j = e / HD, d = e % HD;
-            float2 kv = make_float2(0.f, 0.f), vv = make_float2(0.f, 0.f);
+    for (int i = 0; i < 4; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; j++) o[i][j] = 0.f;
+    }
+    const int last_key = min(rows, q0 + BQ);  // keys [0, last_key) are needed by this tile
+    for (int k0 = 0; k0 < last_key; k0 += BK) {
+        __syncthreads();  // the previous tile's K, V and P are consumed (and Q^T is written)
+        for (int e = t; e < BK * HD / 4; e += 256) {
+            const int j = ((e >> 5) & 7) * 8 + (e & 7), d = (((e >> 8) * 4) + ((e >> 3) & 3)) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (k0 + j < rows) {
-                kv = P2<T>::ld(kb + (size_t)(k0 + j) * HD + d);
-                vv = P2<T>::ld(vb + (size_t)(k0 + j) * HD + d);
+                kv = *reinterpret_cast<const float4*>(kb + (size_t)(k0 + j) * HD + d);
+                vv = *reinterpret_cast<const float4*>(vb + (size_t)(k0 + j) * HD + d);
             }
-            ks[j][d] = kv.x;
-            ks[j][d + 1] = kv.y;
-            vs[j][d] = vv.x;
-            vs[j][d + 1] = vv.y;
+            sm.k[d][j] = kv.x;
+            sm.k[d + 1][j] = kv.y;
+            sm.k[d + 2][j] = kv.z;
+            sm.k[d + 3][j] = kv.w;
+            *reinterpret_cast<float4*>(&sm.v[j][d]) = vv;
         }
         __syncthreads();
-        // groups of 8 keys: 8 scores, one rescale of the accumulators, then 8
-        // exponentials and P.V.  Uniform trip counts (the pair shuffle needs the
-        // whole warp); the causal mask key <= query is applied per thread.
-        const int jend = min(64, last_key - k0);
-        for (int j0 = 0; j0 < jend; j0 += 8) {
-            float sc[8];
-            float gmax = -INFINITY;
+        // ---- S block: rows 4tq.., keys 4tk..
+        float sc[4][4];
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int j = j0 + u;
-                float sdot = 0.f;
-                if (j < jend) {
+        for (int i = 0; i < 4; i++)
 #pragma unroll
-                    for (int d = 0; d < 32; d++) sdot = fmaf(q[d], ks[j][half * 32 + d], sdot);
-                }
-                sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
-                sc[u] = (active && j < jend && k0 + j <= qi) ? sdot : -INFINITY;
-                gmax = fmaxf(gmax, sc[u]);
+            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < HD; d++) {
+            const float4 qa = *reinterpret_cast<const float4*>(&sm.q[d][4 * tq]);
+            const float4 ka = *reinterpret_cast<const float4*>(&sm.k[d][4 * tk]);
+            const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {ka.x, ka.y, ka.z, ka.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) sc[i][j] = fmaf(qv[i], kv[j], sc[i][j]);
+        }
+        // ---- causal mask (key <= query, key < rows), row maxima over the half-warp
+        float mnew[4], corr[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int qi = q0 + 4 * tq + i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int kj = k0 + 4 * tk + j;
+                if (kj > qi || kj >= rows) sc[i][j] = -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
             }
-            if (gmax != -INFINITY) {
-                const float mn = fmaxf(m, gmax);
-                const float corr = exp2f(m - mn);  // 0 on the first live group (m = -inf)
-                l *= corr;
 #pragma unroll
-                for (int d = 0; d < 32; d++) acc[d] *= corr;
+            for (int o2 = 8; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
+            mnew[i] = fmaxf(m[i], mx);
+            // a row with nothing live yet keeps m = -inf: its p and corr stay 0
+            corr[i] = mnew[i] == -INFINITY ? 1.f : exp2f(m[i] - mnew[i]);
+        }
+        // ---- P = 2^(s - m), row sums, P^T to shared memory
+        float ps[4][4];
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const float p = exp2f(sc[u] - mn);  // 0 for masked keys
-                    l += p;
-                    if (j0 + u < jend) {
+        for (int i = 0; i < 4; i++) {
+            float sum = 0.f;
 #pragma unroll
-                        for (int d = 0; d < 32; d++) acc[d] = fmaf(p, vs[j0 + u][half * 32 + d], acc[d]);
-                    }
-                }
-                m = mn;
+            for (int j = 0; j < 4; j++) {
+                ps[i][j] = sc[i][j] == -INFINITY ? 0.f : exp2f(sc[i][j] - mnew[i]);
+                sum += ps[i][j];
             }
+#pragma unroll
+            for (int o2 = 8; o2 > 0; o2 >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
+            l[i] = l[i] * corr[i] + sum;
+            m[i] = mnew[i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[i][j] *= corr[i];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            *reinterpret_cast<float4*>(&sm.p[4 * tk + j][4 * tq]) = make_float4(ps[0][j], ps[1][j], ps[2][j], ps[3][j]);
+        __syncthreads();
+        // ---- O block += P V: rows 4tq.., dims 4tk..
+        const int kend = min(BK, last_key - k0);
+#pragma unroll 8
+        for (int kk = 0; kk < kend; kk++) {
+            const float4 pa = *reinterpret_cast<const float4*>(&sm.p[kk][4 * tq]);
+            const float4 va = *reinterpret_cast<const float4*>(&sm.v[kk][4 * tk]);
+            const float pv[4] = {pa.x, pa.y, pa.z, pa.w}, vv[4] = {va.x, va.y, va.z, va.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) o[i][j] = fmaf(pv[i], vv[j], o[i][j]);
         }
     }
-    if (active) {
-        float* o = out + ((size_t)item * rows + qi) * H * HD + h * HD + half * 32;
-        const float inv = 1.f / l;
 #pragma unroll
-        for (int d = 0; d < 32; d += 4)
-            *reinterpret_cast<float4*>(o + d) = make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv,
-                                                            acc[d + 3] * inv);
+    for (int i = 0; i < 4; i++) {
+        const int qi = q0 + 4 * tq + i;
+        if (qi < rows) {
+            const float inv = 1.f / l[i];
+            *reinterpret_cast<float4*>(out + ((size_t)item * rows + qi) * H * HD + h * HD + 4 * tk) =
+                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+        }
     }
 }
 
@@ -213,8 +264,21 @@ static cudaError_t prefill_t(const RingView& r, int n, const int32_t* streams, i
     if constexpr (sizeof(T) == 2)  // 16-bit rings: tensor cores (mb_prefill_tc.cu)
         return launch_prefill_attn_tc(std::is_same<T, __nv_bfloat16>::value ? MB_BF16 : MB_F16, r, n, streams, rows,
                                       q_stage, out, st);
-    prefill_attn_simt_kernel<T><<<dim3((rows + 63) / 64, r.heads, n), 128, 0, st>>>(
-        r, streams, rows, reinterpret_cast<const T*>(q_stage), out);
+    if constexpr (sizeof(T) == 4) {
+        static bool attr_set[64] = {};  // per device
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+        if (!attr_set[dev]) {
+            e = cudaFuncSetAttribute(prefill_attn_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sizeof(simt::Smem));
+            if (e != cudaSuccess) return e;
+            attr_set[dev] = true;
+        }
+        prefill_attn_simt_kernel<<<dim3((rows + simt::BQ - 1) / simt::BQ, r.heads, n), 256, sizeof(simt::Smem), st>>>(
+            r, streams, rows, reinterpret_cast<const float*>(q_stage), out);
+    }
     return cudaGetLastError();
 }
 
