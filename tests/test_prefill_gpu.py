@@ -41,11 +41,14 @@ def test_prefill_16bit_444_rows(dtype):
         assert_window_equal(ring, orc, 0, s, 0, s, 443)
 
 
+@pytest.mark.parametrize("dtype", ["f16", "f32"])
 @pytest.mark.parametrize("rows", [1, 2, 63, 64, 65, 128, 257])
-def test_prefill_row_edges(rows):
-    ring, orc, out, ref = _prefill_both("f16", [0], rows, 300, 1, seed=rows, scale=0.5)
+def test_prefill_row_edges(rows, dtype):
+    """Tile edges of both attention kernels: 128-query / 64-key tiles on tensor
+    cores (16-bit rings), 64 x 64 tiles on CUDA cores (fp32 rings)."""
+    ring, orc, out, ref = _prefill_both(dtype, [0], rows, 300, 1, seed=rows, scale=0.5)
     ring.sync()
-    assert max_err(out, ref) < TOL["f16"]
+    assert max_err(out, ref) < TOL[dtype]
     assert_window_equal(ring, orc, 0, 0, 0, 0, rows - 1)
 
 
