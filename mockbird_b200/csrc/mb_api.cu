@@ -424,9 +424,10 @@ MB_API int mb_prefill(mb_ctx* c, int32_t layer, int32_t n, const int32_t* stream
     DeviceGuard g(c->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     void* stage = nullptr;
-    CK(cudaMallocAsync(&stage, prefill_stage_bytes(c->cfg.dtype, n, c->cfg.heads, rows), st), "prefill stage");
+    const size_t stage_bytes = prefill_stage_bytes(c->cfg.dtype, n, c->cfg.heads, rows);
+    if (stage_bytes) CK(cudaMallocAsync(&stage, stage_bytes, st), "prefill stage");
     cudaError_t e = launch_prefill(c->cfg.dtype, ring_view(c, layer), n, streams, rows, qkv, out, stage, st);
-    cudaError_t e2 = cudaFreeAsync(stage, st);
+    cudaError_t e2 = stage ? cudaFreeAsync(stage, st) : cudaSuccess;
     if (e != cudaSuccess) return cuda_fail(c, e, "prefill launch");
     if (e2 != cudaSuccess) return cuda_fail(c, e2, "prefill stage free");
     return MB_OK;

@@ -70,14 +70,6 @@ __device__ __forceinline__ float dot8(uint4 raw, const float4* q2, float acc, __
     return acc;
 }
 
-// RoPE of one (even, odd) pair: out = (a c - b s, b c + a s) with every product
-// and sum rounded separately (no FMA) so the stored K matches a CPU restatement
-// bit for bit (kernels-decode.ts:220-232; partner -v[d+1] / +v[d-1]).
-__device__ __forceinline__ float2 rope_pair(float2 v, float2 cs) {
-    return make_float2(__fadd_rn(__fmul_rn(v.x, cs.x), -__fmul_rn(v.y, cs.y)),
-                       __fadd_rn(__fmul_rn(v.y, cs.x), __fmul_rn(v.x, cs.y)));
-}
-
 // Validate one item against the ring; on failure record why (every thread of
 // the CTA evaluates the same condition, so the early return is uniform).
 __device__ __forceinline__ bool item_ok(const RingView& r, int s, int pos) {

@@ -84,6 +84,16 @@ inline RingView ring_view(const mb_ctx* c, int layer) {
     return v;
 }
 
+// RoPE of one (even, odd) pair: out = (a c - b s, b c + a s) with every product
+// and sum rounded separately (no FMA), so every kernel that ropes a row (decode
+// append, prefill cache, prefill Q) rounds it the same way and the stored K
+// matches a CPU restatement bit for bit (kernels-decode.ts:220-232; partner
+// -v[d+1] / +v[d-1]).
+__device__ __forceinline__ float2 rope_pair(float2 v, float2 cs) {
+    return make_float2(__fadd_rn(__fmul_rn(v.x, cs.x), -__fmul_rn(v.y, cs.y)),
+                       __fadd_rn(__fmul_rn(v.y, cs.x), __fmul_rn(v.x, cs.y)));
+}
+
 // rows of one split-K chunk: 16 KB of K (and 16 KB of V) per chunk
 inline int chunk_rows(int dtype) { return dtype == MB_F32 ? 64 : 128; }
 
@@ -107,7 +117,7 @@ cudaError_t launch_prefill(int dtype, const RingView& r, int n, const int32_t* s
                            const float* qkv, float* out, void* q_stage, cudaStream_t st);
 size_t prefill_stage_bytes(int dtype, int n, int heads, int rows);
 cudaError_t launch_prefill_attn_tc(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
-                                   const void* q_stage, float* out, cudaStream_t st);
+                                   const float* qkv, float* out, cudaStream_t st);
 cudaError_t launch_gather(int dtype, const RingView& r, int stream, int position, void* k_out, void* v_out,
                           int32_t* slots_out, cudaStream_t st);
 cudaError_t launch_ring_write(int dtype, const RingView& r, int stream, int first, int count, const void* k,

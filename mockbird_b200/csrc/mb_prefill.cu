@@ -13,11 +13,6 @@
 
 namespace mb {
 
-__device__ __forceinline__ float2 rope_pair_p(float2 v, float2 cs) {
-    return make_float2(__fadd_rn(__fmul_rn(v.x, cs.x), -__fmul_rn(v.y, cs.y)),
-                       __fadd_rn(__fmul_rn(v.y, cs.x), __fmul_rn(v.x, cs.y)));
-}
-
 template <typename T>
 struct P2;
 template <>
@@ -62,10 +57,11 @@ __device__ __forceinline__ void st4(T* p, float2 a, float2 b) {
 // ROPE_SPLIT_CACHE for all rows of n items: grid (ceil(rows / ROPE_ROWS), n),
 // heads * 16 threads, each owning 4 consecutive dims (two RoPE pairs) of one head
 // in ROPE_ROWS consecutive rows: 16-byte loads of q, k, v and the (cos, sin) pairs.
-// K roped and V raw go to slot = row; the roped Q goes to the stage
-// [n][heads][rows][64] (rounded to the storage dtype for 16-bit rings: the
-// attention kernel consumes Q in that type).  Block 0 of an item also marks the
-// item's slots >= rows empty: a prefill starts an utterance at position 0.
+// K roped and V raw go to slot = row.  For fp32 rings the roped Q goes to the
+// stage [n][heads][rows][64]; for 16-bit rings q_stage is null and the
+// tensor-core attention kernel ropes Q itself as it loads it.  Block 0 of an item
+// also marks the item's slots >= rows empty: a prefill starts an utterance at
+// position 0.
 constexpr int ROPE_ROWS = 4;
 
 template <typename T>
@@ -82,16 +78,18 @@ __global__ void __launch_bounds__(1024) prefill_rope_kernel(RingView r, const in
     const int rend = min(r0 + ROPE_ROWS, rows);
     T* kbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD + d4;
     T* vbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD + d4;
-    T* qbase = q_stage + ((size_t)item * H + h) * rows * HD + d4;
+    T* qbase = q_stage ? q_stage + ((size_t)item * H + h) * rows * HD + d4 : nullptr;
     for (int row = r0; row < rend; row++) {
         const float* src = qkv + ((size_t)item * rows + row) * 3 * HID + h * HD + d4;
         const float4 cs = *reinterpret_cast<const float4*>(r.rope + (size_t)row * 32 + d4 / 2);
-        const float4 q = *reinterpret_cast<const float4*>(src);
         const float4 k = *reinterpret_cast<const float4*>(src + HID);
         const float4 v = *reinterpret_cast<const float4*>(src + 2 * HID);
         const float2 c0 = make_float2(cs.x, cs.y), c1 = make_float2(cs.z, cs.w);
-        st4(qbase + (size_t)row * HD, rope_pair_p(make_float2(q.x, q.y), c0), rope_pair_p(make_float2(q.z, q.w), c1));
-        st4(kbase + (size_t)row * HD, rope_pair_p(make_float2(k.x, k.y), c0), rope_pair_p(make_float2(k.z, k.w), c1));
+        if (q_stage) {
+            const float4 q = *reinterpret_cast<const float4*>(src);
+            st4(qbase + (size_t)row * HD, rope_pair(make_float2(q.x, q.y), c0), rope_pair(make_float2(q.z, q.w), c1));
+        }
+        st4(kbase + (size_t)row * HD, rope_pair(make_float2(k.x, k.y), c0), rope_pair(make_float2(k.z, k.w), c1));
         st4(vbase + (size_t)row * HD, make_float2(v.x, v.y), make_float2(v.z, v.w));
     }
     if (t < rend - r0) r.slot_pos[(size_t)s * C + r0 + t] = r0 + t;
@@ -250,7 +248,7 @@ __global__ void __launch_bounds__(256) prefill_attn_simt_kernel(RingView r, cons
 }
 
 size_t prefill_stage_bytes(int dtype, int n, int heads, int rows) {
-    return (size_t)n * heads * rows * HD * (dtype == MB_F32 ? 4 : 2);
+    return dtype == MB_F32 ? (size_t)n * heads * rows * HD * 4 : 0;  // 16-bit rings rope Q in the attention kernel
 }
 
 template <typename T>
@@ -258,12 +256,12 @@ static cudaError_t prefill_t(const RingView& r, int n, const int32_t* streams, i
                              float* out, void* q_stage, cudaStream_t st) {
     if (r.heads * 16 > 1024) return cudaErrorInvalidConfiguration;
     prefill_rope_kernel<T><<<dim3((rows + ROPE_ROWS - 1) / ROPE_ROWS, n), r.heads * 16, 0, st>>>(
-        r, streams, rows, qkv, reinterpret_cast<T*>(q_stage));
+        r, streams, rows, qkv, sizeof(T) == 4 ? reinterpret_cast<T*>(q_stage) : nullptr);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if constexpr (sizeof(T) == 2)  // 16-bit rings: tensor cores (mb_prefill_tc.cu)
+    if constexpr (sizeof(T) == 2)  // 16-bit rings: tensor cores (mb_prefill_tc.cu), Q roped there
         return launch_prefill_attn_tc(std::is_same<T, __nv_bfloat16>::value ? MB_BF16 : MB_F16, r, n, streams, rows,
-                                      q_stage, out, st);
+                                      qkv, out, st);
     if constexpr (sizeof(T) == 4) {
         static bool attr_set[64] = {};  // per device
         int dev = 0;

@@ -4,7 +4,9 @@
 // flash-attention kernel.
 //
 // One CTA = 128 queries of one (item, head); 4 warps, thread t owns query row t,
-// which is also its TMEM lane.  TMEM holds S (64 columns) and the running O (64
+// which is also its TMEM lane.  The CTA reads its Q rows straight from the fp32
+// QKV input and ropes them itself (the RoPE/cache kernel writes only K and V),
+// so Q never makes a round trip through HBM.  TMEM holds S (64 columns) and the running O (64
 // columns): 128 columns, so four CTAs share an SM's 512, and 48 KB of shared
 // memory each.  Per 64-key tile j (causal: keys up to the CTA's last query):
 //   S_j = Q K_j^T      tcgen05.mma kind::f16, M=128 N=64 K=64, fp32 in TMEM
@@ -46,7 +48,7 @@ struct alignas(1024) TcSmem {
     unsigned char p[QTILE];               // P [128 rows][64 keys]; at the end O dims 0-31
     unsigned char k[KTILE];               // k and v together hold O dims 32-63 at the end
     unsigned char v[KTILE];
-    uint64_t bar_q, bar_k, bar_v, bar_s, bar_o;
+    uint64_t bar_k, bar_v, bar_s, bar_o;
     uint32_t tmem_base;
 };
 constexpr size_t SMEM_BYTES = sizeof(TcSmem) + 1024;  // + alignment slack of the dynamic base
@@ -75,7 +77,7 @@ __device__ __forceinline__ unsigned char* swz(unsigned char* base, int r, int c)
 
 template <bool BF16>
 __global__ void __launch_bounds__(NTHREADS, 4)
-    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
+    prefill_attn_tc_kernel(const float* __restrict__ qkv, const __grid_constant__ CUtensorMap tkv,
                              const __grid_constant__ CUtensorMap tout, RingView r,
                              const int32_t* __restrict__ streams, int rows) {
     extern __shared__ unsigned char smem_raw[];
@@ -87,17 +89,15 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     if (s < 0 || s >= r.streams) return;        // the RoPE/cache kernel has flagged it
     const int H = r.heads, q0 = qt * BM;
     const int ntiles = (min(q0 + BM, rows) + BN - 1) / BN;
-    const int kplane = (s * 2 + 0) * H + h, vplane = (s * 2 + 1) * H + h, qplane = item * H + h;
+    const int kplane = (s * 2 + 0) * H + h, vplane = (s * 2 + 1) * H + h;
 
     if (warp == 0) tmem_alloc(&sm.tmem_base, TMEM_COLS);
     if (tid == 0) {
-        mbar_init(&sm.bar_q, 1);
         mbar_init(&sm.bar_k, 1);
         mbar_init(&sm.bar_v, 1);
         mbar_init(&sm.bar_s, 1);
         mbar_init(&sm.bar_o, 1);
         fence_mbar_init();
-        prefetch_tmap(&tq);
         prefetch_tmap(&tkv);
         prefetch_tmap(&tout);
     }
@@ -109,8 +109,6 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     // issue/complete counts per barrier (identical in every thread: the control flow is uniform)
     int k_issued = 1, k_done = 0, v_issued = 1, v_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
     if (tid == 0) {
-        mbar_expect_tx(&sm.bar_q, QTILE);
-        tma_load_3d(sm.q, &tq, 0, q0, qplane, &sm.bar_q);
         mbar_expect_tx(&sm.bar_k, KTILE);
         tma_load_3d(sm.k, &tkv, 0, 0, kplane, &sm.bar_k);
         mbar_expect_tx(&sm.bar_v, KTILE);
@@ -124,9 +122,41 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
     float m_run = -INFINITY, l_run = 0.f;
 
+    // Q: the CTA's 128 rows from the fp32 QKV input, roped at position = row with
+    // the cache kernel's rope_pair (so Q rounds exactly as a staged copy would),
+    // converted to 16 bits and stored as the 128-byte-swizzled K-major tile the
+    // QK^T MMA reads.  Half a warp per row, lane l16 owning dims 4*l16..4*l16+3
+    // (two RoPE pairs): 256-byte coalesced reads of the row and of its (cos, sin)
+    // pairs.  Rows past the last are zero, as a zero-filled TMA load leaves them.
+    {
+        const int HID = H * HD, lane = tid & 31, l16 = lane & 15;
+        const float* qbase = qkv + (size_t)item * rows * 3 * HID + h * HD + 4 * l16;
+#pragma unroll
+        for (int it = 0; it < 16; it += 4) {
+            float4 qv[4], cs[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int gq = q0 + warp * 32 + 2 * (it + u) + (lane >> 4);
+                qv[u] = cs[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (gq < rows) {
+                    qv[u] = *reinterpret_cast<const float4*>(qbase + (size_t)gq * 3 * HID);
+                    cs[u] = *reinterpret_cast<const float4*>(r.rope + (size_t)gq * 32 + 2 * l16);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int rr = warp * 32 + 2 * (it + u) + (lane >> 4);
+                const float2 a = rope_pair(make_float2(qv[u].x, qv[u].y), make_float2(cs[u].x, cs[u].y));
+                const float2 b = rope_pair(make_float2(qv[u].z, qv[u].w), make_float2(cs[u].z, cs[u].w));
+                *reinterpret_cast<uint2*>(swz(sm.q, rr, l16 >> 1) + (l16 & 1) * 8) =
+                    make_uint2(pack2<BF16>(a.x, a.y), pack2<BF16>(b.x, b.y));
+            }
+        }
+    }
+    fence_async_smem();  // the Q stores, seen by the tensor core
+
     // S_0 = Q K_0^T
-    bool ok = __syncthreads_and(mbar_wait(&sm.bar_q, 0, WAIT_LIMIT) && mbar_wait(&sm.bar_k, 0, WAIT_LIMIT));
-    const bool q_done = ok;
+    bool ok = __syncthreads_and(mbar_wait(&sm.bar_k, 0, WAIT_LIMIT));
     if (ok) {
         k_done++;
         if (tid == 0) {
@@ -282,7 +312,6 @@ __global__ void __launch_bounds__(NTHREADS, 4)
         // gave up: record it, then let everything in flight land before the
         // shared memory and TMEM of this CTA are released
         atomicOr(r.err, DERR_TIMEOUT);
-        if (!q_done) mbar_wait(&sm.bar_q, 0, WAIT_LIMIT);
         for (; k_done < k_issued; k_done++) mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT);
         for (; v_done < v_issued; v_done++) mbar_wait(&sm.bar_v, v_done & 1, WAIT_LIMIT);
         for (; s_done < s_issued; s_done++) mbar_wait(&sm.bar_s, s_done & 1, WAIT_LIMIT);
@@ -341,11 +370,10 @@ bool make_out_map(CUtensorMap* m, float* out, int rows, int n, int width) {
 }
 
 template <bool BF16>
-cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows, const void* q_stage, float* out,
+cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows, const float* qkv, float* out,
                         cudaStream_t st) {
-    CUtensorMap tq, tkv, tout;
-    if (!make_map(&tq, BF16, q_stage, rows, n * r.heads, (size_t)rows * HD * 2, BM) ||
-        !make_map(&tkv, BF16, r.kv, rows, r.streams * 2 * r.heads, (size_t)r.capacity * HD * 2, BN) ||
+    CUtensorMap tkv, tout;
+    if (!make_map(&tkv, BF16, r.kv, rows, r.streams * 2 * r.heads, (size_t)r.capacity * HD * 2, BN) ||
         !make_out_map(&tout, out, rows, n, r.heads * HD))
         return cudaErrorInvalidValue;
     static bool attr_set[64] = {};  // per device
@@ -360,16 +388,16 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
         attr_set[dev] = true;
     }
     dim3 grid((rows + BM - 1) / BM, r.heads, n);
-    prefill_attn_tc_kernel<BF16><<<grid, NTHREADS, SMEM_BYTES, st>>>(tq, tkv, tout, r, streams, rows);
+    prefill_attn_tc_kernel<BF16><<<grid, NTHREADS, SMEM_BYTES, st>>>(qkv, tkv, tout, r, streams, rows);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_prefill_attn_tc(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
-                                     const void* q_stage, float* out, cudaStream_t st) {
-    return dtype == MB_BF16 ? launch_tc<true>(r, n, streams, rows, q_stage, out, st)
-                            : launch_tc<false>(r, n, streams, rows, q_stage, out, st);
+                                     const float* qkv, float* out, cudaStream_t st) {
+    return dtype == MB_BF16 ? launch_tc<true>(r, n, streams, rows, qkv, out, st)
+                            : launch_tc<false>(r, n, streams, rows, qkv, out, st);
 }
 
 }  // namespace mb
