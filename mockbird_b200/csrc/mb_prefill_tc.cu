@@ -75,6 +75,46 @@ __device__ __forceinline__ unsigned char* swz(unsigned char* base, int r, int c)
     return base + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
+// Loads of eight row pairs of Q (pairs p0..p0+7 of this warp's 32 rows; the
+// half-warp's rows are grow0 + 2p): q dims 4*l16..4*l16+3 and their two (cos,
+// sin) pairs; rows past `rows` read as zero.
+__device__ __forceinline__ void q_rows_load(const float* qkv_row0, const float2* rope, int grow0, int rows, int l16,
+                                            int HID, float4 (&qv)[8], float4 (&cs)[8], int p0) {
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int gq = grow0 + 2 * (p0 + u);
+        qv[u] = cs[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (gq < rows) {
+            qv[u] = *reinterpret_cast<const float4*>(qkv_row0 + (size_t)gq * 3 * HID);
+            cs[u] = *reinterpret_cast<const float4*>(rope + (size_t)gq * 32 + 2 * l16);
+        }
+    }
+}
+
+// An L2 prefetch of the q rows of pairs p0..p0+7 (no registers held)
+__device__ __forceinline__ void q_rows_prefetch(const float* qkv_row0, int grow0, int rows, int HID, int p0) {
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int gq = grow0 + 2 * (p0 + u);
+        if (gq < rows) asm volatile("prefetch.global.L2 [%0];" ::"l"(qkv_row0 + (size_t)gq * 3 * HID));
+    }
+}
+
+// RoPE of the loaded pairs and their 8-byte stores into the swizzled Q tile
+template <bool BF16>
+__device__ __forceinline__ void q_rows_store(unsigned char* q, int warp, int lane, const float4 (&qv)[8],
+                                             const float4 (&cs)[8], int p0) {
+    const int l16 = lane & 15;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int rr = warp * 32 + 2 * (p0 + u) + (lane >> 4);
+        const float2 a = rope_pair(make_float2(qv[u].x, qv[u].y), make_float2(cs[u].x, cs[u].y));
+        const float2 b = rope_pair(make_float2(qv[u].z, qv[u].w), make_float2(cs[u].z, cs[u].w));
+        *reinterpret_cast<uint2*>(swz(q, rr, l16 >> 1) + (l16 & 1) * 8) =
+            make_uint2(pack2<BF16>(a.x, a.y), pack2<BF16>(b.x, b.y));
+    }
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(NTHREADS, 4)
     prefill_attn_tc_kernel(const float* __restrict__ qkv, const __grid_constant__ CUtensorMap tkv,
@@ -90,6 +130,20 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     const int H = r.heads, q0 = qt * BM;
     const int ntiles = (min(q0 + BM, rows) + BN - 1) / BN;
     const int kplane = (s * 2 + 0) * H + h, vplane = (s * 2 + 1) * H + h;
+
+    // Q: the CTA's 128 rows come straight from the fp32 QKV input and are roped
+    // here (position = row), with the cache kernel's rope_pair so they round
+    // exactly as a staged copy would, then stored in 16 bits as the
+    // 128-byte-swizzled K-major tile the QK^T MMA reads.  Half a warp per row,
+    // lane l16 owning dims 4*l16..4*l16+3 (two RoPE pairs): 256-byte coalesced
+    // reads of the row and of its (cos, sin) pairs.  The loads of the first half
+    // of the rows, and an L2 prefetch of the second, are issued before the setup
+    // below, so their latency overlaps it.
+    const int HID = H * HD, lane = tid & 31, l16 = lane & 15;
+    const float* qkv_row0 = qkv + (size_t)item * rows * 3 * HID + h * HD + 4 * l16;
+    float4 qv[8], cs[8];
+    q_rows_load(qkv_row0, r.rope, q0 + warp * 32 + (lane >> 4), rows, l16, HID, qv, cs, 0);
+    q_rows_prefetch(qkv_row0, q0 + warp * 32 + (lane >> 4), rows, HID, 8);
 
     if (warp == 0) tmem_alloc(&sm.tmem_base, TMEM_COLS);
     if (tid == 0) {
@@ -122,37 +176,11 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
     float m_run = -INFINITY, l_run = 0.f;
 
-    // Q: the CTA's 128 rows from the fp32 QKV input, roped at position = row with
-    // the cache kernel's rope_pair (so Q rounds exactly as a staged copy would),
-    // converted to 16 bits and stored as the 128-byte-swizzled K-major tile the
-    // QK^T MMA reads.  Half a warp per row, lane l16 owning dims 4*l16..4*l16+3
-    // (two RoPE pairs): 256-byte coalesced reads of the row and of its (cos, sin)
-    // pairs.  Rows past the last are zero, as a zero-filled TMA load leaves them.
-    {
-        const int HID = H * HD, lane = tid & 31, l16 = lane & 15;
-        const float* qbase = qkv + (size_t)item * rows * 3 * HID + h * HD + 4 * l16;
-#pragma unroll
-        for (int it = 0; it < 16; it += 4) {
-            float4 qv[4], cs[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int gq = q0 + warp * 32 + 2 * (it + u) + (lane >> 4);
-                qv[u] = cs[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (gq < rows) {
-                    qv[u] = *reinterpret_cast<const float4*>(qbase + (size_t)gq * 3 * HID);
-                    cs[u] = *reinterpret_cast<const float4*>(r.rope + (size_t)gq * 32 + 2 * l16);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int rr = warp * 32 + 2 * (it + u) + (lane >> 4);
-                const float2 a = rope_pair(make_float2(qv[u].x, qv[u].y), make_float2(cs[u].x, cs[u].y));
-                const float2 b = rope_pair(make_float2(qv[u].z, qv[u].w), make_float2(cs[u].z, cs[u].w));
-                *reinterpret_cast<uint2*>(swz(sm.q, rr, l16 >> 1) + (l16 & 1) * 8) =
-                    make_uint2(pack2<BF16>(a.x, a.y), pack2<BF16>(b.x, b.y));
-            }
-        }
-    }
+    // Q: the first half of the rows roped and stored, then the second half
+    // loaded, roped and stored
+    q_rows_store<BF16>(sm.q, warp, lane, qv, cs, 0);
+    q_rows_load(qkv_row0, r.rope, q0 + warp * 32 + (lane >> 4), rows, l16, HID, qv, cs, 8);
+    q_rows_store<BF16>(sm.q, warp, lane, qv, cs, 8);
     fence_async_smem();  // the Q stores, seen by the tensor core
 
     // S_0 = Q K_0^T
