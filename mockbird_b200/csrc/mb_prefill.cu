@@ -67,6 +67,9 @@ constexpr int ROPE_ROWS = 4;
 template <typename T>
 __global__ void __launch_bounds__(1024) prefill_rope_kernel(RingView r, const int32_t* __restrict__ streams, int rows,
                                                             const float* __restrict__ qkv, T* q_stage) {
+    // the attention kernel that follows may start its Q prologue now; it reads
+    // what this kernel writes only after this grid has completed
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int item = blockIdx.y, r0 = blockIdx.x * ROPE_ROWS;
     const int s = streams[item];
     if (s < 0 || s >= r.streams) {

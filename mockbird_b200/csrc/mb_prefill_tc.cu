@@ -163,6 +163,12 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     // issue/complete counts per barrier (identical in every thread: the control flow is uniform)
     int k_issued = 1, k_done = 0, v_issued = 1, v_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
     if (tid == 0) {
+        // The kernel is a programmatic dependent of the RoPE/cache kernel: all of
+        // the above (Q loads, setup) may run during that kernel's tail, but the
+        // K/V it writes are read only after it has completed.  Thread 0 is the
+        // only thread that reads or writes global memory from here on (the K/V
+        // loads and the output stores are its TMA copies).
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         mbar_expect_tx(&sm.bar_k, KTILE);
         tma_load_3d(sm.k, &tkv, 0, 0, kplane, &sm.bar_k);
         mbar_expect_tx(&sm.bar_v, KTILE);
@@ -415,9 +421,18 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    dim3 grid((rows + BM - 1) / BM, r.heads, n);
-    prefill_attn_tc_kernel<BF16><<<grid, NTHREADS, SMEM_BYTES, st>>>(qkv, tkv, tout, r, streams, rows);
-    return cudaGetLastError();
+    // programmatic dependent of the RoPE/cache kernel launched just before it
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows + BM - 1) / BM, r.heads, n);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_attn_tc_kernel<BF16>, (const float*)qkv, tkv, tout, r, streams, rows);
 }
 
 }  // namespace
