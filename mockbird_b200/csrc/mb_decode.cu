@@ -134,7 +134,7 @@ template <typename T, bool APPEND>
 __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, const int32_t* __restrict__ streams,
                                                      const int32_t* __restrict__ positions,
                                                      const float* __restrict__ q_in, int q_stride, void* out,
-                                                     int out_bf16) {
+                                                     int out_bf16, int pf_dist) {
     using S = DecodeShape<T>;
     constexpr int ROWS = S::ROWS, TPR = S::TPR, RB = S::ROW_BYTES;
     __shared__ __align__(128) unsigned char sk[ROWS * RB];
@@ -180,6 +180,28 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         mbar_expect_tx(&bar[1], bytes);
         if (a > 0) bulk_g2s(sv, vbase + (size_t)j0 * HD, (uint32_t)a * RB, &bar[1]);
         if (b < rows) bulk_g2s(sv + b * RB, vbase + (size_t)(j0 + b) * HD, (uint32_t)(rows - b) * RB, &bar[1]);
+    }
+
+    // An idle thread asks L2 for the chunk of the CTA pf_dist places later in
+    // launch order (part of a wave of resident CTAs ahead), so that CTA's bulk
+    // copies find it there.  Every byte still comes from HBM once.
+    if (pf_dist > 0 && tid == 64) {
+        const unsigned gx = gridDim.x, gy = gridDim.y;
+        const unsigned t = blockIdx.x + gx * (blockIdx.y + gy * blockIdx.z) + (unsigned)pf_dist;
+        if (t < gx * gy * gridDim.z) {
+            const int c2 = (int)(t % gx), h2 = (int)((t / gx) % gy), it2 = (int)(t / (gx * gy));
+            const int s2 = streams[it2], p2 = positions[it2];
+            if (s2 >= 0 && s2 < r.streams && p2 >= 0) {
+                const int count2 = min(p2 + 1, C), j2 = c2 * ROWS;
+                if (j2 < count2) {
+                    const uint32_t bytes2 = (uint32_t)min(ROWS, count2 - j2) * RB;
+                    const T* k2 = reinterpret_cast<const T*>(r.kv) + (((size_t)s2 * 2 + 0) * H + h2) * (size_t)C * HD;
+                    const T* v2 = reinterpret_cast<const T*>(r.kv) + (((size_t)s2 * 2 + 1) * H + h2) * (size_t)C * HD;
+                    bulk_prefetch_l2(k2 + (size_t)j2 * HD, bytes2);
+                    bulk_prefetch_l2(v2 + (size_t)j2 * HD, bytes2);
+                }
+            }
+        }
     }
 
     // query (roped here when appending) and, in the chunk holding the new slot,
@@ -457,6 +479,29 @@ cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_
     }
 }
 
+// CTAs between a CTA and the one whose chunk it prefetches into L2 (0: none).
+// 1.5 x the SM count (222 on a B200): measured best on the config-2 ring (8
+// chunks per window: +3.6 % at full windows) and on config 4 (16 chunks: +1.2 %).
+// Off for rings of more than 16 chunks: with long, uneven windows most CTAs a
+// fixed distance ahead exit empty, and config 5 (32 chunks) lost 0.4-1.1 %.
+// MOCKBIRD_DECODE_PREFETCH=<distance> overrides the choice.
+static int decode_prefetch_distance(int max_splits) {
+    static const int forced = [] {
+        const char* v = getenv("MOCKBIRD_DECODE_PREFETCH");
+        return v ? atoi(v) : -1;
+    }();
+    if (forced >= 0) return forced;
+    if (max_splits > 16) return 0;
+    static int sms[64] = {};  // per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        sms[dev] = 0;
+        return 0;
+    }
+    return sms[dev] * 3 / 2;
+}
+
 template <typename T>
 static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, int n, const int32_t* streams,
                             const int32_t* positions, const float* q, int q_stride, void* out, cudaStream_t st,
@@ -483,8 +528,10 @@ static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, in
     cfg.attrs = attr;
     cfg.numAttrs = overlap_previous ? 1 : 0;
     if (append)
-        return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out, ob);
-    return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out, ob);
+        return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out, ob,
+                                  decode_prefetch_distance(s.max_splits));
+    return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out, ob,
+                              decode_prefetch_distance(s.max_splits));
 }
 
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
