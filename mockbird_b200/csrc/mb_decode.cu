@@ -376,20 +376,40 @@ __global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int
     const T* kbase = reinterpret_cast<const T*>(r.kv) + (((size_t)s * 2 + 0) * H + (head_ok ? h : 0)) * (size_t)C * HD;
     const T* vbase = reinterpret_cast<const T*>(r.kv) + (((size_t)s * 2 + 1) * H + (head_ok ? h : 0)) * (size_t)C * HD;
 
+    // The reads that depend only on (s, pos) go out together, before the first
+    // store: the q, k, v of the new row and the K row and stored position of
+    // slot `lane`.  The new slot's old K row and position are read too and
+    // replaced by the on-chip ones.
+    constexpr int NV = HD * (int)sizeof(T) / 16;  // 16-byte pieces of a row
+    uint4 raw[NV];
+    int stored = -1;
+    float2 qv = make_float2(0.f, 0.f), kin = qv, vin = qv, cs = qv;
+    if (head_ok) {
+        qv = *reinterpret_cast<const float2*>(row + h * HD + 2 * lane);
+        if (APPEND) {
+            cs = r.rope[(size_t)pos * 32 + lane];
+            kin = *reinterpret_cast<const float2*>(row + HID + h * HD + 2 * lane);
+            vin = *reinterpret_cast<const float2*>(row + 2 * HID + h * HD + 2 * lane);
+        }
+        if (lane < count) {
+            const uint4* kp = reinterpret_cast<const uint4*>(kbase + (size_t)lane * HD);
+#pragma unroll
+            for (int v = 0; v < NV; v++) raw[v] = kp[v];
+            stored = r.slot_pos[(size_t)s * C + lane];
+        }
+    }
+
     float2 vnew = make_float2(0.f, 0.f);
     if (head_ok) {
-        float2 qv = *reinterpret_cast<const float2*>(row + h * HD + 2 * lane);
         if (APPEND) {
-            const float2 cs = r.rope[(size_t)pos * 32 + lane];
             qv = rope_pair(qv, cs);
-            const float2 kr = rope_pair(*reinterpret_cast<const float2*>(row + HID + h * HD + 2 * lane), cs);
-            const float2 vv = *reinterpret_cast<const float2*>(row + 2 * HID + h * HD + 2 * lane);
+            const float2 kr = rope_pair(kin, cs);
             Store<T>::store2(const_cast<T*>(kbase) + (size_t)newslot * HD + 2 * lane, kr);
-            Store<T>::store2(const_cast<T*>(vbase) + (size_t)newslot * HD + 2 * lane, vv);
+            Store<T>::store2(const_cast<T*>(vbase) + (size_t)newslot * HD + 2 * lane, vin);
             const float2 kq = Store<T>::round2(kr);
             kn[warp][2 * lane] = kq.x;
             kn[warp][2 * lane + 1] = kq.y;
-            vnew = Store<T>::round2(vv);
+            vnew = Store<T>::round2(vin);
             if (h == 0 && lane == 0) r.slot_pos[(size_t)s * C + newslot] = pos;
         }
         qs[warp][2 * lane] = qv.x;
@@ -397,17 +417,10 @@ __global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int
     }
     __syncwarp();
 
-    // ---- lane j: the score of slot j (kernels-decode.ts:622-623 liveness).  The
-    // slot's position and its K row (16-byte loads) are read together; the row
-    // of the new slot is read too but replaced by the on-chip one.
+    // ---- lane j: the score of slot j (kernels-decode.ts:622-623 liveness)
     float sc = -INFINITY;
     if (head_ok && lane < count) {
-        constexpr int NV = HD * (int)sizeof(T) / 16;  // 16-byte pieces of a row
-        uint4 raw[NV];
-        const uint4* kp = reinterpret_cast<const uint4*>(kbase + (size_t)lane * HD);
-#pragma unroll
-        for (int v = 0; v < NV; v++) raw[v] = kp[v];
-        const int stored = (APPEND && lane == newslot) ? pos : r.slot_pos[(size_t)s * C + lane];
+        if (APPEND && lane == newslot) stored = pos;
         if (stored >= 0 && pos - stored >= 0 && pos - stored < C) {
             float dot = 0.f;
             if (APPEND && lane == newslot) {
