@@ -22,68 +22,16 @@ using bf16 = __nv_bfloat16;
 // ---------------------------------------------------------------- kernels
 
 // One warp per row: mean, then the mean squared deviation (the two passes of
-// LAYERNORM_1), out = (x - mean) * rsqrt(var + 1e-5) * w + b.  In place is fine:
-// the row is in registers before it is written.
+// LAYERNORM_1), out = (x - mean) * rsqrt(var + 1e-5) * w + b (mb::dec::ln_load /
+// ln_apply).  In place is fine: the row is in registers before it is written.
 template <typename TO, int PER>
 __global__ void layernorm_rows(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                                TO* __restrict__ y, int rows, int width) {
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const float* xr = x + (size_t)row * width;
     float v[PER];
-    float sum = 0.f;
-    if constexpr (PER % 4 == 0) {  // 16-byte loads: lane owns columns 4 lane + 128 k .. + 3
-#pragma unroll
-        for (int k = 0; k < PER / 4; k++) {
-            const float4 q = *reinterpret_cast<const float4*>(xr + 4 * lane + 128 * k);
-            v[4 * k] = q.x, v[4 * k + 1] = q.y, v[4 * k + 2] = q.z, v[4 * k + 3] = q.w;
-        }
-#pragma unroll
-        for (int i = 0; i < PER; i++) sum += v[i];
-    } else {
-#pragma unroll
-        for (int i = 0; i < PER; i++) {
-            v[i] = xr[lane + 32 * i];
-            sum += v[i];
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = sum / (float)width;
-    float sq = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER; i++) {
-        const float d = v[i] - mean;
-        sq += d * d;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float inv = rsqrtf(sq / (float)width + 1e-5f);
-    TO* yr = y + (size_t)row * width;
-    if constexpr (PER % 4 == 0) {  // 16-byte weight/bias loads, 4-element stores
-#pragma unroll
-        for (int k = 0; k < PER / 4; k++) {
-            const int c = 4 * lane + 128 * k;
-            const float4 wk = *reinterpret_cast<const float4*>(w + c), bk = *reinterpret_cast<const float4*>(b + c);
-            const float r0 = (v[4 * k] - mean) * inv * wk.x + bk.x, r1 = (v[4 * k + 1] - mean) * inv * wk.y + bk.y;
-            const float r2 = (v[4 * k + 2] - mean) * inv * wk.z + bk.z, r3 = (v[4 * k + 3] - mean) * inv * wk.w + bk.w;
-            if constexpr (sizeof(TO) == 4) {
-                *reinterpret_cast<float4*>(yr + c) = make_float4(r0, r1, r2, r3);
-            } else {
-                const __nv_bfloat162 lo = __floats2bfloat162_rn(r0, r1), hi = __floats2bfloat162_rn(r2, r3);
-                uint2 u;
-                u.x = *reinterpret_cast<const uint32_t*>(&lo);
-                u.y = *reinterpret_cast<const uint32_t*>(&hi);
-                *reinterpret_cast<uint2*>(yr + c) = u;
-            }
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < PER; i++) {
-            const int c = lane + 32 * i;
-            yr[c] = (TO)((v[i] - mean) * inv * w[c] + b[c]);
-        }
-    }
+    mb::dec::ln_load<PER>(x + (size_t)row * width, lane, v);
+    mb::dec::ln_apply<TO, PER>(v, w, b, y + (size_t)row * width, width, lane);
 }
 
 // tanh on the MUFU unit (tanh.approx.f32, max relative error about 2^-11): the
@@ -212,14 +160,15 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const
 }
 
 int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
-        cudaStream_t st) {
+        cudaStream_t st, bool ln1_ready) {
     mb_ctx* c = d->ctx;
     const int h = d->hid, f = d->ffn;
     int rc = MB_OK;
     cudaError_t e = cudaSuccess;
     for (int l = 0; l < d->layers && rc == MB_OK && e == cudaSuccess; l++) {
         const auto& W = d->L[l];
-        if ((e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess) break;
+        if (!(l == 0 && ln1_ready) && (e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess)
+            break;
         if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, false, st))) break;
         // the context rows go straight to the bf16 input of the c_proj GEMM
         if ((e = mb::launch_decode(c->cfg.dtype, true, mb::ring_view(c, l), c->scratch, n, streams, positions, d->qkv,

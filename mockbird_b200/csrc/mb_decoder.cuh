@@ -62,9 +62,90 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const
 
 // The layers of mb_decoder_step on `hidden` [n][hid], then ln_f: into `lnf_bf16`
 // [n][hid] (bf16) when it is non-null, else into `hidden` in place (fp32).
+// ln1_ready: the caller has already written layer 0's LN1 of `hidden` into
+// d->xb (bf16), so that LayerNorm is skipped.
 // Arguments are the caller's to check; the current device must be the context's.
 int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
-        cudaStream_t st);
+        cudaStream_t st, bool ln1_ready = false);
+
+// ---- LayerNorm of one row by one warp (LAYERNORM_1: mean, then the mean squared
+// deviation, out = (x - mean) * rsqrt(var + 1e-5) * w + b), width = 32 * PER.
+// The row sits in registers between ln_load and ln_apply, so a kernel may also
+// store it (ln_store) or take it from elsewhere.
+
+// lane's PER values: columns 4 lane + 128 k .. + 3 when PER % 4 == 0 (16-byte
+// loads), else lane + 32 i
+template <int PER>
+__device__ __forceinline__ void ln_load(const float* xr, int lane, float (&v)[PER]) {
+    if constexpr (PER % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < PER / 4; k++) {
+            const float4 q = *reinterpret_cast<const float4*>(xr + 4 * lane + 128 * k);
+            v[4 * k] = q.x, v[4 * k + 1] = q.y, v[4 * k + 2] = q.z, v[4 * k + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; i++) v[i] = xr[lane + 32 * i];
+    }
+}
+
+// the row back to memory in ln_load's layout (fp32)
+template <int PER>
+__device__ __forceinline__ void ln_store(float* yr, int lane, const float (&v)[PER]) {
+    if constexpr (PER % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < PER / 4; k++)
+            *reinterpret_cast<float4*>(yr + 4 * lane + 128 * k) =
+                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; i++) yr[lane + 32 * i] = v[i];
+    }
+}
+
+template <typename TO, int PER>
+__device__ __forceinline__ void ln_apply(const float (&v)[PER], const float* __restrict__ w,
+                                         const float* __restrict__ b, TO* yr, int width, int lane) {
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) sum += v[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / (float)width;
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const float d = v[i] - mean;
+        sq += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float inv = rsqrtf(sq / (float)width + 1e-5f);
+    if constexpr (PER % 4 == 0) {  // 16-byte weight/bias loads, 4-element stores
+#pragma unroll
+        for (int k = 0; k < PER / 4; k++) {
+            const int c = 4 * lane + 128 * k;
+            const float4 wk = *reinterpret_cast<const float4*>(w + c), bk = *reinterpret_cast<const float4*>(b + c);
+            const float r0 = (v[4 * k] - mean) * inv * wk.x + bk.x, r1 = (v[4 * k + 1] - mean) * inv * wk.y + bk.y;
+            const float r2 = (v[4 * k + 2] - mean) * inv * wk.z + bk.z, r3 = (v[4 * k + 3] - mean) * inv * wk.w + bk.w;
+            if constexpr (sizeof(TO) == 4) {
+                *reinterpret_cast<float4*>(yr + c) = make_float4(r0, r1, r2, r3);
+            } else {
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(r0, r1), hi = __floats2bfloat162_rn(r2, r3);
+                uint2 u;
+                u.x = *reinterpret_cast<const uint32_t*>(&lo);
+                u.y = *reinterpret_cast<const uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(yr + c) = u;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int c = lane + 32 * i;
+            yr[c] = (TO)((v[i] - mean) * inv * w[c] + b[c]);
+        }
+    }
+}
 
 // y = bf16(x), n elements.
 cudaError_t to_bf16(const float* x, bf16* y, size_t n, cudaStream_t st);

@@ -38,13 +38,20 @@ namespace {
 using bf16 = __nv_bfloat16;
 
 // x[i] = the step's input row (EMBED_ROW_LOCAL, kernels-decode.ts:96-124, modes
-// 1 and 2; mode "hidden" is the writeBuffer of decode.ts:792).  Tokens come from
-// argmax_penalty_kernel and are always in [0, codes); the clamp only keeps a
-// corrupted token from addressing outside the table.
-__global__ void local_embed_kernel(int step, int h, int channels, int codes, const float* __restrict__ hin,
-                                   const float* __restrict__ wte_slot, const float* __restrict__ emb,
-                                   const int32_t* __restrict__ tokens, float* __restrict__ x) {
-    const int i = blockIdx.x;
+// 1 and 2; mode "hidden" is the writeBuffer of decode.ts:792), and then the local
+// layer's LN1 of it, one warp per item: the row goes to x (fp32, the residual
+// stream) and LN1(row) to xb (bf16, the QKV GEMM's input), so the layer starts
+// at its GEMM.  Same arithmetic as the separate LayerNorm (mb::dec::ln_apply).
+// Tokens come from argmax_penalty_kernel and are always in [0, codes); the clamp
+// only keeps a corrupted token from addressing outside the table.
+template <int PER>
+__global__ void local_embed_ln_kernel(int n, int step, int h, int channels, int codes, const float* __restrict__ hin,
+                                      const float* __restrict__ wte_slot, const float* __restrict__ emb,
+                                      const int32_t* __restrict__ tokens, const float* __restrict__ ln_w,
+                                      const float* __restrict__ ln_b, float* __restrict__ x,
+                                      __nv_bfloat16* __restrict__ xb) {
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (i >= n) return;
     const float* src;
     if (step == 0) {
         src = hin + (size_t)i * h;
@@ -56,9 +63,10 @@ __global__ void local_embed_kernel(int step, int h, int channels, int codes, con
         tok = min(max(tok, 0), codes - 1);
         src = emb + ((size_t)ch * codes + tok) * h;
     }
-    float4* dst = reinterpret_cast<float4*>(x + (size_t)i * h);
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    for (int d = threadIdx.x; d < h / 4; d += blockDim.x) dst[d] = s4[d];
+    float v[PER];
+    mb::dec::ln_load<PER>(src, lane, v);
+    mb::dec::ln_store<PER>(x + (size_t)i * h, lane, v);
+    mb::dec::ln_apply<__nv_bfloat16, PER>(v, ln_w, ln_b, xb + (size_t)i * h, h, lane);
 }
 
 // TEXT_HEAD_DECIDE (kernels-decode.ts:487-535): the dot products of ln_f(x) with
@@ -203,12 +211,31 @@ int enqueue_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
     const int h = lh->h, steps = lh->channels + 1;
     const int warps = 4, wblocks = (n + warps - 1) / warps;
     for (int step = 0; step < steps; step++) {
-        local_embed_kernel<<<n, 192, 0, st>>>(step, h, lh->channels, lh->codes, lh->hin, lh->wte_slot, lh->emb,
-                                              lh->tok, lh->x);
+        {
+            const int eb = (n + 1) / 2;  // two warps (items) per block
+            const float *w1 = lh->dec->L[0].ln1_w, *b1 = lh->dec->L[0].ln1_b;
+            switch (h / 32) {
+                case 2:
+                    local_embed_ln_kernel<2><<<eb, 64, 0, st>>>(n, step, h, lh->channels, lh->codes, lh->hin,
+                                                                lh->wte_slot, lh->emb, lh->tok, w1, b1, lh->x,
+                                                                lh->dec->xb);
+                    break;
+                case 8:
+                    local_embed_ln_kernel<8><<<eb, 64, 0, st>>>(n, step, h, lh->channels, lh->codes, lh->hin,
+                                                                lh->wte_slot, lh->emb, lh->tok, w1, b1, lh->x,
+                                                                lh->dec->xb);
+                    break;
+                default:
+                    local_embed_ln_kernel<24><<<eb, 64, 0, st>>>(n, step, h, lh->channels, lh->codes, lh->hin,
+                                                                 lh->wte_slot, lh->emb, lh->tok, w1, b1, lh->x,
+                                                                 lh->dec->xb);
+                    break;
+            }
+        }
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head: ") + cudaGetErrorString(e));
         int rc = mb::dec::run(lh->dec, n, lh->ids, lh->pos + (size_t)step * lh->max_batch, lh->x,
-                              step == 0 ? nullptr : lh->hb, st);
+                              step == 0 ? nullptr : lh->hb, st, /*ln1_ready=*/true);
         if (rc) return rc;
         if (step == 0) {
             local_decide_kernel<<<wblocks, 32 * warps, 0, st>>>(n, h, lh->x, lh->cols, lh->cont);
