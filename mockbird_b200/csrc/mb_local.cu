@@ -102,10 +102,22 @@ __global__ void local_decide_kernel(int n, int h, const float* __restrict__ x, c
 // (row_sel(i) = streams[i] when `streams` is given, else i; rows whose stream is
 // outside [0, n_seen_rows) get token 0 and leave the masks alone -- the ring's
 // own kernel reports such a stream); token -> tokens[i*tok_stride + ch].
-template <int PER>  // ids per lane = codes / 32, a multiple of 4
+// The next step's input, built by the warp that has just chosen the token: row
+// emb[ch][token] to x and the local layer's LN1 of it to xb (the next step of
+// the frame embeds channel ch's token, and local_embed_ln_kernel does the same
+// for the other steps).
+struct EmbedNext {
+    const float* emb;  // [channels - 1][codes][h]
+    const float *ln_w, *ln_b;
+    float* x;
+    __nv_bfloat16* xb;
+    int h;
+};
+
+template <int PER, int HPER>  // ids per lane = codes / 32, a multiple of 4; HPER = h / 32, 0: no EmbedNext
 __global__ void argmax_penalty_kernel(int n, int codes, const float* __restrict__ logits, uint32_t* __restrict__ seen,
                                       const int32_t* __restrict__ streams, int n_seen_rows, int seen_row_words, int ch,
-                                      float penalty, int32_t* __restrict__ tokens, int tok_stride) {
+                                      float penalty, int32_t* __restrict__ tokens, int tok_stride, EmbedNext en) {
     const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (i >= n) return;
     const int row = streams ? streams[i] : i;
@@ -149,17 +161,27 @@ __global__ void argmax_penalty_kernel(int n, int codes, const float* __restrict_
         tokens[(size_t)i * tok_stride + ch] = ok ? idx : 0;
         if (ok) mask[idx >> 5] |= 1u << (idx & 31);
     }
+    if constexpr (HPER > 0) {  // every lane holds the reduced (best, idx)
+        const int tok = ok ? idx : 0;
+        float x[HPER];
+        mb::dec::ln_load<HPER>(en.emb + ((size_t)ch * codes + tok) * en.h, lane, x);
+        mb::dec::ln_store<HPER>(en.x + (size_t)i * en.h, lane, x);
+        mb::dec::ln_apply<__nv_bfloat16, HPER>(x, en.ln_w, en.ln_b, en.xb + (size_t)i * en.h, en.h, lane);
+    }
 }
 
 // Launches the argmax for `codes` in {128, 256, 512, 1024, 2048} (ids per lane a
 // multiple of 4); other sizes are rejected by the callers' checks.
-cudaError_t launch_argmax(int n, int codes, const float* logits, uint32_t* seen, const int32_t* streams,
-                          int n_seen_rows, int seen_row_words, int ch, float penalty, int32_t* tokens, int tok_stride,
-                          cudaStream_t st) {
+// next: when non-null, the same launch also builds the next step's input (EmbedNext).
+template <int HPER>
+cudaError_t launch_argmax_h(int n, int codes, const float* logits, uint32_t* seen, const int32_t* streams,
+                            int n_seen_rows, int seen_row_words, int ch, float penalty, int32_t* tokens,
+                            int tok_stride, const EmbedNext& en, cudaStream_t st) {
     const int warps = 2, blocks = (n + warps - 1) / warps;
-#define MB_ARGMAX(PER)                                                                                          \
-    argmax_penalty_kernel<PER><<<blocks, 32 * warps, 0, st>>>(n, codes, logits, seen, streams, n_seen_rows,    \
-                                                                seen_row_words, ch, penalty, tokens, tok_stride)
+#define MB_ARGMAX(PER)                                                                                              \
+    argmax_penalty_kernel<PER, HPER><<<blocks, 32 * warps, 0, st>>>(n, codes, logits, seen, streams, n_seen_rows, \
+                                                                      seen_row_words, ch, penalty, tokens,          \
+                                                                      tok_stride, en)
     switch (codes) {
         case 128: MB_ARGMAX(4); break;
         case 256: MB_ARGMAX(8); break;
@@ -170,6 +192,26 @@ cudaError_t launch_argmax(int n, int codes, const float* logits, uint32_t* seen,
     }
 #undef MB_ARGMAX
     return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(int n, int codes, const float* logits, uint32_t* seen, const int32_t* streams,
+                          int n_seen_rows, int seen_row_words, int ch, float penalty, int32_t* tokens, int tok_stride,
+                          cudaStream_t st, const EmbedNext* next = nullptr) {
+    if (!next)
+        return launch_argmax_h<0>(n, codes, logits, seen, streams, n_seen_rows, seen_row_words, ch, penalty, tokens,
+                                  tok_stride, EmbedNext{}, st);
+    switch (next->h / 32) {
+        case 2:
+            return launch_argmax_h<2>(n, codes, logits, seen, streams, n_seen_rows, seen_row_words, ch, penalty,
+                                      tokens, tok_stride, *next, st);
+        case 8:
+            return launch_argmax_h<8>(n, codes, logits, seen, streams, n_seen_rows, seen_row_words, ch, penalty,
+                                      tokens, tok_stride, *next, st);
+        case 24:
+            return launch_argmax_h<24>(n, codes, logits, seen, streams, n_seen_rows, seen_row_words, ch, penalty,
+                                       tokens, tok_stride, *next, st);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace
@@ -210,8 +252,9 @@ size_t dec_count(const mb_ctx* c, int ffn) { return mb_decoder_weight_count(c, f
 int enqueue_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
     const int h = lh->h, steps = lh->channels + 1;
     const int warps = 4, wblocks = (n + warps - 1) / warps;
+    bool input_ready = false;  // x and xb already hold this step's input (built by the previous argmax)
     for (int step = 0; step < steps; step++) {
-        {
+        if (!input_ready) {
             const int eb = (n + 1) / 2;  // two warps (items) per block
             const float *w1 = lh->dec->L[0].ln1_w, *b1 = lh->dec->L[0].ln1_b;
             switch (h / 32) {
@@ -244,8 +287,12 @@ int enqueue_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
             rc = mb::dec::gemm(lh->dec, n, lh->codes, h, lh->hb, lh->heads + (size_t)ch * h * lh->codes, nullptr,
                                lh->lg, false, st);
             if (rc) return rc;
+            // steps before the last also embed the chosen tokens for the next step
+            const EmbedNext next{lh->emb, lh->dec->L[0].ln1_w, lh->dec->L[0].ln1_b, lh->x, lh->dec->xb, h};
+            const bool fuse = step < lh->channels;
             e = launch_argmax(n, lh->codes, lh->lg, lh->seen, lh->ids, lh->ctx->cfg.streams, lh->seen_words, ch,
-                              lh->penalty, lh->tok, lh->channels, st);
+                              lh->penalty, lh->tok, lh->channels, st, fuse ? &next : nullptr);
+            input_ready = fuse;
             if (e != cudaSuccess)
                 return lfail(lh, MB_ERR_CUDA, std::string("local head argmax: ") + cudaGetErrorString(e));
             if (want_logits) {
