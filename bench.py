@@ -506,8 +506,18 @@ def run_decoder(args, cfg, rank, world, device):
     return result, ring
 
 
+def use_all_host_threads():
+    """The CPU legs run on every host thread this process may use.  torchrun sets
+    OMP_NUM_THREADS=1 in its workers, and the oracle's OpenMP runtime reads that
+    variable when it is first loaded, so it is set here, before that load."""
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    return cores
+
+
 def run_cpu_decoder(cfg, steps, sample_streams=2, budget_s=None):
     """The reference's decode step (ref-decode.mjs decodeStep restated by the oracle) on the host cores."""
+    use_all_host_threads()
     import oracle
 
     n, L, C, F = sample_streams, cfg["layers"], cfg["capacity"], cfg["ffn"]
@@ -662,6 +672,7 @@ def run_local(args, cfg, rank, world, device):
 
 def run_cpu_local(cfg, frames, sample_streams=2, budget_s=None):
     """The reference's local head (ref-decode.mjs localStep/argmaxPenalty restated by the oracle) on the host."""
+    use_all_host_threads()
     import oracle
 
     n, F, codes, ch = sample_streams, cfg["ffn"], cfg["codes"], cfg["channels"]
@@ -688,6 +699,7 @@ def run_cpu_local(cfg, frames, sample_streams=2, budget_s=None):
 def run_cpu(cfg, steps, warmup, sample_streams, budget_s=None):
     """The reference algorithm (oracle mirror of the WGSL kernels) on the host cores:
     `sample_streams` streams of the workload, all 12 layers per frame."""
+    use_all_host_threads()
     import oracle
 
     n, L, C = sample_streams, cfg["layers"], cfg["capacity"]
@@ -740,6 +752,7 @@ def run_cpu(cfg, steps, warmup, sample_streams, budget_s=None):
 def run_cpu_prefill(cfg, steps, warmup, sample_streams=1, budget_s=None):
     """The reference's prefill (ROPE_SPLIT_CACHE + ATTENTION_SCORES/_SOFTMAX/_APPLY,
     oracle restatement) on the host cores: `sample_streams` streams x 12 layers per step."""
+    use_all_host_threads()
     import oracle
 
     n, L, C, S = sample_streams, cfg["layers"], cfg["capacity"], cfg["rows"]
