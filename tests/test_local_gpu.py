@@ -117,16 +117,21 @@ def test_argmax_penalty_rules_and_random_rows():
 
 # ------------------------------------------------------------------ the whole head
 
-@pytest.mark.parametrize("graph", ["1", "0"])
-def test_local_frame_matches_oracle(graph, monkeypatch):
+@pytest.mark.parametrize("graph,heads,ffn,codes,channels", [
+    ("1", H, 3072, 1024, 16),
+    ("0", H, 3072, 1024, 16),
+    ("1", 4, 512, 256, 4),   # a 256-wide layer: the other LayerNorm width of the fused embedding kernels
+])
+def test_local_frame_matches_oracle(graph, heads, ffn, codes, channels, monkeypatch):
     monkeypatch.setenv("MOCKBIRD_LOCAL_GRAPH", graph)
-    h, ffn, codes, channels, penalty = HID, 3072, 1024, 16, 1.2
+    h, penalty = heads * 64, 1.2
     S = 8
     order = [6, 1, 3, 0, 7]
     w = local_weights(h, ffn, codes, channels, seed=11)
-    ring = _ring(S, channels)
+    ring = KvRing(layers=1, heads=heads, capacity=channels + 1, streams=S, dtype="f32", wrap=False,
+                  max_position=channels + 1)
     head = LocalHead(ring, w, ffn, codes, channels, penalty)
-    orc = oracle.Ring(layers=1, streams=S, heads=H, capacity=channels + 1, dtype="f32", wrap=False,
+    orc = oracle.Ring(layers=1, streams=S, heads=heads, capacity=channels + 1, dtype="f32", wrap=False,
                       max_position=channels + 1)
     seen_o = np.zeros((S, channels, codes // 32), np.uint32)
     seen_k = np.zeros((S, channels, codes // 32), np.uint32)  # follows the kernel's picks
