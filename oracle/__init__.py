@@ -67,6 +67,7 @@ def lib():
         L.orc_prefill.restype = ctypes.c_int
         L.orc_round_to.argtypes = [i32, P, P, ctypes.c_size_t]
         L.orc_xorshift_js.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int64, P]
+        L.orc_xorshift_js_f64.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int64, P]
         _lib = L
     return _lib
 
@@ -197,6 +198,38 @@ def xorshift32_stream(seed: int = 0x2F6E2B1):
     return rnd
 
 
+def xorshift32_stream_f64(seed: int = 0x2F6E2B1):
+    """The same PRNG with its draws in fp64, before any Float32Array store:
+    rnd(count) -> float64 draws.  kernels.test.mjs scales some draws in fp64 before
+    storing them (`rnd() * 0.1`), so `(rnd(n) * 0.1).astype(np.float32)` is what
+    its arrays hold."""
+    state = ctypes.c_uint32(seed & 0xFFFFFFFF)
+
+    def rnd(count: int):
+        out = np.empty(count, np.float64)
+        lib().orc_xorshift_js_f64(ctypes.byref(state), count, _p(out))
+        return out
+
+    return rnd
+
+
+def layer_norm(x: np.ndarray, g: np.ndarray, b: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """LAYERNORM_1 (kernels-decode.ts:168-200) over the last axis: two passes (mean,
+    then the mean of squared deviations), statistics in fp64 rounded to fp32,
+    (x - mean) / sqrt(var + eps) * g + b in fp32."""
+    mean = x.mean(-1, keepdims=True, dtype=np.float64).astype(np.float32)
+    d = x - mean
+    var = (d.astype(np.float64) ** 2).mean(-1, keepdims=True).astype(np.float32)
+    return (d / np.sqrt(var + np.float32(eps)) * g + b).astype(np.float32)
+
+
+def gemm_bf16(x: np.ndarray, W: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """GEMV (kernels-decode.ts:127-142), y = b + x W with W [K, N] row-major, at the
+    rounding points of the CUDA path's bf16 GEMMs: x rounded to bf16, W given
+    already in bf16, products and sums exact (fp64), the result rounded to fp32."""
+    return (round_to("bf16", x).astype(np.float64) @ W.astype(np.float64) + b).astype(np.float32)
+
+
 def decoder_step(ring: "Ring", weights: np.ndarray, ffn: int, streams, positions, hidden: np.ndarray) -> np.ndarray:
     """The global decode step of tools/onnx-probe/ref-decode.mjs:207-235 (decodeStep)
     for several streams, with the rounding points of a bf16 GEMM path: matrices and
@@ -213,14 +246,7 @@ def decoder_step(ring: "Ring", weights: np.ndarray, ffn: int, streams, positions
         a = round_to("bf16", a) if mat else a
         return a.reshape(shape) if shape else a
 
-    def ln(x, g, b):
-        mean = x.mean(-1, keepdims=True, dtype=np.float64).astype(np.float32)
-        d = x - mean
-        var = (d.astype(np.float64) ** 2).mean(-1, keepdims=True).astype(np.float32)
-        return (d / np.sqrt(var + np.float32(1e-5)) * g + b).astype(np.float32)
-
-    def gemm(x, W, b):  # bf16 inputs, fp32 accumulation
-        return (round_to("bf16", x).astype(np.float64) @ W.astype(np.float64) + b).astype(np.float32)
+    ln, gemm = layer_norm, gemm_bf16
 
     x = np.array(hidden, np.float32, copy=True)
     for layer in range(ring.g.layers):

@@ -448,3 +448,18 @@ void orc_xorshift_js(uint32_t* state, int64_t n, float* out) {
     }
     *state = x;
 }
+
+/* The same draws before the Float32Array store: the tests scale some draws in
+ * fp64 first (`rnd() * 0.1`, kernels.test.mjs:98, :176-178), so the stored value
+ * is the fp32 rounding of the scaled double, not a scaled fp32 draw. */
+void orc_xorshift_js_f64(uint32_t* state, int64_t n, double* out) {
+    uint32_t x = *state;
+    for (int64_t i = 0; i < n; i++) {
+        x ^= x << 13;
+        uint32_t t = (x >> 17) | ((x & 0x80000000u) ? 0xFFFF8000u : 0u);
+        x ^= t;
+        x ^= x << 5;
+        out[i] = ((double)x / 4294967295.0) * 2.0 - 1.0;
+    }
+    *state = x;
+}

@@ -38,6 +38,21 @@ kat_argmax_c1024.npz
       best     int         expected id
       skip     int         draws consumed before test 5
       logits_sum           float64 sum of the logits (regeneration check)
+
+kat_layernorm_d768.npz
+    The known answer of kernels.test.mjs test 1 ("layernorm d=768 eps=1e-5",
+    :90-163), the first draws of the stream; the expected row is the test's
+    float64 loop restated below in plain Python.
+      out      [768] f32   expected row
+      x_sum, b_sum         float64 sums of the inputs (regeneration check)
+
+kat_gemv_k768_n2304.npz
+    The known answer of kernels.test.mjs test 2 ("gemv [K=768, N=2304] c_attn",
+    :165-223), drawn right after test 1's inputs; the expected vector is the
+    test's float64 loop, summed in its order.
+      out      [2304] f32  expected y = bias + x W
+      skip     int         draws consumed before test 2
+      x_sum, w_sum, bias_sum  float64 sums of the inputs (regeneration check)
 """
 from __future__ import annotations
 
@@ -100,6 +115,44 @@ def kat_argmax():
     return logits, best, skip
 
 
+def kat_layernorm():
+    """kernels.test.mjs:90-109 (test 1, "layernorm d=768 eps=1e-5"): per i, x[i] =
+    rnd()*4 then b[i] = rnd()*0.1 (scaled in fp64, stored fp32), g = 1; the
+    expected row is the test's fp64 loop restated (sequential sums)."""
+    rnd = oracle.xorshift32_stream_f64(0x2F6E2B1)
+    d = rnd(2 * D)
+    x = (d[0::2] * 4).astype(np.float32)
+    b = (d[1::2] * 0.1).astype(np.float32)
+    mean = 0.0
+    for v in x:
+        mean += float(v)
+    mean /= D
+    var = 0.0
+    for v in x:
+        var += (float(v) - mean) ** 2
+    var /= D
+    inv = 1.0 / np.sqrt(var + 1e-5)
+    out = np.array([(float(x[i]) - mean) * inv * 1.0 + float(b[i]) for i in range(D)]).astype(np.float32)
+    return x, b, out
+
+
+def kat_gemv():
+    """kernels.test.mjs:165-223 (test 2, "gemv [K=768, N=2304] c_attn"), drawn after
+    test 1's 2*768 values: x[k] = rnd(), W[k*N+n] = rnd()*0.05, bias[n] = rnd()*0.02;
+    the expected y[n] = bias[n] + sum_k x[k] W[k, n] is the test's fp64 loop, summed
+    in its order (k ascending from the bias)."""
+    K, N = D, 3 * D
+    rnd = oracle.xorshift32_stream_f64(0x2F6E2B1)
+    rnd(2 * D)
+    x = rnd(K).astype(np.float32)
+    W = (rnd(K * N) * 0.05).astype(np.float32).reshape(K, N)
+    bias = (rnd(N) * 0.02).astype(np.float32)
+    acc = bias.astype(np.float64)
+    for k in range(K):
+        acc = acc + float(x[k]) * W[k].astype(np.float64)
+    return x, W, bias, acc.astype(np.float32)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference tree")
@@ -125,6 +178,14 @@ def main():
     logits, best, skip = kat_argmax()
     np.savez_compressed(os.path.join(HERE, "kat_argmax_c1024.npz"), best=np.array(best), skip=np.array(skip),
                         logits_sum=np.array(logits.astype(np.float64).sum()))
+    x, b, out = kat_layernorm()
+    np.savez_compressed(os.path.join(HERE, "kat_layernorm_d768.npz"), out=out,
+                        x_sum=np.array(x.astype(np.float64).sum()), b_sum=np.array(b.astype(np.float64).sum()))
+    x, W, bias, y = kat_gemv()
+    np.savez_compressed(os.path.join(HERE, "kat_gemv_k768_n2304.npz"), out=y, skip=np.array(2 * D),
+                        x_sum=np.array(x.astype(np.float64).sum()), w_sum=np.array(W.astype(np.float64).sum()),
+                        bias_sum=np.array(bias.astype(np.float64).sum()))
+    print("wrote kat_layernorm_d768.npz and kat_gemv_k768_n2304.npz")
     print("wrote layer0_kv.npz (rows %d, k8_equal=%s), kat_attention_n512.npz and kat_argmax_c1024.npz (best %d)"
           % (len(rows), k8_equal, best))
 

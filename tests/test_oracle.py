@@ -114,6 +114,52 @@ def test_kat_attention_n512_oracle():
         assert err < 1e-5, (mode, err)
 
 
+# ---------------------------------------------------------------- pins of the decoder step's LayerNorm and GEMV
+
+def test_kat_layernorm_d768_oracle():
+    """kernels.test.mjs test 1: LayerNorm of one 768-row (x = 4 rnd(), g = 1,
+    b = 0.1 rnd(), eps 1e-5), the test's own tolerance 2e-5.  This is the
+    LayerNorm that `oracle.decoder_step` and `oracle.local_frame` apply, against
+    which the CUDA decoder and local head are checked."""
+    kat = np.load(os.path.join(os.path.dirname(__file__), "golden", "kat_layernorm_d768.npz"))
+    d = oracle.xorshift32_stream_f64(0x2F6E2B1)(2 * H * HD)
+    x = (d[0::2] * 4).astype(np.float32)
+    b = (d[1::2] * 0.1).astype(np.float32)
+    assert abs(x.astype(np.float64).sum() - float(kat["x_sum"])) < 1e-9
+    assert abs(b.astype(np.float64).sum() - float(kat["b_sum"])) < 1e-12
+    out = oracle.layer_norm(x[None, :], np.ones(H * HD, np.float32), b[None, :])[0]
+    assert float(np.abs(out - kat["out"]).max()) < 2e-5
+
+
+def test_kat_gemv_c_attn_oracle():
+    """kernels.test.mjs test 2: y = bias + x W for the c_attn shape (K 768, N 2304),
+    W = 0.05 rnd(), bias = 0.02 rnd(), the test's own tolerance 5e-3.  Checked at
+    the CUDA path's rounding points (x and W rounded to bf16, exact products and
+    sums), which is how `oracle.decoder_step` computes every GEMM of the layer,
+    and in fp32 (no rounding of x or W), which must agree far closer."""
+    kat = np.load(os.path.join(os.path.dirname(__file__), "golden", "kat_gemv_k768_n2304.npz"))
+    K, N = H * HD, 3 * H * HD
+    rnd = oracle.xorshift32_stream_f64(0x2F6E2B1)
+    rnd(int(kat["skip"]))
+    x = rnd(K).astype(np.float32)
+    W = (rnd(K * N) * 0.05).astype(np.float32).reshape(K, N)
+    bias = (rnd(N) * 0.02).astype(np.float32)
+    assert abs(x.astype(np.float64).sum() - float(kat["x_sum"])) < 1e-9
+    assert abs(W.astype(np.float64).sum() - float(kat["w_sum"])) < 1e-6
+    assert abs(bias.astype(np.float64).sum() - float(kat["bias_sum"])) < 1e-12
+    y = oracle.gemm_bf16(x[None, :], oracle.round_to("bf16", W), bias)[0]
+    assert float(np.abs(y - kat["out"]).max()) < 5e-3
+    y32 = (x.astype(np.float64) @ W.astype(np.float64) + bias).astype(np.float32)
+    assert float(np.abs(y32 - kat["out"]).max()) < 1e-5
+
+
+def test_fp64_draws_round_to_the_fp32_stream():
+    """The fp64 draws, stored to fp32, are the fp32 stream's draws."""
+    a = oracle.xorshift32_stream_f64(0x2F6E2B1)(4096)
+    b = oracle.xorshift32_stream(0x2F6E2B1)(4096)
+    assert np.array_equal(a.astype(np.float32), b)
+
+
 # ---------------------------------------------------------------- ring semantics
 
 def _np_attend(q, ks, vs):
