@@ -367,6 +367,44 @@ MB_API int mb_append_attend_host(mb_ctx* c, int32_t layer, int32_t n, const int3
     return finish_host_call(c, st, st);
 }
 
+// Copy groups of mb_decode_step_host.  A wait for a layer's inputs, and an event
+// that lets a layer's outputs leave, each end the programmatic overlap of two
+// consecutive decode launches (a few microseconds each).  When a layer's decode
+// takes several times as long as its copies, consecutive layers share one copy:
+// input groups grow from the front by the ratio, so each group lands while the
+// group before it decodes; output groups grow from the back by theirs, so each
+// group's copy ends while the group after it decodes and only the last layer's
+// rows are copied after the final launch.  Otherwise every layer is its own group.
+// The estimates: the decode streams its live windows at ~5 TB/s, a page-locked
+// copy moves ~50 GB/s each way; each ratio is divided by a margin of 1.5 and
+// rounded down, so copies up to 1.5 times slower than estimated still land in time.
+// in_start[l]: layer l begins an input group; out_end[l]: layer l ends an output group.
+static void host_step_groups(const mb_ctx* c, int n, const int32_t* positions, std::vector<char>& in_start,
+                             std::vector<char>& out_end) {
+    const int L = c->cfg.layers;
+    double window_bytes = 0;  // K and V windows one layer's decode reads
+    for (int i = 0; i < n; i++) {
+        const int w = positions[i] + 1 < c->cfg.capacity ? positions[i] + 1 : c->cfg.capacity;
+        window_bytes += 2.0 * w * c->cfg.heads * HD * (double)c->esize;
+    }
+    const double hid = (double)c->cfg.heads * HD;
+    const double t_decode = window_bytes / 5.0e12, margin = 1.5;
+    const double rho_in = t_decode / (n * 3 * hid * 4 / 50.0e9) / margin;
+    const double rho_out = t_decode / (n * hid * 4 / 50.0e9) / margin;
+    in_start.assign(L, 0);
+    out_end.assign(L, 0);
+    double len = 1;
+    for (int l = 0; l < L; len = len * rho_in < 1 ? 1 : floor(len * rho_in)) {
+        in_start[l] = 1;
+        l += (int)(len < L ? len : L);
+    }
+    len = 1;
+    for (int l = L - 1; l >= 0; len = len * rho_out < 1 ? 1 : floor(len * rho_out)) {
+        out_end[l] = 1;
+        l -= (int)(len < L ? len : L);
+    }
+}
+
 MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, const int32_t* positions,
                                const float* qkv, float* out, void* cuda_stream) {
     if (!c) return MB_ERR_ARG;
@@ -379,32 +417,40 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     const size_t hid = (size_t)c->cfg.heads * HD, L = c->cfg.layers;
     const size_t in_l = (size_t)n * 3 * hid, out_l = (size_t)n * hid;  // floats per layer
-    // Per layer: its qkv rows copied in on cp_in, its decode on `st` once they
-    // have landed, its context rows copied out on cp_out once it is done; the
-    // copies of one layer overlap the decode of the others.  Both copy streams
-    // start behind the work already queued on `st`, and `st` ends behind them.
+    std::vector<char> in_start, out_end;
+    host_step_groups(c, n, positions, in_start, out_end);
+    // Per input group: its qkv rows copied in on cp_in, and the decode of its
+    // first layer on `st` waits for them.  Per output group: its context rows
+    // copied out on cp_out once its last layer is done.  The copies of one group
+    // overlap the decode of the others.  Both copy streams start behind the work
+    // already queued on `st`, and `st` ends behind them.
     CK(cudaEventRecord(c->ev_start, st), "order copies");
     CK(cudaStreamWaitEvent(c->cp_in, c->ev_start, 0), "order copies");
     CK(cudaStreamWaitEvent(c->cp_out, c->ev_start, 0), "order copies");
     CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->cp_in), "copy streams");
     CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->cp_in),
        "copy positions");
-    for (size_t l = 0; l < L; l++) {
-        CK(cudaMemcpyAsync(c->d_qkv + l * in_l, qkv + l * in_l, in_l * sizeof(float), cudaMemcpyHostToDevice,
-                           c->cp_in),
+    for (size_t l = 0, gi = 0; l < L; gi++) {
+        size_t end = l + 1;
+        while (end < L && !in_start[end]) end++;
+        CK(cudaMemcpyAsync(c->d_qkv + l * in_l, qkv + l * in_l, (end - l) * in_l * sizeof(float),
+                           cudaMemcpyHostToDevice, c->cp_in),
            "copy qkv");
-        CK(cudaEventRecord(c->ev_in[l], c->cp_in), "copy qkv");
+        CK(cudaEventRecord(c->ev_in[gi], c->cp_in), "copy qkv");
+        l = end;
     }
-    for (size_t l = 0; l < L; l++) {
-        CK(cudaStreamWaitEvent(st, c->ev_in[l], 0), "wait qkv");
+    for (size_t l = 0, gi = 0, go = 0, first_out = 0; l < L; l++) {
+        if (in_start[l]) CK(cudaStreamWaitEvent(st, c->ev_in[gi++], 0), "wait qkv");
         CK(run_decode(c, true, (int)l, n, c->d_streams, c->d_positions, c->d_qkv + l * in_l, 3 * (int)hid,
                       c->d_out + l * out_l, st, l > 0),
            "append_attend launch");
-        CK(cudaEventRecord(c->ev_done[l], st), "layer done");
-        CK(cudaStreamWaitEvent(c->cp_out, c->ev_done[l], 0), "wait layer");
-        CK(cudaMemcpyAsync(out + l * out_l, c->d_out + l * out_l, out_l * sizeof(float), cudaMemcpyDeviceToHost,
-                           c->cp_out),
+        if (!out_end[l]) continue;
+        CK(cudaEventRecord(c->ev_done[go++], st), "layer done");
+        CK(cudaStreamWaitEvent(c->cp_out, c->ev_done[go - 1], 0), "wait layer");
+        CK(cudaMemcpyAsync(out + first_out * out_l, c->d_out + first_out * out_l,
+                           (l + 1 - first_out) * out_l * sizeof(float), cudaMemcpyDeviceToHost, c->cp_out),
            "copy out");
+        first_out = l + 1;
     }
     return finish_host_call(c, st, c->cp_out);
 }

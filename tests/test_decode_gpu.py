@@ -220,6 +220,23 @@ def test_host_entry_points_match_device_path():
             assert np.array_equal(one, host[layer])
 
 
+def test_host_step_with_shared_copy_groups_matches_device_path():
+    """Windows long enough (64 streams x 512 fp32 slots) that the host step copies
+    several layers' rows in and out as one group; results equal the device path
+    bit for bit, layer by layer."""
+    S, C, L = 64, 512, 12
+    a = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
+    b = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
+    order = list(np.random.default_rng(3).permutation(S))
+    for step in range(4):
+        qkv = randn((L, S, QKV), seed=500 + step)
+        pos = [700 + step + (s % 5) for s in order]
+        host = a.decode_step_host(order, pos, qkv)
+        for layer in range(L):
+            dev = b.append_attend(layer, order, pos, torch.from_numpy(qkv[layer]).to(DEV))
+            assert np.array_equal(host[layer], dev.cpu().numpy()), (step, layer)
+
+
 def test_errors_are_reported_and_the_context_survives():
     ring = KvRing(layers=2, streams=4, capacity=8, dtype="f32", wrap=False, max_batch=4)
     qkv = randn((1, QKV), seed=0)
