@@ -44,7 +44,7 @@ CONFIGS = {
             streams=64, layers=12, capacity=512, dtype="f32", job_steps=1500, steps=3000, warmup=30),
     3: dict(workload="config3: causal prefill, 32 streams x (188 prompt + 256 text = 444 positions) x 12 layers "
                      "x 12 heads x 64, fp16 ring storage (capacity 2048), fp32 accumulation, q/k/v ~ N(0, 0.5)",
-            streams=32, layers=12, capacity=2048, dtype="f16", job_steps=None, steps=20, warmup=3, rows=444),
+            streams=32, layers=12, capacity=2048, dtype="f16", job_steps=None, steps=600, warmup=3, rows=444),
     4: dict(workload="config4: full 0.1B-class decoder decode step, 256 streams/GPU x 12 layers (hidden 768, 12 "
                      "heads x 64, FFN 3072), bf16 weights ~N(0,0.02) and bf16 ring capacity 2048, positions U[444,2048) "
                      "from seed 0; LN1 -> QKV GEMM -> append+RoPE+attention -> proj GEMM -> LN2 -> FFN per layer",
@@ -55,7 +55,7 @@ CONFIGS = {
     6: dict(workload="local head: 256 streams/GPU, one frame = 17 sequential steps (one 768-wide layer, FFN 3072, "
                      "over a 17-slot ring; ln_f; 16 audio heads 768x1024 with greedy argmax and repetition penalty "
                      "1.2), bf16 weights ~N(0,0.02), tokens kept on the device",
-            streams=256, layers=1, capacity=17, dtype="bf16", job_steps=None, steps=100, warmup=5, ffn=3072,
+            streams=256, layers=1, capacity=17, dtype="bf16", job_steps=None, steps=400, warmup=5, ffn=3072,
             codes=1024, channels=16),
 }
 LOCAL_METRIC = "local-head frames/sec/GPU (17 steps: layer + ln_f + audio head + penalised argmax)"

@@ -237,6 +237,29 @@ def test_host_step_with_shared_copy_groups_matches_device_path():
             assert np.array_equal(host[layer], dev.cpu().numpy()), (step, layer)
 
 
+def test_empty_batches_are_no_ops():
+    """A call with no items succeeds on every decode and prefill entry point and
+    leaves the ring as it was (bytes and slot positions)."""
+    ring = KvRing(layers=2, streams=3, capacity=64, dtype="f32", wrap=True)
+    orc = oracle.Ring(layers=2, streams=3, heads=H, capacity=64, dtype="f32", wrap=True)
+    for p in range(5):
+        qkv = randn((3, QKV), seed=40 + p)
+        ring.append_attend(1, [0, 1, 2], [p] * 3, torch.from_numpy(qkv).to(DEV))
+        orc.append_attend(1, [0, 1, 2], [p] * 3, qkv)
+    none = torch.empty(0, dtype=torch.int32, device=DEV)
+    q0 = torch.empty(0, QKV, device=DEV)
+    assert ring.append_attend(1, none, none, q0).shape == (0, HID)
+    assert ring.rope_split_ring(1, none, none, q0).shape == (0, QKV)
+    assert ring.attend_ring(1, none, none, q0).shape == (0, HID)
+    assert ring.decode_step(none, none, torch.empty(2, 0, QKV, device=DEV)).shape == (2, 0, HID)
+    assert ring.append_attend_host(1, [], [], np.empty((0, QKV), np.float32)).shape == (0, HID)
+    assert ring.decode_step_host([], [], np.empty((2, 0, QKV), np.float32)).shape == (2, 0, HID)
+    assert ring.prefill(0, none, torch.empty(0, 8, QKV, device=DEV)).shape == (0, 8, HID)
+    ring.sync()
+    for s in range(3):
+        assert_window_equal(ring, orc, 1, s, 1, s, 4)
+
+
 def test_errors_are_reported_and_the_context_survives():
     ring = KvRing(layers=2, streams=4, capacity=8, dtype="f32", wrap=False, max_batch=4)
     qkv = randn((1, QKV), seed=0)
