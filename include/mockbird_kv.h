@@ -142,9 +142,11 @@ MB_API int mb_append_attend_host(mb_ctx* ctx, int32_t layer, int32_t n, const in
                                  void* cuda_stream);
 
 /* One global decode step for n streams through ALL layers, HOST arrays:
- * qkv [layers][n][3*heads*64], out [layers][n][heads*64]; one copy in, one
- * launch per layer, one copy out, blocking -- the granularity of
- * DecodeRunner.globalStep (decode.ts:712-775: one submit, one readback). */
+ * qkv [layers][n][3*heads*64], out [layers][n][heads*64]; one launch per
+ * layer; the rows are copied in and out in groups of consecutive layers on the
+ * context's own copy streams, overlapping the other layers' decode; returns
+ * once `out` is complete -- the granularity of DecodeRunner.globalStep
+ * (decode.ts:712-775: one submit, one readback). */
 MB_API int mb_decode_step_host(mb_ctx* ctx, int32_t n, const int32_t* streams, const int32_t* positions,
                                const float* qkv, float* out, void* cuda_stream);
 
