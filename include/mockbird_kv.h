@@ -265,6 +265,15 @@ MB_API int mb_local_head_clear(mb_local_head* head, int32_t stream, void* cuda_s
 MB_API int mb_local_head_frame(mb_local_head* head, int32_t n, const int32_t* streams, const float* hidden,
                                int32_t* tokens, int32_t* cont, float* logits, void* cuda_stream);
 
+/* mb_local_head_frame with HOST arrays, as DecodeRunner.nextFrame takes the
+ * hidden row from the host and reads the stop flag and the tokens back
+ * (decode.ts:788, 933-935): streams [n] are checked on the host (range,
+ * duplicates), hidden [n][H*64] is copied in, the frame runs, tokens
+ * [n][channels] and cont [n] are copied out with the ring's device status word,
+ * and the call returns once they are in place (one synchronisation). */
+MB_API int mb_local_head_frame_host(mb_local_head* head, int32_t n, const int32_t* streams, const float* hidden,
+                                    int32_t* tokens, int32_t* cont, void* cuda_stream);
+
 /* ARGMAX_PENALTY alone (kernels-decode.ts:428-485), on the current device: for
  * each of n rows, token = the penalised argmax of logits [n][codes] under the
  * row's seen mask seen [n][codes/32] (bit j of word j/32), whose bit is then

@@ -110,6 +110,7 @@ SIGNATURES = {
     "mb_local_head_destroy": (ctypes.c_int, [_P]),
     "mb_local_head_clear": (ctypes.c_int, [_P, _I, _P]),
     "mb_local_head_frame": (ctypes.c_int, [_P, _I, _P, _P, _P, _P, _P, _P]),
+    "mb_local_head_frame_host": (ctypes.c_int, [_P, _I, _P, _P, _P, _P, _P]),
     "mb_argmax_penalty": (ctypes.c_int, [_I, _I, _P, _P, ctypes.c_float, _P, _P]),
     "mb_append_attend_noalloc": (ctypes.c_int, [ctypes.POINTER(MbRingRef), _I, _I, _P, _P, _P, _P, _P]),
     "mb_ring_info_get": (ctypes.c_int, [_P, ctypes.POINTER(MbRingInfo)]),

@@ -57,10 +57,10 @@ struct mb_ctx {
     int32_t* d_positions = nullptr;
     float* d_qkv = nullptr;   // [layers][max_batch][3*H*64]
     float* d_out = nullptr;   // [layers][max_batch][H*64]
-    // mb_decode_step_host's copy pipeline: inputs in and outputs out per layer on
-    // their own streams, so that the copies overlap the decode of other layers
+    // mb_decode_step_host's copy pipeline: inputs in and outputs out in groups of
+    // layers on their own streams, so that the copies overlap the decode of others
     cudaStream_t cp_in = nullptr, cp_out = nullptr;
-    std::vector<cudaEvent_t> ev_in, ev_done;  // per layer: inputs landed / layer decoded
+    std::vector<cudaEvent_t> ev_in, ev_done;  // per copy group: inputs landed / last layer decoded
     cudaEvent_t ev_start = nullptr, ev_end = nullptr;
     int32_t* h_err = nullptr;  // pinned copy of d_err, read by the host-array entry points
     bool persistent = false;  // decode with the persistent stream-K kernel (when it applies) instead

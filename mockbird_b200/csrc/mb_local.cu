@@ -29,6 +29,7 @@
 #include <string.h>
 
 #include <map>
+#include <vector>
 #include <utility>
 
 #include "mb_decoder.cuh"
@@ -496,6 +497,43 @@ MB_API int mb_local_head_frame(mb_local_head* lh, int32_t n, const int32_t* stre
         e = cudaMemcpyAsync(logits, lh->lg_all, (size_t)n * ch * codes * 4, cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head outputs: ") + cudaGetErrorString(e));
     return MB_OK;
+}
+
+MB_API int mb_local_head_frame_host(mb_local_head* lh, int32_t n, const int32_t* streams, const float* hidden,
+                                    int32_t* tokens, int32_t* cont, void* cuda_stream) {
+    if (!lh) return MB_ERR_ARG;
+    if (n < 0 || n > lh->max_batch) return lfail(lh, MB_ERR_ARG, "local head: item count out of range");
+    if (n == 0) return MB_OK;
+    if (!streams || !hidden || !tokens || !cont) return lfail(lh, MB_ERR_ARG, "local head: null host pointer");
+    mb_ctx* c = lh->ctx;
+    std::vector<char> seen(c->cfg.streams, 0);
+    for (int i = 0; i < n; i++) {
+        const int s = streams[i];
+        if (s < 0 || s >= c->cfg.streams) return lfail(lh, MB_ERR_STREAM, "local head: stream id out of range");
+        if (seen[s]) return lfail(lh, MB_ERR_STREAM, "local head: a stream appears twice in one call");
+        seen[s] = 1;
+    }
+    DeviceGuard g(c->cfg.device);
+    if (!g.ok) return MB_ERR_CUDA;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const size_t h = lh->h, ch = lh->channels;
+    cudaError_t e = cudaMemcpyAsync(lh->ids, streams, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(lh->hin, hidden, (size_t)n * h * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head inputs: ") + cudaGetErrorString(e));
+    const int rc = lh->use_graph ? launch_frame(lh, n, false, st) : enqueue_frame(lh, n, false, st);
+    if (rc) return rc;
+    // the frame's tokens, the stop flags and the ring's device status word, then one wait
+    e = cudaMemcpyAsync(tokens, lh->tok, (size_t)n * ch * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(cont, lh->cont, (size_t)n * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head outputs: ") + cudaGetErrorString(e));
+    const int32_t bits = *c->h_err;
+    if (!bits) return MB_OK;
+    if (cudaMemset(c->d_err, 0, sizeof(int32_t)) != cudaSuccess)
+        return lfail(lh, MB_ERR_CUDA, "local head: clearing the device status failed");
+    if (bits & mb::DERR_TIMEOUT) return lfail(lh, MB_ERR_TIMEOUT, "local head: a bounded device-side wait gave up");
+    return lfail(lh, MB_ERR_DEVICE, "local head: a kernel rejected an item");
 }
 
 MB_API int mb_argmax_penalty(int32_t n, int32_t codes, const float* logits, uint32_t* seen, float penalty,

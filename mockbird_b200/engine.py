@@ -348,6 +348,24 @@ class LocalHead:
         self.ring._check(rc)
         return tok, cont, lg
 
+    def frame_host(self, streams, hidden, tokens=None, cont=None, stream=None):
+        """One frame on host arrays, as nextFrame (decode.ts:788-939) takes the
+        hidden row from the host and reads its tokens back: hidden [n][H*64] fp32
+        (numpy or a CPU tensor, ideally pinned).  Blocks until the outputs are in
+        place.  Returns (tokens [n][channels] int32, cont [n] int32)."""
+        s = np.ascontiguousarray(streams, np.int32)
+        if isinstance(hidden, np.ndarray):
+            hidden = np.ascontiguousarray(hidden, np.float32)
+        n = len(s)
+        if tokens is None:
+            tokens = np.empty((n, self.channels), np.int32)
+        if cont is None:
+            cont = np.empty(n, np.int32)
+        rc = self.lib.mb_local_head_frame_host(self.handle, n, _ptr(s), _ptr(hidden), _ptr(tokens), _ptr(cont),
+                                               self.ring._stream(stream))
+        self.ring._check(rc)
+        return tokens, cont
+
     def dispose(self) -> None:
         if getattr(self, "handle", None):
             self.lib.mb_local_head_destroy(self.handle)

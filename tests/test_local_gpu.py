@@ -241,3 +241,34 @@ def test_local_head_rejects_bad_arguments():
     with pytest.raises(MockbirdError):
         head.clear(2)
     head.dispose()
+
+
+@pytest.mark.parametrize("graph", ["1", "0"])
+def test_local_frame_host_arrays_match_device_arrays(graph, monkeypatch):
+    """mb_local_head_frame_host (hidden rows from the host, tokens and stop flags
+    back to the host, as nextFrame does) gives the device entry point's tokens and
+    flags exactly, frame after frame (the seen masks carry over); bad stream ids
+    are rejected on the host and the head stays usable."""
+    monkeypatch.setenv("MOCKBIRD_LOCAL_GRAPH", graph)
+    h, ffn, codes, channels, S = HID, 3072, 1024, 16, 6
+    w = local_weights(h, ffn, codes, channels, seed=21)
+    a = LocalHead(_ring(S, channels, dtype="bf16"), w, ffn, codes, channels, 1.2)
+    b = LocalHead(_ring(S, channels, dtype="bf16"), w, ffn, codes, channels, 1.2)
+    order = [4, 0, 5, 2]
+    rng = np.random.default_rng(5)
+    for frame in range(3):
+        hidden = rng.standard_normal((len(order), h)).astype(np.float32)
+        tok_a, cont_a, _ = a.frame(order, torch.from_numpy(hidden).to(DEV))
+        tok_b, cont_b = b.frame_host(order, hidden)
+        assert np.array_equal(tok_a.cpu().numpy(), tok_b), frame
+        assert np.array_equal(cont_a.cpu().numpy(), cont_b), frame
+    for bad in ([0, 0], [S], [-1]):
+        with pytest.raises(MockbirdError) as e:
+            b.frame_host(bad, np.zeros((len(bad), h), np.float32))
+        assert e.value.status == "MB_ERR_STREAM"
+    hidden = rng.standard_normal((2, h)).astype(np.float32)
+    tok_a, cont_a, _ = a.frame([1, 3], torch.from_numpy(hidden).to(DEV))
+    tok_b, cont_b = b.frame_host([1, 3], hidden)
+    assert np.array_equal(tok_a.cpu().numpy(), tok_b) and np.array_equal(cont_a.cpu().numpy(), cont_b)
+    a.dispose()
+    b.dispose()
