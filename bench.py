@@ -181,17 +181,25 @@ def setup_ours(cfg, rank, world, device):
         all_len = config5_lengths(max(total, 4096), cfg["capacity"])[:total]
         shard_ids = partition_streams(total, world, all_len)[rank].streams
         lengths0 = all_len[shard_ids].astype(np.int64)
-        # fill positions 0..L-2 of every stream with N(0,1) K/V (the same rows for all layers)
-        for i, L in enumerate(lengths0):
-            if L <= 1:
-                continue
-            kv = torch.randn(2, H, int(L) - 1, HD, generator=g, device=device).to(ring.torch_dtype)
-            for layer in range(cfg["layers"]):
-                ring.ring_write(layer, i, 0, kv[0], kv[1])
-        torch.cuda.synchronize(device)
+        fill_lengths(ring, lengths0, cfg["layers"], g, device)
     info["global_streams"] = n * world
     info["shard"] = [int(shard_ids.min()), int(shard_ids.max())] if len(shard_ids) else []
     return ring, qkv_pool, out, streams, lengths0, info
+
+
+def fill_lengths(ring, lengths0, layers, gen, device):
+    """Config 5's starting rings: positions 0..L-2 of every stream filled with
+    N(0,1) K/V (the same rows for all layers), every other slot empty."""
+    import torch
+
+    ring.reset()
+    for i, L in enumerate(lengths0):
+        if L <= 1:
+            continue
+        kv = torch.randn(2, H, int(L) - 1, HD, generator=gen, device=device).to(ring.torch_dtype)
+        for layer in range(layers):
+            ring.ring_write(layer, i, 0, kv[0], kv[1])
+    torch.cuda.synchronize(device)
 
 
 def positions_for(cfg, step, n, lengths0):
@@ -269,8 +277,14 @@ def run_ours(args, cfg, rank, world, device):
         ids = np.arange(n, dtype=np.int32)
         if lengths0 is None:
             ring.reset()
-        e2e_steps = K if lengths0 is None else min(K, 50)
-        base = W + K
+        else:  # config 5: the starting rings again and the warm-up replayed, so the
+            # e2e steps run the timed region's positions over the same windows
+            gen = torch.Generator(device=device)
+            gen.manual_seed(5678 + rank)
+            fill_lengths(ring, lengths0, L, gen, device)
+            for t in range(W):
+                step(t)
+        e2e_steps = K
         if dist:
             dist.barrier()
         torch.cuda.synchronize(device)
@@ -278,7 +292,7 @@ def run_ours(args, cfg, rank, world, device):
         for t in range(e2e_steps):
             if lengths0 is None and t > 0 and t % cfg["job_steps"] == 0:
                 ring.reset()
-            pos = positions_for(cfg, t if lengths0 is None else base + t, n, lengths0)
+            pos = positions_for(cfg, t, n, None) if lengths0 is None else pos_host[W + t]
             ring.decode_step_host(ids, pos, host_qkv[t % sets], host_out)
         torch.cuda.synchronize(device)
         e2e_s = max_over_ranks(time.perf_counter() - t0, device if dist else None)
