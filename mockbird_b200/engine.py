@@ -58,6 +58,19 @@ def _ptr(t) -> ctypes.c_void_p:
 _TORCH_DTYPE = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
 
 
+def _host_array(name: str, a, shape: tuple, dtype: str):
+    """Check a host buffer that the C ABI reads or writes in place through its
+    address: a C-contiguous numpy array or CPU torch tensor of `dtype` and
+    `shape` (anything else would be read or written at the wrong places)."""
+    if isinstance(a, torch.Tensor):
+        ok = not a.is_cuda and a.is_contiguous() and a.dtype == getattr(torch, dtype) and tuple(a.shape) == shape
+    else:
+        ok = isinstance(a, np.ndarray) and a.flags["C_CONTIGUOUS"] and a.dtype == np.dtype(dtype) and a.shape == shape
+    if not ok:
+        raise TypeError(f"{name} must be a contiguous host {dtype} array of shape {shape}")
+    return a
+
+
 class KvRing:
     """The rings of `streams` independent synthesis streams on one GPU.
 
@@ -169,6 +182,8 @@ class KvRing:
         q = np.ascontiguousarray(qkv, np.float32)
         if out is None:
             out = np.empty((len(s), self.hidden), np.float32)
+        _host_array("qkv", q, (len(s), 3 * self.hidden), "float32")
+        _host_array("out", out, (len(s), self.hidden), "float32")
         self._check(self.lib.mb_append_attend_host(self.ctx, layer, len(s), _ptr(s), _ptr(p), _ptr(q), _ptr(out),
                                                    self._stream(stream)))
         return out
@@ -183,6 +198,8 @@ class KvRing:
             qkv = np.ascontiguousarray(qkv, np.float32)
         if out is None:
             out = np.empty((self.layers, len(s), self.hidden), np.float32)
+        _host_array("qkv", qkv, (self.layers, len(s), 3 * self.hidden), "float32")
+        _host_array("out", out, (self.layers, len(s), self.hidden), "float32")
         self._check(self.lib.mb_decode_step_host(self.ctx, len(s), _ptr(s), _ptr(p), _ptr(qkv), _ptr(out),
                                                  self._stream(stream)))
         return out
@@ -361,6 +378,9 @@ class LocalHead:
             tokens = np.empty((n, self.channels), np.int32)
         if cont is None:
             cont = np.empty(n, np.int32)
+        _host_array("hidden", hidden, (n, self.ring.hidden), "float32")
+        _host_array("tokens", tokens, (n, self.channels), "int32")
+        _host_array("cont", cont, (n,), "int32")
         rc = self.lib.mb_local_head_frame_host(self.handle, n, _ptr(s), _ptr(hidden), _ptr(tokens), _ptr(cont),
                                                self.ring._stream(stream))
         self.ring._check(rc)

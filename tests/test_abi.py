@@ -78,3 +78,21 @@ def test_missing_library_fails_loudly(tmp_path):
             _lib.load(str(tmp_path / "libmockbird_kv.so"))
         finally:
             _lib._lib = None
+
+
+def test_host_buffers_are_checked_before_the_call():
+    """The host-array entry points read and write caller buffers through their
+    addresses, so the Python mirror rejects a buffer of the wrong dtype, shape or
+    layout (or one on the GPU) before the call."""
+    import numpy as np
+    import torch
+
+    from mockbird_b200.engine import _host_array
+
+    ok = np.zeros((2, 3), np.float32)
+    assert _host_array("x", ok, (2, 3), "float32") is ok
+    assert _host_array("x", torch.zeros(2, 3), (2, 3), "float32") is not None
+    for bad in (np.zeros((2, 3), np.float64), np.zeros((3, 2), np.float32).T, np.zeros((2, 4), np.float32),
+                torch.zeros(3, 2).t(), torch.zeros(2, 3, dtype=torch.int32), [[0.0] * 3] * 2):
+        with pytest.raises(TypeError):
+            _host_array("x", bad, (2, 3), "float32")
