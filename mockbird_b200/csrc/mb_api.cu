@@ -193,8 +193,8 @@ MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
 
     // staging for the host-array entry points
     const size_t hid = (size_t)cfg.heads * HD;
-    if (cudaMalloc(&c->d_streams, cfg.max_batch * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
-    if (cudaMalloc(&c->d_positions, cfg.max_batch * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMalloc(&c->d_ids, 2 * cfg.max_batch * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
+    if (cudaMallocHost(&c->h_ids, 2 * cfg.max_batch * sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
     if (cudaMalloc(&c->d_qkv, (size_t)cfg.layers * cfg.max_batch * 3 * hid * sizeof(float)) != cudaSuccess)
         return bail(MB_ERR_OOM);
     if (cudaMalloc(&c->d_out, (size_t)cfg.layers * cfg.max_batch * hid * sizeof(float)) != cudaSuccess)
@@ -221,7 +221,7 @@ MB_API int mb_destroy(mb_ctx* c) {
     {
         DeviceGuard g(c->cfg.device);
         void* ptrs[] = {c->kv, c->slot_pos, c->rope, c->d_err, c->scratch.part, c->scratch.counters,
-                        c->d_streams, c->d_positions, c->d_qkv, c->d_out};
+                        c->d_ids, c->d_qkv, c->d_out};
         for (void* p : ptrs)
             if (p) cudaFree(p);
         for (auto* evs : {&c->ev_in, &c->ev_done})
@@ -230,6 +230,7 @@ MB_API int mb_destroy(mb_ctx* c) {
         if (c->ev_start) cudaEventDestroy(c->ev_start);
         if (c->ev_end) cudaEventDestroy(c->ev_end);
         if (c->h_err) cudaFreeHost(c->h_err);
+        if (c->h_ids) cudaFreeHost(c->h_ids);
         if (c->cp_in) cudaStreamDestroy(c->cp_in);
         if (c->cp_out) cudaStreamDestroy(c->cp_out);
     }
@@ -337,6 +338,18 @@ MB_API int mb_sync(mb_ctx* c, void* cuda_stream) {
 // The end of a host-array call: the status word rides behind the outputs on
 // `copy_st` into pinned memory, so one synchronisation of `st` (which waits for
 // `copy_st`) returns both.
+// The stream ids and positions of a host-array call, packed into the context's
+// page-locked staging (ids, then positions) and copied in with one transfer: the
+// caller's arrays are usually pageable, and each pageable copy is staged and
+// synchronous on the host.  Every host-array call synchronises before it returns,
+// so the staging is free again when the next call packs it.
+static cudaError_t stage_ids(mb_ctx* c, int n, const int32_t* streams, const int32_t* positions,
+                             cudaStream_t st) {
+    memcpy(c->h_ids, streams, n * sizeof(int32_t));
+    memcpy(c->h_ids + n, positions, n * sizeof(int32_t));
+    return cudaMemcpyAsync(c->d_ids, c->h_ids, 2 * n * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+}
+
 static int finish_host_call(mb_ctx* c, cudaStream_t st, cudaStream_t copy_st) {
     CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, copy_st), "read device status");
     if (copy_st != st) {
@@ -358,10 +371,9 @@ MB_API int mb_append_attend_host(mb_ctx* c, int32_t layer, int32_t n, const int3
     DeviceGuard g(c->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     const size_t hid = (size_t)c->cfg.heads * HD;
-    CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy streams");
-    CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, st), "copy positions");
+    CK(stage_ids(c, n, streams, positions, st), "copy streams and positions");
     CK(cudaMemcpyAsync(c->d_qkv, qkv, n * 3 * hid * sizeof(float), cudaMemcpyHostToDevice, st), "copy qkv");
-    CK(run_decode(c, true, layer, n, c->d_streams, c->d_positions, c->d_qkv, 3 * (int)hid, c->d_out, st),
+    CK(run_decode(c, true, layer, n, c->d_ids, c->d_ids + n, c->d_qkv, 3 * (int)hid, c->d_out, st),
        "append_attend launch");
     CK(cudaMemcpyAsync(out, c->d_out, n * hid * sizeof(float), cudaMemcpyDeviceToHost, st), "copy out");
     return finish_host_call(c, st, st);
@@ -427,9 +439,7 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
     CK(cudaEventRecord(c->ev_start, st), "order copies");
     CK(cudaStreamWaitEvent(c->cp_in, c->ev_start, 0), "order copies");
     CK(cudaStreamWaitEvent(c->cp_out, c->ev_start, 0), "order copies");
-    CK(cudaMemcpyAsync(c->d_streams, streams, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->cp_in), "copy streams");
-    CK(cudaMemcpyAsync(c->d_positions, positions, n * sizeof(int32_t), cudaMemcpyHostToDevice, c->cp_in),
-       "copy positions");
+    CK(stage_ids(c, n, streams, positions, c->cp_in), "copy streams and positions");
     for (size_t l = 0, gi = 0; l < L; gi++) {
         size_t end = l + 1;
         while (end < L && !in_start[end]) end++;
@@ -441,7 +451,7 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
     }
     for (size_t l = 0, gi = 0, go = 0, first_out = 0; l < L; l++) {
         if (in_start[l]) CK(cudaStreamWaitEvent(st, c->ev_in[gi++], 0), "wait qkv");
-        CK(run_decode(c, true, (int)l, n, c->d_streams, c->d_positions, c->d_qkv + l * in_l, 3 * (int)hid,
+        CK(run_decode(c, true, (int)l, n, c->d_ids, c->d_ids + n, c->d_qkv + l * in_l, 3 * (int)hid,
                       c->d_out + l * out_l, st, l > 0),
            "append_attend launch");
         if (!out_end[l]) continue;

@@ -53,8 +53,8 @@ struct mb_ctx {
     mb::Scratch scratch{};
     size_t scratch_bytes = 0;
     // staging for the host-array entry points
-    int32_t* d_streams = nullptr;
-    int32_t* d_positions = nullptr;
+    int32_t* d_ids = nullptr;  // [2][max_batch]: a call's stream ids, then its positions
+    int32_t* h_ids = nullptr;  // page-locked staging of the same, one copy per call
     float* d_qkv = nullptr;   // [layers][max_batch][3*H*64]
     float* d_out = nullptr;   // [layers][max_batch][H*64]
     // mb_decode_step_host's copy pipeline: inputs in and outputs out in groups of
