@@ -7,7 +7,10 @@ A *step* is one decode frame of every stream this GPU owns: 12 launches of the
 fused append+attend kernel (one per layer), through the C ABI (mb_decode_step).
 Workloads:
   2 (default)  64 streams/GPU, 12 layers x 12 heads x 64, fp32 ring of 512 slots;
-               positions 0..1499 (the ring wraps twice), repeated, reset between passes
+               positions 0..1499 (the ring wraps twice), repeated, reset between passes.
+               With fewer timed steps than the job has (the driver's --steps 20),
+               the whole job still runs, and the K timed steps sit at positions
+               spread evenly over it, each timed alone with L2 flushed before it
   5            512 streams/GPU, bf16 ring of 4096 slots, live lengths U[1, 4096]
                from a seed, consecutive appends (streams shard by length at N > 1)
 Weak scaling: every GPU runs its own streams; no collective on the decode path
@@ -215,6 +218,15 @@ def live_len(pos, capacity):
     return np.minimum(pos + 1, capacity)
 
 
+def sampled_positions(job_steps, k):
+    """K positions spread evenly over a job of `job_steps` steps: step t at
+    floor((t + 1/2) * job_steps / K), so the timed windows follow the job's own mix."""
+    return [int((t + 0.5) * job_steps / k) for t in range(k)]
+
+
+L2_FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
+
+
 def run_ours(args, cfg, rank, world, device):
     import torch
 
@@ -224,19 +236,26 @@ def run_ours(args, cfg, rank, world, device):
     n, L, C = cfg["streams"], cfg["layers"], cfg["capacity"]
     K, W = args.steps, args.warmup
     es = _esize(cfg["dtype"])
-    # positions of every step, staged on the device (warm-up steps first)
-    steps_total = W + K
-    pos_host = np.stack([positions_for(cfg, t, n, lengths0) for t in range(steps_total)])
-    if lengths0 is None and cfg.get("start") is None:  # config 2: warm-up 0..W-1, then the job from 0
-        pos_host[W:] = np.stack([positions_for(cfg, t, n, None) for t in range(K)])
+    job = lengths0 is None and cfg.get("start") is None  # config 2's 1500-frame job
+    J = cfg["job_steps"]
+    # Sampled: fewer timed steps than the job has.  The whole job runs (so every
+    # ring holds exactly the job's state), and only K steps spread evenly over it
+    # are timed, each with its own event pair and with L2 flushed before it.
+    sampled = job and K < J
+    if sampled:
+        timed = sampled_positions(J, K)
+        pos_host = np.stack([positions_for(cfg, t, n, None) for t in range(J)])
+    else:
+        pos_host = np.stack([positions_for(cfg, t, n, lengths0) for t in range(W + K)])
+        if job:  # warm-up 0..W-1, then the job from 0
+            pos_host[W:] = np.stack([positions_for(cfg, t, n, None) for t in range(K)])
+        timed = list(range(W, W + K))
     pos_dev = torch.from_numpy(pos_host).to(device)
-    algo_bytes = sum(float(window_bytes(live_len(pos_host[t].astype(np.int64), C), es, L).sum())
-                     for t in range(W, steps_total))
-
-    job = lengths0 is None and cfg.get("start") is None  # the 1500-frame job with resets
+    algo_bytes = sum(float(window_bytes(live_len(pos_host[t].astype(np.int64), C), es, L).sum()) for t in timed)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device) if sampled else None
 
     def step(t):
-        if job and t >= W and (t - W) % cfg["job_steps"] == 0:
+        if job and not sampled and t >= W and (t - W) % J == 0:
             ring.reset()  # a new pass of the 1500-frame job starts from an empty ring
         ring.decode_step(streams, pos_dev[t], qkv_pool[t % qkv_pool.shape[0]], out)
 
@@ -252,17 +271,31 @@ def run_ours(args, cfg, rank, world, device):
     clocks = ClockSampler(device.index)
     clocks.start()
     stream = torch.cuda.current_stream(device)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for t in range(W, steps_total):
-        step(t)
-    ev1.record(stream)
-    torch.cuda.synchronize(device)
+    if sampled:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in timed]
+        k = 0
+        for t in range(J):
+            if k < K and t == timed[k]:
+                flush.zero_()
+                evs[k][0].record(stream)
+                step(t)
+                evs[k][1].record(stream)
+                k += 1
+            else:
+                step(t)
+        torch.cuda.synchronize(device)
+        ms = sum(a.elapsed_time(b) for a, b in evs)
+    else:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for t in range(W, W + K):
+            step(t)
+        ev1.record(stream)
+        torch.cuda.synchronize(device)
+        ms = ev0.elapsed_time(ev1)
     if dist:
         dist.barrier()
-    clk = clocks.stop()
     ring.sync()
-    ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, device if dist else None)
     launches = L * K
 
@@ -284,22 +317,39 @@ def run_ours(args, cfg, rank, world, device):
             fill_lengths(ring, lengths0, L, gen, device)
             for t in range(W):
                 step(t)
-        e2e_steps = K
         if dist:
             dist.barrier()
         torch.cuda.synchronize(device)
-        t0 = time.perf_counter()
-        for t in range(e2e_steps):
-            if lengths0 is None and t > 0 and t % cfg["job_steps"] == 0:
-                ring.reset()
-            pos = positions_for(cfg, t, n, None) if lengths0 is None else pos_host[W + t]
-            ring.decode_step_host(ids, pos, host_qkv[t % sets], host_out)
-        torch.cuda.synchronize(device)
-        e2e_s = max_over_ranks(time.perf_counter() - t0, device if dist else None)
-        e2e = {"value": world * n * e2e_steps / e2e_s, "unit": "frames/s",
+        if sampled:  # the same K job positions through the host call; the other steps on the device
+            e2e_s, k = 0.0, 0
+            for t in range(J):
+                if k < K and t == timed[k]:
+                    flush.zero_()
+                    stream.synchronize()
+                    t0 = time.perf_counter()
+                    ring.decode_step_host(ids, pos_host[t], host_qkv[t % sets], host_out)
+                    e2e_s += time.perf_counter() - t0
+                    k += 1
+                else:
+                    step(t)
+            torch.cuda.synchronize(device)
+        else:
+            t0 = time.perf_counter()
+            for t in range(K):
+                if lengths0 is None and t > 0 and t % J == 0:
+                    ring.reset()
+                pos = positions_for(cfg, t, n, None) if lengths0 is None else pos_host[W + t]
+                ring.decode_step_host(ids, pos, host_qkv[t % sets], host_out)
+            torch.cuda.synchronize(device)
+            e2e_s = time.perf_counter() - t0
+        e2e_s = max_over_ranks(e2e_s, device if dist else None)
+        e2e = {"value": world * n * K / e2e_s, "unit": "frames/s",
                "h2d_bytes_per_step": int(L * n * QKV * 4 + 2 * n * 4),
                "d2h_bytes_per_step": int(L * n * HID * 4),
-               "steps": e2e_steps, "api": "mb_decode_step_host (C ABI, pinned host buffers, blocking per step)"}
+               "steps": K, "api": "mb_decode_step_host (C ABI, pinned host buffers, blocking per step)"
+               + ("; the same K sampled job positions, wall clock per call, L2 flushed before each" if sampled
+                  else "")}
+    clk = clocks.stop()
 
     value = world * n * K / (ms_max / 1e3)
     peak, peak_kind = peaks()
@@ -315,8 +365,18 @@ def run_ours(args, cfg, rank, world, device):
                 "kernel": "decode_kernel<fused append+RoPE+split-K attention>",
                 "algorithmic_bytes_per_launch": algo_bytes / launches,
                 "avg_launch_us": ms * 1e3 / launches,
-                "timing": "CUDA events over the timed region on the launching stream; every launch in the region "
-                          "is this kernel, so avg launch = region / launches (launch gaps included)"}
+                "timing": ("CUDA events around each timed step on the launching stream (sum over the K steps); "
+                           if sampled else "CUDA events over the timed region on the launching stream; ")
+                + "every launch timed is this kernel, so avg launch = timed time / launches (launch gaps included)"}
+    if sampled:
+        timing_note = (f"{K} of the job's {J} steps timed, at positions floor((t + 1/2) * {J} / {K}) "
+                       f"({timed[0]}, {timed[1] if K > 1 else ''} ... {timed[-1]}); the other steps run untimed "
+                       f"in order, so each timed step sees the job's own ring; L2 flushed (256 MB write) before "
+                       f"each timed step")
+    elif job:
+        timing_note = f"{K} consecutive steps of the job (positions t mod {J}, reset between passes)"
+    else:
+        timing_note = f"{K} consecutive steps"
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "frames/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms_max / K, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -324,8 +384,13 @@ def run_ours(args, cfg, rank, world, device):
         "config": {"workload": cfg["workload"], "streams_per_gpu": n, "global_streams": info["global_streams"],
                    "layers": L, "heads": H, "head_dim": HD, "capacity": C, "storage": cfg["dtype"],
                    "parallelism": f"stream-sharded x{world} (no collective on the decode path)",
-                   "l2": "inputs larger than L2: every step streams the live K/V windows "
-                         f"(~{algo_bytes / K / 1e9:.2f} GB/step) plus {info['qkv_pool_sets']} rotating qkv sets",
+                   "timed_steps": timing_note,
+                   "mean_window": round(float(np.mean([live_len(pos_host[t].astype(np.int64), C).mean()
+                                                       for t in timed])), 1),
+                   "l2": (f"L2 flushed before every timed step; ~{algo_bytes / K / 1e9:.2f} GB of K/V windows per "
+                          "timed step" if sampled else
+                          "inputs larger than L2: every step streams the live K/V windows "
+                          f"(~{algo_bytes / K / 1e9:.2f} GB/step) plus {info['qkv_pool_sets']} rotating qkv sets"),
                    "value_per_gpu": round(value / world, 1)},
         "roofline": roofline, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
     }
@@ -769,10 +834,23 @@ def run_cpu(cfg, steps, warmup, sample_streams, budget_s=None):
             break
     dt = time.perf_counter() - t0
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    if lengths0 is None:
+        what = (f"the whole {cfg['job_steps']}-step job (positions 0..{cfg['job_steps'] - 1})"
+                if done == cfg["job_steps"] else f"the first {done} steps of the job (time budget)")
+    else:
+        what = f"{done} consecutive steps from the seeded live lengths"
     return {"value": round(n * done / dt, 2), "unit": "frames/s", "cores": cores, "kind": "port",
-            "sample": f"{n} of the workload's streams x {done} consecutive steps (positions as in the GPU run), "
-                      f"all {L} layers per frame, oracle/oracle.c fp32 mirror of the WGSL kernels, "
-                      f"OpenMP over (stream, head), {dt:.1f} s"}
+            "sample": f"{n} of the workload's streams x {what}, all {L} layers per frame, oracle/oracle.c fp32 "
+                      f"mirror of the WGSL kernels, OpenMP over (stream, head), {dt:.1f} s"}
+
+
+def cpu_job_steps(cfg, steps):
+    """Steps of a CPU leg: config 2's whole job (its windows grow, then wrap, so
+    a prefix would time only short windows); for config 5 its default 200
+    serving steps, or more if the GPU arm runs more."""
+    if cfg["job_steps"] is not None:
+        return cfg["job_steps"]
+    return max(steps, cfg["steps"])
 
 
 def run_cpu_prefill(cfg, steps, warmup, sample_streams=1, budget_s=None):
@@ -849,7 +927,7 @@ def main():
             base = run_cpu_local(cfg, args.steps, sample_streams=2, budget_s=120.0)
             metric, unit = LOCAL_METRIC, "frames/s"
         else:
-            base = run_cpu(cfg, args.steps, args.warmup, sample_streams=4)
+            base = run_cpu(cfg, cpu_job_steps(cfg, args.steps), args.warmup, sample_streams=4, budget_s=240.0)
             metric, unit = METRIC, "frames/s"
         line = {"metric": metric, "value": base["value"], "unit": unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
@@ -889,8 +967,8 @@ def main():
         elif args.config == 6:
             result["cpu_baseline"] = run_cpu_local(cfg, 3, sample_streams=2, budget_s=30.0)
         else:
-            result["cpu_baseline"] = run_cpu(cfg, min(args.steps, cfg["job_steps"] or args.steps), 2,
-                                             sample_streams=4, budget_s=30.0)
+            result["cpu_baseline"] = run_cpu(cfg, cpu_job_steps(cfg, args.steps), 2, sample_streams=4,
+                                             budget_s=60.0)
     elif rank == 0:
         result["cpu_baseline"] = None
     ring.dispose()

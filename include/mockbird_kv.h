@@ -321,8 +321,12 @@ typedef struct mb_ring_ref {
  * call before any stream capture.  Every call shares the one array and its
  * ticket counters are cleared at the start of each call: calls that overlap on
  * the GPU (other streams, other threads) race and must be serialised by the
- * caller.  Uses the current CUDA device.  Returns MB_ERR_ARG for bad arguments
- * or a call that needs more than MB_NOALLOC_SCRATCH_BYTES of scratch. */
+ * caller.  Uses the current CUDA device, in its primary context; the looked-up
+ * address stays cached for the life of the process, so do not reset the device
+ * (cudaDeviceReset) while using this entry point.  Returns MB_ERR_ARG for bad
+ * arguments -- null or misaligned pointers (qkv, out and kv 16-byte aligned,
+ * rope 8-byte, streams, positions, slot_pos and status 4-byte) -- or for a call
+ * that needs more than MB_NOALLOC_SCRATCH_BYTES of scratch. */
 MB_API int mb_append_attend_noalloc(const mb_ring_ref* ring, int32_t layer, int32_t n, const int32_t* streams,
                                     const int32_t* positions, const float* qkv, float* out, void* cuda_stream);
 

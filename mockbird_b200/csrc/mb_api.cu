@@ -202,7 +202,8 @@ MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
     if (cudaStreamCreateWithFlags(&c->cp_in, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->cp_out, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_ids, cudaEventDisableTiming) != cudaSuccess)
         return bail(MB_ERR_CUDA);
     if (cudaMallocHost(&c->h_err, sizeof(int32_t)) != cudaSuccess) return bail(MB_ERR_OOM);
     c->ev_in.assign(cfg.layers, nullptr);
@@ -229,6 +230,7 @@ MB_API int mb_destroy(mb_ctx* c) {
                 if (e) cudaEventDestroy(e);
         if (c->ev_start) cudaEventDestroy(c->ev_start);
         if (c->ev_end) cudaEventDestroy(c->ev_end);
+        if (c->ev_ids) cudaEventDestroy(c->ev_ids);
         if (c->h_err) cudaFreeHost(c->h_err);
         if (c->h_ids) cudaFreeHost(c->h_ids);
         if (c->cp_in) cudaStreamDestroy(c->cp_in);
@@ -341,13 +343,17 @@ MB_API int mb_sync(mb_ctx* c, void* cuda_stream) {
 // The stream ids and positions of a host-array call, packed into the context's
 // page-locked staging (ids, then positions) and copied in with one transfer: the
 // caller's arrays are usually pageable, and each pageable copy is staged and
-// synchronous on the host.  Every host-array call synchronises before it returns,
-// so the staging is free again when the next call packs it.
+// synchronous on the host.  A call that succeeds synchronises before it returns,
+// but one that fails after queueing this copy returns without waiting, so the
+// staging is reused only once the event behind the previous copy has completed.
 static cudaError_t stage_ids(mb_ctx* c, int n, const int32_t* streams, const int32_t* positions,
                              cudaStream_t st) {
+    cudaError_t e = cudaEventSynchronize(c->ev_ids);
+    if (e != cudaSuccess) return e;
     memcpy(c->h_ids, streams, n * sizeof(int32_t));
     memcpy(c->h_ids + n, positions, n * sizeof(int32_t));
-    return cudaMemcpyAsync(c->d_ids, c->h_ids, 2 * n * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+    e = cudaMemcpyAsync(c->d_ids, c->h_ids, 2 * n * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+    return e == cudaSuccess ? cudaEventRecord(c->ev_ids, st) : e;
 }
 
 static int finish_host_call(mb_ctx* c, cudaStream_t st, cudaStream_t copy_st) {

@@ -55,6 +55,7 @@ struct mb_ctx {
     // staging for the host-array entry points
     int32_t* d_ids = nullptr;  // [2][max_batch]: a call's stream ids, then its positions
     int32_t* h_ids = nullptr;  // page-locked staging of the same, one copy per call
+    cudaEvent_t ev_ids = nullptr;  // recorded behind the copy out of h_ids
     float* d_qkv = nullptr;   // [layers][max_batch][3*H*64]
     float* d_out = nullptr;   // [layers][max_batch][H*64]
     // mb_decode_step_host's copy pipeline: inputs in and outputs out in groups of

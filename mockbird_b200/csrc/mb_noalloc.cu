@@ -18,7 +18,8 @@ void* g_scratch_addr[kMaxDevices] = {};
 
 // Host code cannot use g_noalloc_scratch as a device address (on the host it
 // names a stand-in); look up the device address once per device, with that
-// device current.
+// device current.  The address belongs to the device's primary context: a
+// cudaDeviceReset while the library is loaded would leave it stale.
 int scratch_address(int device, void** out) {
     if (device < 0 || device >= kMaxDevices) return MB_ERR_ARG;
     std::lock_guard<std::mutex> lock(g_setup_mutex);
@@ -45,8 +46,14 @@ extern "C" MB_API int mb_append_attend_noalloc(const mb_ring_ref* ring, int32_t 
     if (layer < 0 || layer >= ring->layers) return MB_ERR_LAYER;
     if (n < 0 || n > 65535) return MB_ERR_ARG;
     if (n == 0) return MB_OK;
-    if (!streams || !positions || !qkv || !out || (reinterpret_cast<uintptr_t>(qkv) & 15) ||
-        (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(ring->kv) & 15))
+    // the kernel reads qkv and the ring 16 bytes at a time, the RoPE table as
+    // (cos, sin) float2 pairs, and stream ids, positions, slot positions and the
+    // status word as int32 (the status by atomics): misaligned pointers are
+    // rejected here rather than faulting on the device
+    auto mis = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; };
+    if (!streams || !positions || !qkv || !out || mis(qkv, 16) || mis(out, 16) || mis(ring->kv, 16) ||
+        mis(ring->rope, 8) || mis(ring->slot_pos, 4) || mis(ring->status, 4) || mis(streams, 4) ||
+        mis(positions, 4))
         return MB_ERR_ARG;
 
     // scratch needed by this call: partials, then counters

@@ -77,7 +77,6 @@ def init_group(backend: str, timeout_s: float = 120.0, device=None):
 
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     os.environ.setdefault("MASTER_PORT", "29511")
-    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout for the report line
     rank, world, _ = dist_env()
     if not dist.is_initialized():
         kw = {"device_id": device} if device is not None else {}

@@ -96,3 +96,36 @@ def test_host_buffers_are_checked_before_the_call():
                 torch.zeros(3, 2).t(), torch.zeros(2, 3, dtype=torch.int32), [[0.0] * 3] * 2):
         with pytest.raises(TypeError):
             _host_array("x", bad, (2, 3), "float32")
+
+
+@pytest.mark.parametrize("field,offset", [("rope", 4), ("slot_pos", 2), ("status", 1), ("kv", 8),
+                                          ("streams", 2), ("positions", 1), ("qkv", 8), ("out", 4)])
+def test_noalloc_rejects_misaligned_pointers(lib, field, offset):
+    """mb_append_attend_noalloc refuses, before any CUDA call, a pointer that its
+    kernel would read with a wider access than the pointer's alignment allows
+    (16-byte rows, 8-byte RoPE pairs, 4-byte ids and status atomics): MB_ERR_ARG
+    instead of a misaligned access on the device.  No GPU is needed: with every
+    pointer aligned the same call gets past the checks and fails at the device
+    query (MB_ERR_CUDA here)."""
+    base = 0x10000  # a fake 256-byte-aligned address; never dereferenced
+    ring = _lib.MbRingRef(base, base, base, base, 1, 12, 64, 1, _lib.MB_F32, 1, 64)
+    args = {"streams": base, "positions": base, "qkv": base, "out": base}
+    if field in args:
+        args[field] += offset
+    else:
+        setattr(ring, field, base + offset)
+    rc = lib.mb_append_attend_noalloc(ctypes.byref(ring), 0, 1, args["streams"], args["positions"], args["qkv"],
+                                      args["out"], None)
+    assert rc == 1  # MB_ERR_ARG
+
+
+def test_noalloc_checks_pass_for_aligned_pointers(lib):
+    """The counterpart of the test above, on a machine without a GPU: aligned
+    pointers pass every argument check and the call stops at the device query."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("only meaningful without a GPU (the call would otherwise run)")
+    base = 0x10000
+    ring = _lib.MbRingRef(base, base, base, base, 1, 12, 64, 1, _lib.MB_F32, 1, 64)
+    assert lib.mb_append_attend_noalloc(ctypes.byref(ring), 0, 1, base, base, base, base, None) == 6  # MB_ERR_CUDA

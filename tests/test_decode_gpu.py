@@ -204,6 +204,67 @@ def test_variable_live_lengths_bf16():
         assert_window_equal(ring, orc, 0, s, 0, s, p)
 
 
+def test_config5_shape_long_uneven_windows_bf16():
+    """BASELINE config 5's shape: bf16 ring of C = 4096 slots, 64 streams with
+    seeded live lengths U[1, 4096], 200 consecutive steps of appends, all streams
+    in one launch per step.  Windows reach 32 split-K chunks (the path without the
+    L2 prefetch, taken above 16 chunks), and the longest streams wrap during the
+    run.  The oracle replays 8 of the streams in lockstep (the 3 longest, the 2
+    shortest, 3 others): contexts within 1e-2 of its fp32 mirror and of its fp64
+    mode; their windows bit-exact; the final slot order of all 64 streams."""
+    S, C, STEPS = 64, 4096, 200
+    rng = np.random.default_rng(2024)
+    lengths = rng.integers(1, C + 1, size=S)
+    by_len = np.argsort(lengths)
+    others = [s for s in rng.permutation(S) if s not in set(by_len[:2]) | set(by_len[-3:])][:3]
+    track = [int(x) for x in list(by_len[-3:]) + list(by_len[:2]) + others]
+    assert lengths[track[0]] + STEPS - 1 > C, "the longest tracked stream must wrap"
+    ring = KvRing(layers=1, streams=S, capacity=C, dtype="bf16", wrap=True, max_position=8192)
+    orc = oracle.Ring(layers=1, streams=len(track), heads=H, capacity=C, dtype="bf16", wrap=True,
+                      max_position=8192)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(11)
+    for s in range(S):  # positions 0..L-2 of every stream, N(0, 1) rows rounded to bf16
+        n = int(lengths[s]) - 1
+        if n == 0:
+            continue
+        k = torch.randn(H, n, HD, generator=gen, device=DEV).to(torch.bfloat16)
+        v = torch.randn(H, n, HD, generator=gen, device=DEV).to(torch.bfloat16)
+        ring.ring_write(0, s, 0, k, v)
+        if s in track:
+            t = track.index(s)
+            orc.kv_view()[0, t, 0, :, :n] = to_np_storage(k)
+            orc.kv_view()[0, t, 1, :, :n] = to_np_storage(v)
+            orc.slot_pos[0, t, :n] = np.arange(n)
+    order = [int(x) for x in rng.permutation(S)]
+    rows = [order.index(s) for s in track]
+    worst = worst64 = 0.0
+    for step in range(STEPS):
+        pos = [int(lengths[s]) - 1 + step for s in order]
+        qkv = randn((S, QKV), seed=7000 + step)
+        out = ring.append_attend(0, order, pos, torch.from_numpy(qkv).to(DEV)).cpu().numpy()
+        tpos = [pos[r] for r in rows]
+        ref, q_roped = orc.append_attend(0, list(range(len(track))), tpos, qkv[rows])
+        worst = max(worst, max_err(out[rows], ref))
+        if step % 25 == 0 or step == STEPS - 1:
+            ref64 = orc.attend(0, list(range(len(track))), tpos, q_roped, mode=1)
+            worst64 = max(worst64, max_err(out[rows], ref64))
+        if step in (0, 99):
+            ring.sync()
+            for t, s in enumerate(track):
+                assert_window_equal(ring, orc, 0, s, 0, t, tpos[t])
+    ring.sync()
+    assert worst < TOL["bf16"], worst
+    assert worst64 < TOL["bf16"], worst64
+    for t, s in enumerate(track):
+        assert_window_equal(ring, orc, 0, s, 0, t, int(lengths[s]) - 1 + STEPS - 1)
+    for s in range(S):
+        p = int(lengths[s]) - 1 + STEPS - 1
+        W = min(p + 1, C)
+        _, _, slots = ring.gather(0, s, p)
+        assert np.array_equal(slots.cpu().numpy(), np.array([q % C for q in range(p - W + 1, p + 1)], np.int32)), s
+
+
 def test_host_entry_points_match_device_path():
     S, C, L = 3, 128, 12
     a = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)

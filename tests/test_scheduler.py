@@ -116,3 +116,43 @@ def test_rank_failure_surfaces_as_an_error():
     assert out[1] == "raised"
     assert out[0].startswith("error"), out[0]
     assert procs[1].exitcode == 3
+
+
+def _balance_worker(rank, world, port, q):
+    """Each rank computes its own share of BASELINE config 5's length-balanced split
+    (4096 streams over 8 shards, seeded lengths U[1, 4096]); the ranks gather their
+    shards' total live lengths and stream counts."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    from mockbird_b200.scheduler import gather_reports, init_group
+
+    dist = init_group("gloo", timeout_s=30)
+    lengths = np.random.default_rng(0).integers(1, 4097, size=4096)
+    shards = partition_streams(4096, 8, lengths)
+    mine = [shards[i] for i in range(rank, 8, world)]  # this rank's 4 of the 8 shards
+    reports = [gather_reports({"shard": sh.rank, "load": int(lengths[sh.streams].sum()), "count": sh.count})
+               for sh in mine]
+    q.put((rank, [r for rep in reports for r in rep], int(lengths.max())))
+    dist.destroy_process_group()
+
+
+def test_two_rank_config5_length_balance():
+    """Run as 2 gloo ranks: config 5's 8 shards each carry the same number of
+    streams (512) and their total live lengths differ by less than the longest
+    stream's length (one stream's worth of imbalance at most)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_balance_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict((r, (reps, mx)) for r, reps, mx in (q.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results[0][0] == results[1][0]  # both ranks saw every shard's report
+    reps, longest = results[0]
+    by_shard = {int(r["shard"]): r for r in reps}
+    assert sorted(by_shard) == list(range(8))
+    loads = [by_shard[i]["load"] for i in range(8)]
+    assert {int(by_shard[i]["count"]) for i in range(8)} == {512}
+    assert max(loads) - min(loads) <= longest

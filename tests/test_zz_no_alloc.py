@@ -22,7 +22,9 @@ pytestmark = pytest.mark.gpu
 
 H, HD = 12, 64
 QKV = 3 * H * HD
-TOL_F32 = 2e-3  # the fp32-storage attention tolerance used by every decode test
+TOL = {"f32": 2e-3, "bf16": 1e-2, "f16": 1e-2}  # the attention tolerances every decode test uses
+TORCH = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+CODE = {"f32": _lib.MB_F32, "bf16": _lib.MB_BF16, "f16": _lib.MB_F16}
 
 
 def _rope_table(max_position, theta=10000.0):
@@ -32,29 +34,34 @@ def _rope_table(max_position, theta=10000.0):
     return np.stack([np.cos(ang), np.sin(ang)], -1).astype(np.float32)  # [P][32][2]
 
 
-def test_noalloc_matches_the_allocating_entry_point():
+# capacity 300: windows of 4 fp32 / 2 16-bit split-K chunks, whose partials go
+# through the fixed scratch array; capacity 17: the warp-per-head path of rings
+# of at most 32 slots (no split-K), wrapping on the second call
+@pytest.mark.parametrize("dtype,capacity,filled", [("f32", 300, 250), ("bf16", 300, 250), ("f16", 300, 250),
+                                                   ("f32", 17, 16), ("bf16", 17, 16)])
+def test_noalloc_matches_the_allocating_entry_point(dtype, capacity, filled):
     lib = _lib.load()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    L, S, C, P = 2, 4, 300, 4096
-    ref = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True, max_position=P)
+    L, S, C, P = 2, 4, capacity, 4096
+    td = TORCH[dtype]
+    ref = KvRing(layers=L, streams=S, capacity=C, dtype=dtype, wrap=True, max_position=P)
 
     # caller-owned ring, laid out like a context's
-    kv = torch.zeros(L, S, 2, H, C, HD, dtype=torch.float32, device=dev)
+    kv = torch.zeros(L, S, 2, H, C, HD, dtype=td, device=dev)
     slot_pos = torch.full((L, S, C), -1, dtype=torch.int32, device=dev)
     rope = torch.from_numpy(_rope_table(P)).to(dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     ring = _lib.MbRingRef(kv.data_ptr(), slot_pos.data_ptr(), rope.data_ptr(), status.data_ptr(),
-                          L, H, C, S, _lib.MB_F32, 1, P)
+                          L, H, C, S, CODE[dtype], 1, P)
 
-    # the same 250 earlier positions in both rings
+    # the same earlier positions in both rings
     g = torch.Generator(device=dev)
     g.manual_seed(0)
-    filled = 250
     for layer in range(L):
         for s in range(S):
-            k = torch.randn(H, filled, HD, generator=g, device=dev)
-            v = torch.randn(H, filled, HD, generator=g, device=dev)
+            k = torch.randn(H, filled, HD, generator=g, device=dev).to(td)
+            v = torch.randn(H, filled, HD, generator=g, device=dev).to(td)
             ref.ring_write(layer, s, 0, k, v)
             kv[layer, s, 0, :, :filled] = k
             kv[layer, s, 1, :, :filled] = v
@@ -62,7 +69,7 @@ def test_noalloc_matches_the_allocating_entry_point():
 
     items = torch.tensor([2, 0, 3], dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    for step in (filled, filled + 1):  # two calls in a row; windows of 251 and 252 slots (4 chunks)
+    for step in (filled, filled + 1):  # two calls in a row
         pos = torch.full((3,), step, dtype=torch.int32, device=dev)
         qkv = torch.randn(3, QKV, generator=g, device=dev)
         want = ref.append_attend(1, items, pos, qkv)
@@ -72,13 +79,14 @@ def test_noalloc_matches_the_allocating_entry_point():
                                           ctypes.c_void_p(got.data_ptr()), ctypes.c_void_p(stream.cuda_stream))
         assert rc == 0
         torch.cuda.synchronize(dev)
-        assert float((got - want).abs().max()) < TOL_F32
-        # the appended rows and positions agree too
+        assert float((got - want).abs().max()) < TOL[dtype]
+        # the appended rows and positions agree bit for bit: both calls rope the
+        # same row with the same table values
         k_ref, v_ref, slots_ref = ref.gather(1, 2, step)
         W = min(step + 1, C)
         assert torch.equal(slot_pos[1, 2][slots_ref.long()],
                            torch.arange(step - W + 1, step + 1, device=dev, dtype=torch.int32))
-        assert float((kv[1, 2, 0, :, step % C] - k_ref[:, -1]).abs().max()) < 1e-6
+        assert torch.equal(kv[1, 2, 0, :, step % C], k_ref[:, -1])
         assert torch.equal(kv[1, 2, 1, :, step % C], v_ref[:, -1])
     ref.sync()
     assert int(status.item()) == 0
