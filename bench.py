@@ -545,12 +545,15 @@ def run_decoder(args, cfg, rank, world, device):
     ring.sync()
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, device if dist else None)
-    # e2e: embedded rows from pinned host memory in, ln_f rows out, every step.
-    # The rings are restored and the warm-up replayed first, so the e2e steps run
-    # the timed region's positions over the same windows.
-    host_in = torch.empty(2, n, HID).pin_memory()
-    host_in.copy_(rows[:2].cpu())
-    host_out = torch.empty(n, HID).pin_memory()
+    # e2e: through mb_decoder_step_host, the call DecodeRunner.globalStep makes --
+    # the embedded rows from pinned host memory in, the ln_f rows back into the
+    # same buffer, one synchronisation per step (each step's output row is the
+    # next step's input row).  The rings are restored and the warm-up replayed
+    # first, so the e2e steps run the timed region's positions over the same windows.
+    host_rows = torch.empty(n, HID).pin_memory()
+    host_rows.copy_(rows[0].cpu())
+    ids = np.arange(n, dtype=np.int32)
+    pos_host = np.stack([(pos0 + t).astype(np.int32) for t in range(W + K)])
     fill()
     for t in range(W):
         hidden.copy_(rows[t % 8])
@@ -560,10 +563,7 @@ def run_decoder(args, cfg, rank, world, device):
         dist.barrier()
     t0 = time.perf_counter()
     for t in range(W, W + K):
-        hidden.copy_(host_in[t % 2], non_blocking=True)
-        dec.step(streams, pos_dev[t], hidden)
-        host_out.copy_(hidden, non_blocking=True)
-        stream.synchronize()
+        dec.step_host(ids, pos_host[t], host_rows)
     e2e_s = max_over_ranks(time.perf_counter() - t0, device if dist else None)
     es = _esize(cfg["dtype"])
     live = np.minimum(pos0[None, :] + np.arange(W, W + K)[:, None] + 1, C)
@@ -582,7 +582,8 @@ def run_decoder(args, cfg, rank, world, device):
                    "capacity": C, "ffn": F, "parallelism": f"stream-sharded x{world} (no collective on the decode path)",
                    "l2": f"inputs larger than L2: ~{kv_bytes / K / 1e9:.1f} GB of K/V windows per step",
                    "value_per_gpu": round(value / world, 1),
-                   "gemms": "cuBLASLt (library GEMMs); LayerNorm, GELU and the attention are this library's kernels"},
+                   "gemms": "this library's tcgen05 GEMMs (bias, residual and GELU in their epilogues); LayerNorm and "
+                            "the attention are this library's kernels too"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
@@ -591,12 +592,13 @@ def run_decoder(args, cfg, rank, world, device):
                                "weights + activations"},
         "e2e": {"value": round(world * n * K / e2e_s, 1), "unit": "frames/s",
                 "h2d_bytes_per_step": n * HID * 4, "d2h_bytes_per_step": n * HID * 4,
-                "api": "mb_decoder_step (C ABI) with the embedded rows copied from pinned host memory and the ln_f "
-                       "rows read back every step"},
-        "gpu_launches": K * (L * 5 + 1),
+                "api": "mb_decoder_step_host (C ABI): the embedded rows from pinned host memory in, the ln_f rows "
+                       "back to it, one synchronisation per step"},
+        "gpu_launches": K * (L * 7 + 1),
         "clocks": clk,
     }
-    result["gpu_launches_note"] = "5 of this library's kernels per layer (2 LayerNorm, attention, 2 conversions) + ln_f; the 4 GEMMs per layer are cuBLASLt"
+    result["gpu_launches_note"] = ("7 of this library's kernels per layer (LN1, QKV GEMM, attention, c_proj GEMM, LN2, "
+                                   "fc_in GEMM + GELU, fc_out GEMM) + ln_f")
     dec.dispose()
     return result, ring
 
@@ -740,8 +742,8 @@ def run_local(args, cfg, rank, world, device):
                    "l2": "weights (15.7 MB per step) are re-read every step and may stay in L2; the bound is "
                          "the tensor pipe at this batch", "cuda_graph": graph,
                    "value_per_gpu": round(value / world, 1),
-                   "gemms": "cuBLASLt (library GEMMs); embedding, LayerNorm, GELU, attention, text-head decision "
-                            "and argmax are this library's kernels"},
+                   "gemms": "this library's tcgen05 GEMMs; embedding, LayerNorm, attention, text-head decision "
+                            "and argmax are this library's kernels too"},
         "roofline": {"bound": "tensor", "achieved": round(flops / t_s / 1e12, 2), "peak": tpeak,
                      "unit": "TFLOP/s", "frac": round(flops / t_s / 1e12 / tpeak, 4), "traffic": None,
                      "peak_source": f"{tkind} bf16_tflops (burst)",
@@ -752,9 +754,10 @@ def run_local(args, cfg, rank, world, device):
                 "h2d_bytes_per_step": n * HID * 4, "d2h_bytes_per_step": n * (ch + 1) * 4,
                 "api": "mb_local_head_frame_host (C ABI): the hidden states from pinned host memory in, the "
                        "tokens and stop flags back to pinned host memory, one synchronisation per frame"},
-        "gpu_launches": K * ((ch + 1) * 7 + ch + 1),
-        "gpu_launches_note": "per step: embedding, 2 LayerNorms, attention, 2 conversions, ln_f, and the text "
-                             "decision (step 0) or the argmax (steps 1-16); the 5 GEMMs per step are cuBLASLt",
+        "gpu_launches": K * ((ch + 1) * 9 + 1),
+        "gpu_launches_note": "per step: LN2, ln_f, attention, the layer's 4 GEMMs, and the text decision (step 0) or "
+                             "the audio-head GEMM and the argmax (steps 1-16, the argmax also embedding and applying "
+                             "LN1 for the next step); steps 0 and 1 embed with their own kernel",
         "clocks": clk,
     }
     head.dispose()

@@ -181,9 +181,10 @@ MB_API int mb_sync(mb_ctx* ctx, void* cuda_stream);
  * transformer layer of DecodeRunner.runLayer (decode.ts:474-620) for n streams
  * at once -- LN1 -> QKV GEMM -> append + RoPE + attention -> c_proj GEMM +
  * residual -> LN2 -> fc_in GEMM + GELU(tanh) -> fc_out GEMM + residual -- and
- * the final LayerNorm, over a context's rings.  The GEMMs are cuBLASLt (bf16
- * weights, fp32 accumulation); LayerNorm (eps 1e-5), GELU(tanh) and the
- * attention are this library's kernels.
+ * the final LayerNorm, over a context's rings.  The GEMMs (mb_gemm_bf16 below,
+ * bf16 weights, fp32 accumulation on the tensor cores, bias / residual / GELU in
+ * their epilogues), LayerNorm (eps 1e-5) and the attention are this library's
+ * kernels.
  * ------------------------------------------------------------------------- */
 
 typedef struct mb_decoder mb_decoder;
@@ -205,6 +206,35 @@ MB_API int mb_decoder_destroy(mb_decoder* dec);
  * stream appends at its position in every layer's ring. */
 MB_API int mb_decoder_step(mb_decoder* dec, int32_t n, const int32_t* streams, const int32_t* positions,
                            float* hidden, void* cuda_stream);
+
+/* mb_decoder_step with HOST arrays -- the call DecodeRunner.globalStep makes
+ * (decode.ts:712-775: the embedded row written in, one submit of every layer,
+ * one readback of the ln_f row, decode.ts:774; gpu.ts:244 decodeStep): streams
+ * and positions [n] are checked on the host (range, duplicates, positions as
+ * mb_append_attend_host does), hidden [n][H*64] fp32 holds the embedded rows on
+ * entry and ln_f of the last layer on return; one synchronisation, and the
+ * ring's device status is reported as by mb_sync. */
+MB_API int mb_decoder_step_host(mb_decoder* dec, int32_t n, const int32_t* streams, const int32_t* positions,
+                                float* hidden, void* cuda_stream);
+
+/* GEMV (kernels-decode.ts:127-142: y = b + x W with W [K][N] row-major), the
+ * projection kernel of DecodeRunner.runLayer (decode.ts:517-526, 553-619), for
+ * m rows (streams) at once on the tensor cores -- the GEMM the decoder step runs
+ * for each of its projections, on the current device:
+ *   x    device bf16 [m][k]          (activation rows)
+ *   wt   device bf16 [n][k]          (W transposed: row j holds column j of W)
+ *   bias device f32 [n] or NULL
+ *   y    epi 0: device f32 [m][n] = x W + bias
+ *        epi 1: device f32 [m][n] += x W + bias      (the residual add)
+ *        epi 2: device bf16 [m][n] = gelu_tanh(x W + bias)   (GELU_TANH, :373-390)
+ * fp32 accumulation; k a multiple of 64, n of 32; every pointer 16-byte aligned
+ * (status 4-byte).  bn, splits: 0, 0 = the library's plan; else bn (32, 64 or
+ * 128, dividing n) output columns per CTA and K split over `splits` (1..8, at
+ * most k / 64) CTAs of a thread-block cluster, whose partials are summed in a
+ * fixed order.  status: device int32 the kernel ORs 8 into when a bounded wait
+ * gives up.  Async on cuda_stream. */
+MB_API int mb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void* x, const void* wt, const float* bias, void* y,
+                        int32_t epi, int32_t bn, int32_t splits, int32_t* status, void* cuda_stream);
 
 /* ---------------------------------------------------------------------------
  * Local head: the 17 sequential steps that turn one global hidden state into one

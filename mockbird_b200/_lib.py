@@ -104,6 +104,7 @@ SIGNATURES = {
     "mb_decoder_create": (ctypes.c_int, [_P, _I, _P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
     "mb_decoder_destroy": (ctypes.c_int, [_P]),
     "mb_decoder_step": (ctypes.c_int, [_P, _I, _P, _P, _P, _P]),
+    "mb_decoder_step_host": (ctypes.c_int, [_P, _I, _P, _P, _P, _P]),
     "mb_local_head_weight_count": (ctypes.c_size_t, [_P, ctypes.POINTER(MbLocalConfig)]),
     "mb_local_head_create": (ctypes.c_int, [_P, ctypes.POINTER(MbLocalConfig), _P, ctypes.c_size_t,
                                             ctypes.POINTER(ctypes.c_void_p)]),
@@ -112,6 +113,7 @@ SIGNATURES = {
     "mb_local_head_frame": (ctypes.c_int, [_P, _I, _P, _P, _P, _P, _P, _P]),
     "mb_local_head_frame_host": (ctypes.c_int, [_P, _I, _P, _P, _P, _P, _P]),
     "mb_argmax_penalty": (ctypes.c_int, [_I, _I, _P, _P, ctypes.c_float, _P, _P]),
+    "mb_gemm_bf16": (ctypes.c_int, [_I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "mb_append_attend_noalloc": (ctypes.c_int, [ctypes.POINTER(MbRingRef), _I, _I, _P, _P, _P, _P, _P]),
     "mb_ring_info_get": (ctypes.c_int, [_P, ctypes.POINTER(MbRingInfo)]),
     "mb_last_error": (ctypes.c_char_p, [_P]),

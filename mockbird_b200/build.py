@@ -18,13 +18,12 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libmockbird_kv.so")
 
-SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_decode_persist.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_decoder.cu", "mb_local.cu",
-           "mb_noalloc.cu"]
-HEADERS = ["mb_internal.cuh", "mb_ptx.cuh", "mb_decoder.cuh"]
+SOURCES = ["mb_api.cu", "mb_decode.cu", "mb_decode_persist.cu", "mb_prefill.cu", "mb_prefill_tc.cu", "mb_gemm.cu",
+           "mb_decoder.cu", "mb_local.cu", "mb_noalloc.cu"]
+HEADERS = ["mb_internal.cuh", "mb_ptx.cuh", "mb_decoder.cuh", "mb_gemm.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-# cuBLASLt: the plain GEMMs of the decoder step around the path
-LINK = ["-lcublasLt", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
+LINK = ["-Xlinker", "-rpath=/usr/local/cuda/lib64"]
 
 
 def nvcc() -> str:

@@ -76,7 +76,11 @@ int check_position(mb_ctx* c, int pos) {
     return MB_OK;
 }
 
-int check_items_host(mb_ctx* c, int n, const int32_t* streams, const int32_t* positions) {
+}  // namespace
+
+// Host-side checks of the items of a host-array call: stream range, no stream
+// twice, positions (decode.ts:719-724 for the non-wrapping ring).
+int mb::check_items_host(mb_ctx* c, int n, const int32_t* streams, const int32_t* positions) {
     std::vector<char> seen(c->cfg.streams, 0);
     for (int i = 0; i < n; i++) {
         const int s = streams[i];
@@ -89,6 +93,8 @@ int check_items_host(mb_ctx* c, int n, const int32_t* streams, const int32_t* po
     }
     return MB_OK;
 }
+
+namespace {
 
 // The decode launch of every context entry point: the per-chunk kernel
 // (mb_decode.cu), or -- when MOCKBIRD_DECODE_KERNEL=persistent and the call fits
@@ -316,8 +322,10 @@ MB_API int mb_decode_step(mb_ctx* c, int32_t n, const int32_t* streams, const in
     return MB_OK;
 }
 
+}  // extern "C"
+
 // The status of device rejection bits read back (clearing them on the device).
-static int report_bits(mb_ctx* c, int32_t bits) {
+int mb::report_bits(mb_ctx* c, int32_t bits) {
     if (!bits) return MB_OK;
     CK(cudaMemset(c->d_err, 0, sizeof(int32_t)), "clear device status");
     if (bits & DERR_TIMEOUT)
@@ -326,6 +334,8 @@ static int report_bits(mb_ctx* c, int32_t bits) {
                 (bits & DERR_POSITION) ? " position out of range" : "",
                 (bits & DERR_CAPACITY) ? " position beyond a non-wrapping ring" : "");
 }
+
+extern "C" {
 
 MB_API int mb_sync(mb_ctx* c, void* cuda_stream) {
     if (!c) return MB_ERR_ARG;

@@ -3,13 +3,15 @@
 // src/lib/tts/engine/decode.ts:474-620) for n streams at once, and the final
 // LayerNorm of globalStep (decode.ts:749-772).
 //
-// Per layer: LN1 -> QKV GEMM -> append + RoPE + attention (this library's decode
-// kernel) -> c_proj GEMM + residual -> LN2 -> fc_in GEMM -> GELU(tanh) -> fc_out
-// GEMM + residual.  The four GEMMs are plain library GEMMs (cuBLASLt, bf16
-// weights and activations, fp32 accumulation, bias and residual in the
-// epilogue: y = b + x W, W [K][N] row-major as the published graph stores it);
-// LayerNorm (LAYERNORM_1, kernels-decode.ts:168-200: eps 1e-5, two passes) and
-// GELU (GELU_TANH, kernels-decode.ts:373-390) are kernels here.
+// Per layer: LN1 -> QKV GEMM (+ bias) -> append + RoPE + attention (this
+// library's decode kernel) -> c_proj GEMM (+ bias + residual) -> LN2 -> fc_in
+// GEMM (+ bias, GELU(tanh), bf16 out) -> fc_out GEMM (+ bias + residual).  The
+// GEMMs are this library's tcgen05 kernels (mb_gemm.cu: bf16 weights and
+// activations, fp32 accumulation in TMEM, bias / residual / GELU in the
+// epilogue; y = b + x W with W [K][N] as the published graph stores it, held
+// transposed on the device); LayerNorm (LAYERNORM_1, kernels-decode.ts:168-200:
+// eps 1e-5, two passes) is a kernel here; GELU (GELU_TANH, :373-390) is fc_in's
+// epilogue.
 #include <stdlib.h>
 #include <string.h>
 
@@ -24,64 +26,45 @@ using bf16 = __nv_bfloat16;
 // One warp per row: mean, then the mean squared deviation (the two passes of
 // LAYERNORM_1), out = (x - mean) * rsqrt(var + 1e-5) * w + b (mb::dec::ln_load /
 // ln_apply).  In place is fine: the row is in registers before it is written.
+// Launched as a programmatic dependent of the GEMM before it: nothing global
+// is touched before that kernel has completed.
 template <typename TO, int PER>
 __global__ void layernorm_rows(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                                TO* __restrict__ y, int rows, int width) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     float v[PER];
     mb::dec::ln_load<PER>(x + (size_t)row * width, lane, v);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     mb::dec::ln_apply<TO, PER>(v, w, b, y + (size_t)row * width, width, lane);
 }
 
-// tanh on the MUFU unit (tanh.approx.f32, max relative error about 2^-11): the
-// result is rounded to bf16 (2^-8) right after, so the approximation is below
-// the output's own resolution.
-__device__ __forceinline__ float tanh_fast(float x) {
-    float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// GELU, tanh approximation (GELU_TANH), fp32 in -> bf16 out, 4 elements a thread
-// (n a multiple of 4, both pointers 16-byte aligned)
-__global__ void gelu_tanh_to_bf16(const float* __restrict__ x, bf16* __restrict__ y, size_t n) {
-    const size_t n4 = n / 4;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-        const float4 v = reinterpret_cast<const float4*>(x)[i];
-        float r[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const float a = r[k];
-            const float inner = 0.7978845608028654f * (a + 0.044715f * a * a * a);
-            r[k] = 0.5f * a * (1.f + tanh_fast(inner));
-        }
-        const __nv_bfloat162 lo = __floats2bfloat162_rn(r[0], r[1]), hi = __floats2bfloat162_rn(r[2], r[3]);
-        uint2 packed;
-        packed.x = *reinterpret_cast<const uint32_t*>(&lo);
-        packed.y = *reinterpret_cast<const uint32_t*>(&hi);
-        reinterpret_cast<uint2*>(y)[i] = packed;
-    }
-}
-
-__global__ void to_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y, size_t n) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        y[i] = __float2bfloat16_rn(x[i]);
+template <typename TO, int PER>
+cudaError_t layernorm_t(const float* x, const float* w, const float* b, TO* y, int rows, int width,
+                        cudaStream_t st) {
+    const int warps = 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows + warps - 1) / warps);
+    cfg.blockDim = dim3(32 * warps);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, layernorm_rows<TO, PER>, x, w, b, y, rows, width);
 }
 
 template <typename TO>
 cudaError_t layernorm(const float* x, const float* w, const float* b, TO* y, int rows, int width, cudaStream_t st) {
-    const int warps = 2, blocks = (rows + warps - 1) / warps;
     switch (width / 32) {  // width = heads * 64
-        case 2: layernorm_rows<TO, 2><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
-        case 8: layernorm_rows<TO, 8><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
-        case 24: layernorm_rows<TO, 24><<<blocks, 32 * warps, 0, st>>>(x, w, b, y, rows, width); break;
+        case 2: return layernorm_t<TO, 2>(x, w, b, y, rows, width, st);
+        case 8: return layernorm_t<TO, 8>(x, w, b, y, rows, width, st);
+        case 24: return layernorm_t<TO, 24>(x, w, b, y, rows, width, st);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
-
-constexpr int CVT_BLOCKS = 2 * 148;
 
 }  // namespace
 
@@ -101,61 +84,41 @@ uint16_t f32_to_bf16_bits(float f) {
     return (uint16_t)(u >> 16);
 }
 
-cudaError_t to_bf16(const float* x, bf16* y, size_t n, cudaStream_t st) {
-    to_bf16_kernel<<<CVT_BLOCKS, 256, 0, st>>>(x, y, n);
-    return cudaGetLastError();
+void transpose_to_bf16(const float* w, int K, int N, uint16_t* out) {
+    for (int k = 0; k < K; k++)
+        for (int n = 0; n < N; n++) out[(size_t)n * K + k] = f32_to_bf16_bits(w[(size_t)k * N + n]);
 }
 
-int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const float* bias, float* y,
-         bool accumulate, cudaStream_t st) {
-    // column-major view: y^T [N x M] = W^T [N x K] * x^T [K x M]
-    cublasStatus_t s = CUBLAS_STATUS_SUCCESS;
-    const bool has_bias = bias != nullptr;
-    const auto key = std::make_tuple(M, N, K, has_bias ? 1 : 0);
-    auto it = d->plans.find(key);
-    if (it == d->plans.end()) {
-        mb_decoder::Plan p;
-        cublasLtEpilogue_t epi = has_bias ? CUBLASLT_EPILOGUE_BIAS : CUBLASLT_EPILOGUE_DEFAULT;
-        cudaDataType_t bias_t = CUDA_R_32F;
-        s = cublasLtMatmulDescCreate(&p.op, CUBLAS_COMPUTE_32F, CUDA_R_32F);
-        if (s == CUBLAS_STATUS_SUCCESS)
-            s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof epi);
-        if (s == CUBLAS_STATUS_SUCCESS && has_bias)
-            s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bias_t, sizeof bias_t);
-        if (s == CUBLAS_STATUS_SUCCESS && has_bias)
-            s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
-        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.a, CUDA_R_16BF, N, K, N);
-        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.b, CUDA_R_16BF, K, M, K);
-        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatrixLayoutCreate(&p.c, CUDA_R_32F, N, M, N);
-        cublasLtMatmulPreference_t pref = nullptr;
-        if (s == CUBLAS_STATUS_SUCCESS) s = cublasLtMatmulPreferenceCreate(&pref);
-        if (s == CUBLAS_STATUS_SUCCESS)
-            s = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &d->ws_bytes,
-                                                     sizeof d->ws_bytes);
-        cublasLtMatmulHeuristicResult_t res = {};
-        int found = 0;
-        if (s == CUBLAS_STATUS_SUCCESS)
-            s = cublasLtMatmulAlgoGetHeuristic(d->lt, p.op, p.a, p.b, p.c, p.c, pref, 1, &res, &found);
-        if (pref) cublasLtMatmulPreferenceDestroy(pref);
-        if (s == CUBLAS_STATUS_SUCCESS && found == 0) s = CUBLAS_STATUS_NOT_SUPPORTED;
-        if (s != CUBLAS_STATUS_SUCCESS) {
-            if (p.c) cublasLtMatrixLayoutDestroy(p.c);
-            if (p.b) cublasLtMatrixLayoutDestroy(p.b);
-            if (p.a) cublasLtMatrixLayoutDestroy(p.a);
-            if (p.op) cublasLtMatmulDescDestroy(p.op);
-            return fail(d, MB_ERR_CUDA, std::string("cuBLASLt setup failed: ") + cublasLtGetStatusString(s));
-        }
-        p.algo = res.algo;
-        it = d->plans.emplace(key, p).first;
+namespace {
+const CUtensorMap* operand_map(mb_decoder* d, const void* base, int k, int rows, int box_rows) {
+    const auto key = std::make_tuple(base, k, rows, box_rows);
+    auto it = d->maps.find(key);
+    if (it == d->maps.end()) {
+        CUtensorMap m;
+        if (!mb::gemm::make_map(&m, base, k, rows, box_rows)) return nullptr;
+        it = d->maps.emplace(key, m).first;
     }
-    mb_decoder::Plan& p = it->second;
-    if (has_bias) s = cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
-    const float alpha = 1.f, beta = accumulate ? 1.f : 0.f;
-    if (s == CUBLAS_STATUS_SUCCESS)
-        s = cublasLtMatmul(d->lt, p.op, &alpha, W, p.a, x, p.b, &beta, y, p.c, y, p.c, &p.algo, d->workspace,
-                           d->ws_bytes, st);
-    if (s != CUBLAS_STATUS_SUCCESS)
-        return fail(d, MB_ERR_CUDA, std::string("cuBLASLt matmul failed: ") + cublasLtGetStatusString(s));
+    return &it->second;
+}
+}  // namespace
+
+int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, const float* bias, void* y, int ldy,
+         int epi, cudaStream_t st) {
+    const auto pkey = std::make_tuple(M, N, K, epi);
+    auto pit = d->gemm_plans.find(pkey);
+    if (pit == d->gemm_plans.end()) pit = d->gemm_plans.emplace(pkey, mb::gemm::choose(M, N, K, epi)).first;
+    const mb::gemm::Plan p = pit->second;
+    const CUtensorMap* ta = operand_map(d, x, K, d->ctx->cfg.max_batch, mb::gemm::BM);
+    const CUtensorMap* tb = operand_map(d, Wt, K, N, p.bn);
+    if (!ta || !tb) return fail(d, MB_ERR_CUDA, "decoder: GEMM tensor map encoding failed");
+    mb::gemm::Args a;
+    a.M = M, a.N = N, a.K = K, a.splits = p.splits;
+    a.bias = bias, a.y = y, a.ldy = ldy;
+    a.err = d->ctx->d_err;
+    // a programmatic dependent of the kernel before it (the GEMM loads its first
+    // weight tiles while that kernel finishes)
+    const cudaError_t e = mb::gemm::launch(*ta, *tb, a, p, epi, st, true);
+    if (e != cudaSuccess) return fail(d, MB_ERR_CUDA, std::string("decoder GEMM: ") + cudaGetErrorString(e));
     return MB_OK;
 }
 
@@ -169,16 +132,15 @@ int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, 
         const auto& W = d->L[l];
         if (!(l == 0 && ln1_ready) && (e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess)
             break;
-        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, false, st))) break;
+        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, 3 * h, mb::gemm::EPI_STORE, st))) break;
         // the context rows go straight to the bf16 input of the c_proj GEMM
         if ((e = mb::launch_decode(c->cfg.dtype, true, mb::ring_view(c, l), c->scratch, n, streams, positions, d->qkv,
                                    3 * h, d->xb, st, false, true)) != cudaSuccess)
             break;
-        if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, true, st))) break;
+        if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, h, mb::gemm::EPI_ACCUM, st))) break;
         if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, d->xb, n, h, st)) != cudaSuccess) break;
-        if ((rc = gemm(d, n, f, h, d->xb, W.w_in, W.b_in, d->h1, false, st))) break;
-        gelu_tanh_to_bf16<<<CVT_BLOCKS, 256, 0, st>>>(d->h1, d->xb, (size_t)n * f);
-        if ((rc = gemm(d, n, h, f, d->xb, W.w_out, W.b_out, hidden, true, st))) break;
+        if ((rc = gemm(d, n, f, h, d->xb, W.w_in, W.b_in, d->h1, f, mb::gemm::EPI_GELU_BF16, st))) break;
+        if ((rc = gemm(d, n, h, f, d->h1, W.w_out, W.b_out, hidden, h, mb::gemm::EPI_ACCUM, st))) break;
         e = cudaGetLastError();
     }
     if (rc == MB_OK && e == cudaSuccess)
@@ -208,16 +170,9 @@ MB_API int mb_decoder_destroy(mb_decoder* d) {
     cudaSetDevice(d->ctx->cfg.device);
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
     if (d->cap) cudaStreamDestroy(d->cap);
-    void* ptrs[] = {d->wmem, d->xb, d->qkv, d->h1, d->workspace, d->g_streams, d->g_positions, d->g_hidden};
+    void* ptrs[] = {d->wmem, d->xb, d->qkv, d->h1, d->g_streams, d->g_positions, d->g_hidden};
     for (void* p : ptrs)
         if (p) cudaFree(p);
-    for (auto& kv : d->plans) {
-        cublasLtMatrixLayoutDestroy(kv.second.c);
-        cublasLtMatrixLayoutDestroy(kv.second.b);
-        cublasLtMatrixLayoutDestroy(kv.second.a);
-        cublasLtMatmulDescDestroy(kv.second.op);
-    }
-    if (d->lt) cublasLtDestroy(d->lt);
     if (prev >= 0) cudaSetDevice(prev);
     delete d;
     return MB_OK;
@@ -250,36 +205,36 @@ MB_API int mb_decoder_create(mb_ctx* c, int32_t ffn, const float* w, size_t coun
         return rc;
     };
     // device image: fp32 vectors first, then bf16 matrices (each block 256-byte aligned)
+    // (a matrix [K][N] is stored transposed, W^T [N][K]: the GEMM's K-major B operand)
     struct Blk {
         size_t src, n;
-        bool mat;
+        int K, N;  // K > 0: a matrix
         size_t dst;
     };
     std::vector<Blk> blks;
     size_t src = 0;
-    auto add = [&](size_t n, bool mat) {
-        blks.push_back({src, n, mat, 0});
+    auto add = [&](size_t n, int K = 0, int N = 0) {
+        blks.push_back({src, n, K, N, 0});
         src += n;
     };
     for (int l = 0; l < d->layers; l++) {
-        add(h, false), add(h, false);                    // ln1
-        add((size_t)h * 3 * h, true), add(3 * h, false);  // c_attn
-        add((size_t)h * h, true), add(h, false);          // c_proj
-        add(h, false), add(h, false);                    // ln2
-        add((size_t)h * ffn, true), add(ffn, false);      // fc_in
-        add((size_t)ffn * h, true), add(h, false);        // fc_out
+        add(h), add(h);                                // ln1
+        add((size_t)h * 3 * h, h, 3 * h), add(3 * h);  // c_attn
+        add((size_t)h * h, h, h), add(h);              // c_proj
+        add(h), add(h);                                // ln2
+        add((size_t)h * ffn, h, ffn), add(ffn);        // fc_in
+        add((size_t)ffn * h, ffn, h), add(h);          // fc_out
     }
-    add(h, false), add(h, false);  // ln_f
+    add(h), add(h);  // ln_f
     size_t bytes = 0;
     for (auto& b : blks) {
         b.dst = bytes;
-        bytes += ((b.n * (b.mat ? 2 : 4)) + 255) & ~size_t(255);
+        bytes += ((b.n * (b.K ? 2 : 4)) + 255) & ~size_t(255);
     }
     std::vector<unsigned char> img(bytes, 0);
     for (auto& b : blks) {
-        if (b.mat) {
-            uint16_t* o = reinterpret_cast<uint16_t*>(img.data() + b.dst);
-            for (size_t i = 0; i < b.n; i++) o[i] = mb::dec::f32_to_bf16_bits(w[b.src + i]);
+        if (b.K) {
+            mb::dec::transpose_to_bf16(w + b.src, b.K, b.N, reinterpret_cast<uint16_t*>(img.data() + b.dst));
         } else {
             memcpy(img.data() + b.dst, w + b.src, b.n * 4);
         }
@@ -296,15 +251,13 @@ MB_API int mb_decoder_create(mb_ctx* c, int32_t ffn, const float* w, size_t coun
     }
     d->lnf_w = F(blks.size() - 2);
     d->lnf_b = F(blks.size() - 1);
-    const size_t mb = c->cfg.max_batch, wide = (size_t)(ffn > h ? ffn : h);
-    if (cudaMalloc(&d->xb, mb * wide * sizeof(bf16)) != cudaSuccess ||
+    const size_t mb = c->cfg.max_batch;
+    if (cudaMalloc(&d->xb, mb * h * sizeof(bf16)) != cudaSuccess ||
         cudaMalloc(&d->qkv, mb * 3 * h * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&d->h1, mb * ffn * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&d->workspace, d->ws_bytes) != cudaSuccess || cudaMalloc(&d->g_streams, mb * 4) != cudaSuccess ||
+        cudaMalloc(&d->h1, mb * ffn * sizeof(bf16)) != cudaSuccess || cudaMalloc(&d->g_streams, mb * 4) != cudaSuccess ||
         cudaMalloc(&d->g_positions, mb * 4) != cudaSuccess ||
         cudaMalloc(&d->g_hidden, mb * h * sizeof(float)) != cudaSuccess)
         return bail(MB_ERR_OOM, "decoder: activation allocation failed");
-    if (cublasLtCreate(&d->lt) != CUBLAS_STATUS_SUCCESS) return bail(MB_ERR_CUDA, "decoder: cublasLtCreate failed");
     if (cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) != cudaSuccess)
         return bail(MB_ERR_CUDA, "decoder: stream creation failed");
     {
@@ -316,6 +269,56 @@ MB_API int mb_decoder_create(mb_ctx* c, int32_t ffn, const float* w, size_t coun
     return MB_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// One step over the staged inputs (d->g_streams, d->g_positions, d->g_hidden) on
+// `st`: a replay of the step captured for this item count, or -- the first step
+// of a count, or with graphs off -- the launches themselves (so kernel modules
+// are loaded and tensor maps built outside any capture), after which the step is
+// captured, without running, for the next calls.
+int step_staged(mb_decoder* d, int n, cudaStream_t st) {
+    if (!d->use_graph) return mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st);
+    auto it = d->graphs.find(n);
+    cudaError_t e;
+    if (it != d->graphs.end()) {
+        e = cudaGraphLaunch(it->second, st);
+        return e == cudaSuccess ? MB_OK : mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder graph: ") + cudaGetErrorString(e));
+    }
+    int rc = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st);
+    if (rc) return rc;
+    cudaGraph_t g = nullptr;
+    if ((e = cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+        return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
+    const int rc2 = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, d->cap);
+    e = cudaStreamEndCapture(d->cap, &g);
+    cudaGraphExec_t ex = nullptr;
+    if (rc2 == MB_OK && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (rc2 != MB_OK) return rc2;
+    if (e != cudaSuccess) return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
+    d->graphs.emplace(n, ex);
+    return MB_OK;
+}
+
+struct DevGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DevGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DevGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
 MB_API int mb_decoder_step(mb_decoder* d, int32_t n, const int32_t* streams, const int32_t* positions,
                            float* hidden, void* cuda_stream) {
     if (!d) return MB_ERR_ARG;
@@ -324,51 +327,54 @@ MB_API int mb_decoder_step(mb_decoder* d, int32_t n, const int32_t* streams, con
     if (n == 0) return MB_OK;
     if (!streams || !positions || !hidden || (reinterpret_cast<uintptr_t>(hidden) & 15))
         return mb::dec::fail(d, MB_ERR_ARG, "decoder: null or misaligned device pointer");
-    int prev = -1;
-    cudaGetDevice(&prev);
-    if (prev != c->cfg.device && cudaSetDevice(c->cfg.device) != cudaSuccess) return MB_ERR_CUDA;
+    DevGuard g(c->cfg.device);
+    if (!g.ok) return MB_ERR_CUDA;
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    int rc = MB_OK;
-    if (!d->use_graph) {
-        rc = mb::dec::run(d, n, streams, positions, hidden, nullptr, st);
-    } else {
-        // One captured step per item count, over inputs staged into this object's
-        // buffers; the first step of a count runs directly (kernel modules loaded,
-        // GEMM plans built outside any capture) and is then captured for the next.
-        const size_t hb = (size_t)n * d->hid * sizeof(float);
-        cudaError_t e = cudaMemcpyAsync(d->g_streams, streams, n * 4, cudaMemcpyDeviceToDevice, st);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_positions, positions, n * 4, cudaMemcpyDeviceToDevice, st);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_hidden, hidden, hb, cudaMemcpyDeviceToDevice, st);
-        auto it = d->graphs.find(n);
-        if (e != cudaSuccess) {
-            rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder inputs: ") + cudaGetErrorString(e));
-        } else if (it != d->graphs.end()) {
-            e = cudaGraphLaunch(it->second, st);
-            if (e != cudaSuccess) rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder graph: ") + cudaGetErrorString(e));
-        } else {
-            rc = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st);
-            cudaGraph_t g = nullptr;
-            if (rc == MB_OK && (e = cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
-                rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
-            if (rc == MB_OK) {
-                const int rc2 = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, d->cap);
-                e = cudaStreamEndCapture(d->cap, &g);
-                cudaGraphExec_t ex = nullptr;
-                if (rc2 == MB_OK && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
-                if (g) cudaGraphDestroy(g);
-                if (rc2 != MB_OK)
-                    rc = rc2;
-                else if (e != cudaSuccess)
-                    rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
-                else
-                    d->graphs.emplace(n, ex);
-            }
-        }
-        if (rc == MB_OK && (e = cudaMemcpyAsync(hidden, d->g_hidden, hb, cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
-            rc = mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder output: ") + cudaGetErrorString(e));
+    if (!d->use_graph) return mb::dec::run(d, n, streams, positions, hidden, nullptr, st);
+    // the captured step reads and writes this object's own buffers only
+    const size_t hb = (size_t)n * d->hid * sizeof(float);
+    cudaError_t e = cudaMemcpyAsync(d->g_streams, streams, n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_positions, positions, n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_hidden, hidden, hb, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder inputs: ") + cudaGetErrorString(e));
+    const int rc = step_staged(d, n, st);
+    if (rc) return rc;
+    if ((e = cudaMemcpyAsync(hidden, d->g_hidden, hb, cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+        return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder output: ") + cudaGetErrorString(e));
+    return MB_OK;
+}
+
+MB_API int mb_decoder_step_host(mb_decoder* d, int32_t n, const int32_t* streams, const int32_t* positions,
+                                float* hidden, void* cuda_stream) {
+    if (!d) return MB_ERR_ARG;
+    mb_ctx* c = d->ctx;
+    if (n < 0 || n > c->cfg.max_batch) return mb::dec::fail(d, MB_ERR_ARG, "decoder: item count out of range");
+    if (n == 0) return MB_OK;
+    if (!streams || !positions || !hidden) return mb::dec::fail(d, MB_ERR_ARG, "decoder: null host pointer");
+    int rc = mb::check_items_host(c, n, streams, positions);
+    if (rc) return rc;
+    DevGuard g(c->cfg.device);
+    if (!g.ok) return MB_ERR_CUDA;
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    // A previous call that failed after queueing its copies may have left them
+    // reading the staging; nothing is reused before they are done.
+    cudaError_t e = cudaEventSynchronize(c->ev_ids);
+    if (e == cudaSuccess) {
+        memcpy(c->h_ids, streams, n * sizeof(int32_t));
+        memcpy(c->h_ids + n, positions, n * sizeof(int32_t));
+        e = cudaMemcpyAsync(d->g_streams, c->h_ids, n * 4, cudaMemcpyHostToDevice, st);
     }
-    if (prev >= 0 && prev != c->cfg.device) cudaSetDevice(prev);
-    return rc;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_positions, c->h_ids + n, n * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaEventRecord(c->ev_ids, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->g_hidden, hidden, (size_t)n * d->hid * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder inputs: ") + cudaGetErrorString(e));
+    if ((rc = step_staged(d, n, st))) return rc;
+    // ln_f of the last layer and the ring's device status word, then one wait
+    e = cudaMemcpyAsync(hidden, d->g_hidden, (size_t)n * d->hid * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder outputs: ") + cudaGetErrorString(e));
+    return mb::report_bits(c, *c->h_err);
 }
 
 }  // extern "C"

@@ -1,16 +1,16 @@
 // The transformer-layer machinery shared by the global decode step
 // (mb_decoder.cu) and the local 17-step head (mb_local.cu): weights on the
-// device, cuBLASLt GEMM plans, and the per-layer sequence of DecodeRunner.runLayer
-// (liyu1981/mockbird, src/lib/tts/engine/decode.ts:474-620).
+// device, the tensor maps of this library's tcgen05 GEMMs (mb_gemm.cu), and the
+// per-layer sequence of DecodeRunner.runLayer (liyu1981/mockbird,
+// src/lib/tts/engine/decode.ts:474-620).
 #pragma once
-
-#include <cublasLt.h>
 
 #include <map>
 #include <string>
 #include <tuple>
 #include <vector>
 
+#include "mb_gemm.cuh"
 #include "mb_internal.cuh"
 
 struct mb_decoder {
@@ -19,23 +19,18 @@ struct mb_decoder {
     int hid = 0, ffn = 0, layers = 0;
     struct Layer {
         const float *ln1_w, *ln1_b, *b_attn, *b_proj, *ln2_w, *ln2_b, *b_in, *b_out;
-        const bf16 *w_attn, *w_proj, *w_in, *w_out;
+        const bf16 *w_attn, *w_proj, *w_in, *w_out;  // transposed: W^T [N][K], K-major
     };
     std::vector<Layer> L;
     const float *lnf_w = nullptr, *lnf_b = nullptr;
     void* wmem = nullptr;      // all weights, one allocation
-    bf16* xb = nullptr;        // [max_batch][max(hid, ffn)] GEMM input
+    bf16* xb = nullptr;        // [max_batch][hid] GEMM input (LayerNorm output, context rows)
     float* qkv = nullptr;      // [max_batch][3*hid]
-    float* h1 = nullptr;       // [max_batch][ffn]
-    cublasLtHandle_t lt = nullptr;
-    void* workspace = nullptr;
-    size_t ws_bytes = 32u << 20;
-    struct Plan {  // one GEMM shape: descriptors and the chosen algorithm, built once
-        cublasLtMatmulDesc_t op = nullptr;
-        cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
-        cublasLtMatmulAlgo_t algo{};
-    };
-    std::map<std::tuple<int, int, int, int>, Plan> plans;  // (M, N, K, has bias)
+    bf16* h1 = nullptr;        // [max_batch][ffn] GELU(fc_in) output, fc_out's input
+    // tensor maps of the GEMM operands, built once per (base, k, rows, box rows),
+    // and the GEMM plans, once per (M, N, K, epilogue)
+    std::map<std::tuple<const void*, int, int, int>, CUtensorMap> maps;
+    std::map<std::tuple<int, int, int, int>, mb::gemm::Plan> gemm_plans;
     // mb_decoder_step replays one captured step per item count over staged inputs
     bool use_graph = true;
     cudaStream_t cap = nullptr;
@@ -55,10 +50,17 @@ int fail(mb_decoder* d, int code, const std::string& msg);
 // fp32 -> bf16 bits, round to nearest even (NaN stays NaN).
 uint16_t f32_to_bf16_bits(float f);
 
-// y[M][N] (fp32, row-major) = x[M][K] (bf16) * W[K][N] (bf16) (+ bias[N] when
-// non-null) (+ y when accumulate).  cuBLASLt, fp32 accumulation.
-int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* W, const float* bias, float* y,
-         bool accumulate, cudaStream_t st);
+// y = x[M][K] (bf16, rows K apart) * W (given transposed, Wt [N][K] bf16) with
+// fp32 accumulation on the tensor cores (mb_gemm.cu), then the epilogue `epi`
+// (mb::gemm::Epi) with bias[N] when non-null: y fp32 [M][ldy] (store or +=), or
+// bf16 [M][ldy] after GELU(tanh).  x and Wt must be buffers whose tensor maps
+// this decoder may cache: x one of its own activation buffers (max_batch rows),
+// Wt a weight matrix it owns.
+int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, const float* bias, void* y, int ldy,
+         int epi, cudaStream_t st);
+
+// W [K][N] fp32 (host, row-major) -> W^T [N][K] as bf16 bits, the layout the GEMM reads.
+void transpose_to_bf16(const float* w, int K, int N, uint16_t* out);
 
 // The layers of mb_decoder_step on `hidden` [n][hid], then ln_f: into `lnf_bf16`
 // [n][hid] (bf16) when it is non-null, else into `hidden` in place (fp32).
@@ -147,8 +149,6 @@ __device__ __forceinline__ void ln_apply(const float (&v)[PER], const float* __r
     }
 }
 
-// y = bf16(x), n elements.
-cudaError_t to_bf16(const float* x, bf16* y, size_t n, cudaStream_t st);
 
 }  // namespace dec
 }  // namespace mb

@@ -1,0 +1,56 @@
+// Batched-stream GEMMs of the decode step on the 5th-generation tensor cores
+// (mb_gemm.cu): y = x W (+ bias) with one activation row per stream.  They
+// replace the GEMV dispatches of DecodeRunner.runLayer (liyu1981/mockbird,
+// src/lib/tts/engine/decode.ts:517-526 QKV, :553-619 c_proj, fc_in, fc_out;
+// GEMV, kernels-decode.ts:127-142: y = b + x W, W [K][N] row-major) and the
+// audio-head GEMV of nextFrame (decode.ts:788-939), for all streams at once.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mb {
+namespace gemm {
+
+// What the epilogue does with acc = x W (fp32) of each output element.
+enum Epi : int {
+    EPI_STORE = 0,      // y (fp32)  = acc + bias
+    EPI_ACCUM = 1,      // y (fp32) += acc + bias      (the residual add of c_proj / fc_out)
+    EPI_GELU_BF16 = 2,  // y (bf16)  = gelu_tanh(acc + bias)   (fc_in, GELU_TANH)
+};
+
+constexpr int BM = 128;  // rows (streams) per tile: the UMMA M, one TMEM lane per row
+constexpr int BK = 64;   // K per stage: one 128-byte swizzle row of bf16
+
+// Tile width and split of K for one GEMM shape, chosen on the host: the fewest
+// bytes per CTA (its operand tiles, plus the partial tiles it reads from the
+// other CTAs of its cluster) with all CTAs resident in one wave.
+struct Plan {
+    int bn;      // 32, 64 or 128 output columns per CTA
+    int splits;  // K split over this many CTAs of one thread-block cluster (1..8)
+};
+Plan choose(int M, int N, int K, int epi);
+
+struct Args {
+    int M, N, K;           // K a multiple of 64, N a multiple of the plan's bn
+    int splits;
+    const float* bias;     // [N] or null
+    void* y;               // fp32 [M][ldy] (EPI_STORE / EPI_ACCUM) or bf16 [M][ldy] (EPI_GELU_BF16)
+    int ldy;
+    int* err;              // device status word: DERR_TIMEOUT is OR-ed in when a bounded wait gives up
+};
+
+// 2-D tensor map of a K-major bf16 matrix [rows][k] (rows k*2 bytes apart, 16-byte
+// aligned base): box 64 x box_rows, 128-byte swizzle, zero fill past the last row.
+bool make_map(CUtensorMap* m, const void* base, int k, int rows, int box_rows);
+
+// ta: x [M][K] bf16 (box rows 128); tb: W^T [N][K] bf16 (box rows plan.bn).
+// pdl: launch as a programmatic dependent of the previous kernel on `st` (the
+// kernel waits for it before its first read of x or access of y).
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, const Plan& p, int epi,
+                   cudaStream_t st, bool pdl);
+
+}  // namespace gemm
+}  // namespace mb

@@ -125,4 +125,10 @@ cudaError_t launch_ring_write(int dtype, const RingView& r, int stream, int firs
                               const void* v, cudaStream_t st);
 cudaError_t launch_reset(const mb_ctx* c, int stream, cudaStream_t st);
 
+// host-array entry points (mb_api.cu): checks of the items on the host, and the
+// status of the device rejection bits a call read back (cleared on the device;
+// the message goes to the context's last error)
+int check_items_host(mb_ctx* c, int n, const int32_t* streams, const int32_t* positions);
+int report_bits(mb_ctx* c, int32_t bits);
+
 }  // namespace mb

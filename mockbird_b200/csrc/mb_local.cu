@@ -15,11 +15,11 @@
 // per-channel 1024-bit seen mask kept on the device.  Tokens never leave the
 // device between steps.
 //
-// The layer is the decoder machinery of mb_decoder.cu (cuBLASLt GEMMs with bf16
-// weights and fp32 accumulation, this library's LayerNorm, GELU and fused
-// append + RoPE + attention kernels).  The 16 audio heads [768][1024] are bf16
-// GEMMs without bias (the graph's bare MatMul, decode.ts:875); the embeddings,
-// the two text-head columns and everything between the GEMMs stay fp32.
+// The layer is the decoder machinery of mb_decoder.cu (this library's tcgen05
+// GEMMs with bf16 weights and fp32 accumulation, its LayerNorm and fused append +
+// RoPE + attention kernels).  The 16 audio heads [768][1024] are bf16 GEMMs
+// without bias (the graph's bare MatMul, decode.ts:875); the embeddings, the two
+// text-head columns and everything between the GEMMs stay fp32.
 //
 // One frame is ~220 launches of small kernels, so by default it is captured once
 // per batch size into a CUDA graph and replayed (MOCKBIRD_LOCAL_GRAPH=0 turns
@@ -224,7 +224,7 @@ struct mb_local_head {
     float penalty = 1.f;
     void* wmem = nullptr;        // wte_slot [h] | cols [2][h] | emb [(channels-1)][codes][h] (fp32) | heads (bf16)
     const float *wte_slot = nullptr, *cols = nullptr, *emb = nullptr;
-    const bf16* heads = nullptr; // [channels][h][codes]
+    const bf16* heads = nullptr; // [channels][codes][h]: each audio head transposed (the GEMM's K-major operand)
     float* hin = nullptr;        // [max_batch][h] staged global hidden states
     float* x = nullptr;          // [max_batch][h] the step's residual stream
     bf16* hb = nullptr;          // [max_batch][h] ln_f output, head GEMM input
@@ -286,7 +286,7 @@ int enqueue_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
         } else {
             const int ch = step - 1;
             rc = mb::dec::gemm(lh->dec, n, lh->codes, h, lh->hb, lh->heads + (size_t)ch * h * lh->codes, nullptr,
-                               lh->lg, false, st);
+                               lh->lg, lh->codes, mb::gemm::EPI_STORE, st);
             if (rc) return rc;
             // steps before the last also embed the chosen tokens for the next step
             const EmbedNext next{lh->emb, lh->dec->L[0].ln1_w, lh->dec->L[0].ln1_b, lh->x, lh->dec->xb, h};
@@ -432,7 +432,9 @@ MB_API int mb_local_head_create(mb_ctx* c, const mb_local_config* cfg, const flo
     std::vector<unsigned char> img(bytes, 0);
     memcpy(img.data(), w + nd, n_f32 * 4);
     uint16_t* hb16 = reinterpret_cast<uint16_t*>(img.data() + f32_bytes);
-    for (size_t i = 0; i < n_heads; i++) hb16[i] = mb::dec::f32_to_bf16_bits(w[nd + n_f32 + i]);
+    for (size_t c2 = 0; c2 < ch; c2++)  // each head [h][codes] stored transposed, [codes][h]
+        mb::dec::transpose_to_bf16(w + nd + n_f32 + c2 * h * codes, (int)h, (int)codes, hb16 + c2 * h * codes);
+
     if (cudaMalloc(&lh->wmem, bytes) != cudaSuccess) return bail(MB_ERR_OOM, "local head: weight allocation failed");
     if (cudaMemcpy(lh->wmem, img.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess)
         return bail(MB_ERR_CUDA, "local head: weight upload failed");

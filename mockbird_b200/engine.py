@@ -304,6 +304,21 @@ class Decoder:
             raise MockbirdError(rc, self.lib.mb_last_error(self.ring.ctx).decode())
         return hidden
 
+    def step_host(self, streams, positions, hidden, stream=None):
+        """One step on host arrays, as DecodeRunner.globalStep (decode.ts:712-775)
+        writes the embedded row and reads back ln_f: hidden [n][H*64] fp32 (numpy
+        or a CPU tensor, ideally pinned) is updated in place; blocks until done."""
+        s = np.ascontiguousarray(streams, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        if len(p) != len(s):
+            raise ValueError("streams and positions differ in length")
+        _host_array("hidden", hidden, (len(s), self.ring.hidden), "float32")
+        rc = self.lib.mb_decoder_step_host(self.handle, len(s), _ptr(s), _ptr(p), _ptr(hidden),
+                                           self.ring._stream(stream))
+        if rc:
+            raise MockbirdError(rc, self.lib.mb_last_error(self.ring.ctx).decode())
+        return hidden
+
     def dispose(self) -> None:
         if getattr(self, "handle", None):
             self.lib.mb_decoder_destroy(self.handle)

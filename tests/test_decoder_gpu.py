@@ -56,3 +56,48 @@ def test_decoder_rejects_bad_weights():
     dec = Decoder(ring, _weights(1, 768, 1024, 0), 1024)
     with pytest.raises(MockbirdError):
         dec.step([0, 1, 0], [0, 0, 0], torch.zeros(3, 768, device=DEV))  # 3 items > max_batch 2
+
+
+def test_decoder_step_host_matches_device_step():
+    """mb_decoder_step_host (host rows in, ln_f rows out, one synchronisation: the
+    call globalStep makes) equals mb_decoder_step on device arrays bit for bit,
+    step after step, over rings that start equal -- the first step of the batch
+    size runs directly, the later ones replay the captured step."""
+    h, S, C, layers, ffn = 768, 6, 128, 2, 1024
+    w = _weights(layers, h, ffn, seed=9)
+    ra = KvRing(layers=layers, streams=S, capacity=C, dtype="bf16", wrap=True)
+    rb = KvRing(layers=layers, streams=S, capacity=C, dtype="bf16", wrap=True)
+    da, db = Decoder(ra, w, ffn), Decoder(rb, w, ffn)
+    rng = np.random.default_rng(11)
+    order = [5, 0, 3, 1]
+    pinned = torch.empty(len(order), h).pin_memory()
+    for step in range(6):
+        x = rng.standard_normal((len(order), h)).astype(np.float32)
+        pos = [step + 3 * i for i in range(len(order))]
+        dev = db.step(order, pos, torch.from_numpy(x).to(DEV)).cpu().numpy()
+        if step % 2:  # a pinned tensor and a plain numpy array both work
+            pinned.copy_(torch.from_numpy(x))
+            host = da.step_host(order, pos, pinned).numpy()
+        else:
+            host = da.step_host(order, pos, x.copy())
+        assert np.array_equal(host, dev), step
+    ra.sync()
+    rb.sync()
+
+
+def test_decoder_step_host_checks_items_on_the_host():
+    ring = KvRing(layers=1, streams=3, capacity=64, dtype="bf16", wrap=True)
+    dec = Decoder(ring, _weights(1, 768, 1024, 0), 1024)
+    x = np.zeros((2, 768), np.float32)
+    with pytest.raises(MockbirdError, match="twice"):
+        dec.step_host([1, 1], [0, 0], x)
+    with pytest.raises(MockbirdError, match="out of range"):
+        dec.step_host([0, 3], [0, 0], x)
+    with pytest.raises(MockbirdError, match="position"):
+        dec.step_host([0, 1], [0, -1], x)
+    with pytest.raises(TypeError):
+        dec.step_host([0, 1], [0, 0], np.zeros((2, 700), np.float32))
+    # the context still works after the rejections
+    out = dec.step_host([0, 1], [0, 0], np.ones((2, 768), np.float32))
+    assert np.isfinite(out).all()
+    ring.sync()
