@@ -176,6 +176,17 @@ MB_API int mb_ring_write(mb_ctx* ctx, int32_t layer, int32_t stream, int32_t fir
 /* Wait for `cuda_stream` and report device-side rejections (then clear them). */
 MB_API int mb_sync(mb_ctx* ctx, void* cuda_stream);
 
+/* Failure detection.  No counterpart in the reference, whose WebGPU queue has no
+ * timeouts (its warm-up checks, gpu.ts:201-234, only catch wrong results).  The
+ * decode kernels of this context wait for their K/V chunks at most `cycles` SM
+ * clock cycles (0 restores the default, about 2 s); a wait that runs out skips
+ * the chunk, lets its copies land (at the default bound), and the next mb_sync
+ * reports MB_ERR_TIMEOUT.  A negative value is the test of that path: the waits
+ * then target a barrier that nothing signals and run out after -cycles cycles,
+ * on every launch, until the bound is set again.  Applies to launches queued
+ * after the call. */
+MB_API int mb_set_wait_limit(mb_ctx* ctx, int64_t cycles);
+
 /* ---------------------------------------------------------------------------
  * The decode step around the path: the whole global
  * transformer layer of DecodeRunner.runLayer (decode.ts:474-620) for n streams

@@ -105,6 +105,7 @@ SIGNATURES = {
     "mb_decoder_destroy": (ctypes.c_int, [_P]),
     "mb_decoder_step": (ctypes.c_int, [_P, _I, _P, _P, _P, _P]),
     "mb_decoder_step_host": (ctypes.c_int, [_P, _I, _P, _P, _P, _P]),
+    "mb_set_wait_limit": (ctypes.c_int, [_P, ctypes.c_int64]),
     "mb_local_head_weight_count": (ctypes.c_size_t, [_P, ctypes.POINTER(MbLocalConfig)]),
     "mb_local_head_create": (ctypes.c_int, [_P, ctypes.POINTER(MbLocalConfig), _P, ctypes.c_size_t,
                                             ctypes.POINTER(ctypes.c_void_p)]),

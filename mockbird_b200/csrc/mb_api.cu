@@ -537,6 +537,13 @@ MB_API int mb_ring_write(mb_ctx* c, int32_t layer, int32_t stream, int32_t first
     return MB_OK;
 }
 
+MB_API int mb_set_wait_limit(mb_ctx* c, int64_t cycles) {
+    if (!c) return MB_ERR_ARG;
+    c->wait_probe = cycles < 0;
+    c->wait_limit = cycles > 0 ? cycles : cycles < 0 ? -cycles : mb::WAIT_LIMIT;
+    return MB_OK;
+}
+
 MB_API int mb_ring_info_get(const mb_ctx* c, mb_ring_info* out) {
     if (!c || !out) return MB_ERR_ARG;
     out->kv = c->kv;

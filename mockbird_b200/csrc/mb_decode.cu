@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     __shared__ float ps[ROWS];
     __shared__ float red[4][HD];
     __shared__ float wmax[4], wsum[4];
-    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ __align__(8) uint64_t bar[3];  // K chunk, V chunk, and one nothing signals (wait probe)
     __shared__ int ticket;
 
     const int c = blockIdx.x, h = blockIdx.y, item = blockIdx.z, tid = threadIdx.x;
@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     if (tid == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
+        mbar_init(&bar[2], 1);
         fence_mbar_init();
         const uint32_t bytes = (uint32_t)(has_new ? rows - 1 : rows) * RB;
         const int a = has_new ? jn : rows;          // first segment [0, a)
@@ -239,7 +240,9 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
 
     // ---- K chunk landed?  Each thread waits for itself (bounded; a copy that
     // never lands reads as an empty chunk, and the CTA agrees on that below)
-    bool ok = mbar_wait(&bar[0], 0, WAIT_LIMIT);
+    // (with the wait probe on, this wait and the V chunk's target the barrier
+    // nothing signals, so they run out after r.wait_limit cycles)
+    bool ok = mbar_wait(&bar[r.wait_probe ? 2 : 0], 0, r.wait_limit);
     if (!ok) live = false;
 
     // ---- scores: slot rr, 128 bytes per thread, 16-byte vectors read in a
@@ -286,9 +289,15 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     if (lane == 0) wsum[warp] = l;
 
     // ---- V chunk (this barrier also publishes ps and wsum)
-    const bool okv = __syncthreads_and(mbar_wait(&bar[1], 0, WAIT_LIMIT));
+    const bool okv = __syncthreads_and(mbar_wait(&bar[r.wait_probe ? 2 : 1], 0, r.wait_limit));
     if (ok && !okv && tid == 0) atomicOr(r.err, DERR_TIMEOUT);
     ok = ok && okv;
+    // A CTA that gave up still lets both of its copies land (at the default
+    // bound) before it can exit, so none writes into a released CTA.
+    if (!ok && tid == 0) {
+        mbar_wait(&bar[0], 0, WAIT_LIMIT);
+        mbar_wait(&bar[1], 0, WAIT_LIMIT);
+    }
     l = wsum[0] + wsum[1] + wsum[2] + wsum[3];
 
     // ---- P.V: warp w takes slots w, w+4, ...; lane owns dims 2*lane, 2*lane+1

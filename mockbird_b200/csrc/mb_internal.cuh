@@ -16,6 +16,9 @@ namespace mb {
 constexpr int HD = 64;                  // head dim (kernels-decode.ts: 64 lanes per head)
 constexpr float SCALE = 0.125f;         // literal attention scale (docs analysis :846)
 constexpr float LOG2E = 1.4426950408889634f;
+// Bound of every device-side wait, in SM clock cycles (~2 s at 1.9 GHz; a bulk
+// copy takes microseconds): a wait that runs out flags DERR_TIMEOUT.
+constexpr long long WAIT_LIMIT = 4000000000LL;
 
 // device-side rejection bits, reported by mb_sync
 enum : int32_t {
@@ -32,6 +35,8 @@ struct RingView {
     const float2* rope;   // [max_position][32] (cos, sin)
     int32_t* err;         // device rejection bits
     int32_t streams, heads, capacity, wrap, max_position;
+    long long wait_limit; // bound of the decode kernel's waits for its K/V chunk (cycles)
+    int32_t wait_probe;   // 1: those waits target a barrier nothing signals (they run out; tests)
 };
 
 struct Scratch {
@@ -65,6 +70,8 @@ struct mb_ctx {
     cudaEvent_t ev_start = nullptr, ev_end = nullptr;
     int32_t* h_err = nullptr;  // pinned copy of d_err, read by the host-array entry points
     bool persistent = false;  // decode with the persistent stream-K kernel (when it applies) instead
+    long long wait_limit = mb::WAIT_LIMIT;  // mb_set_wait_limit
+    bool wait_probe = false;                // mb_set_wait_limit with a negative bound
     std::string last_error;
 };
 
@@ -82,6 +89,8 @@ inline RingView ring_view(const mb_ctx* c, int layer) {
     v.capacity = c->cfg.capacity;
     v.wrap = c->cfg.wrap;
     v.max_position = c->cfg.max_position;
+    v.wait_limit = c->wait_limit;
+    v.wait_probe = c->wait_probe ? 1 : 0;
     return v;
 }
 

@@ -55,7 +55,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, long lo
     }
 }
 
-constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s at 1.9 GHz; a bulk copy takes microseconds
+// (WAIT_LIMIT, the default bound of these waits, is defined in mb_internal.cuh)
 
 // ---------------------------------------------------------------- TMA (no multicast)
 

@@ -249,6 +249,13 @@ class KvRing:
         """Every slot of `stream_id` (all streams if -1) becomes empty."""
         self._check(self.lib.mb_reset(self.ctx, stream_id, self._stream(stream)))
 
+    def set_wait_limit(self, cycles: int) -> None:
+        """Bound (SM cycles) of the decode kernels' waits for their K/V chunks;
+        0 restores the default (about 2 s).  A wait that runs out surfaces as
+        MB_ERR_TIMEOUT at the next sync.  Negative: every wait targets a barrier
+        that nothing signals and runs out after -cycles (the test of that path)."""
+        self._check(self.lib.mb_set_wait_limit(self.ctx, int(cycles)))
+
     def sync(self, stream=None) -> None:
         """Wait for the stream and raise on any device-side rejection."""
         self._check(self.lib.mb_sync(self.ctx, self._stream(stream)))

@@ -561,3 +561,34 @@ def test_decode_on_a_capturing_stream(C):
     a.sync()
     b.sync()
     del g
+
+
+def test_bounded_wait_runs_out_and_the_context_recovers():
+    """A decode whose chunk waits target a barrier that nothing signals (bounded
+    at 20 000 cycles, ~10 us) gives up: mb_sync reports MB_ERR_TIMEOUT, the
+    appends of that step are in the ring all the same (they precede the waits),
+    and the next step at the default bound matches the oracle, which appended
+    both steps."""
+    S, C, L = 3, 200, 1
+    ring = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
+    orc = oracle.Ring(layers=L, streams=S, heads=H, capacity=C, dtype="f32", wrap=True)
+    items = [2, 0, 1]
+    for step in range(150):  # windows of several chunks
+        qkv = randn((S, QKV), seed=9000 + step)
+        ring.append_attend(0, items, [step] * S, torch.from_numpy(qkv).to(DEV))
+        orc.append_attend(0, items, [step] * S, qkv)
+    ring.sync()
+    ring.set_wait_limit(-20000)
+    qkv = randn((S, QKV), seed=9150)
+    ring.append_attend(0, items, [150] * S, torch.from_numpy(qkv).to(DEV))
+    orc.append_attend(0, items, [150] * S, qkv)
+    with pytest.raises(MockbirdError, match="MB_ERR_TIMEOUT"):
+        ring.sync()
+    ring.set_wait_limit(0)
+    for s in items:
+        assert_window_equal(ring, orc, 0, s, 0, s, 150)
+    qkv = randn((S, QKV), seed=9151)
+    out = ring.append_attend(0, items, [151] * S, torch.from_numpy(qkv).to(DEV))
+    ref, _ = orc.append_attend(0, items, [151] * S, qkv)
+    ring.sync()
+    assert max_err(out, ref) < TOL["f32"]
