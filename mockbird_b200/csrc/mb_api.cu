@@ -100,13 +100,22 @@ namespace {
 // (mb_decode.cu), or -- when MOCKBIRD_DECODE_KERNEL=persistent and the call fits
 // it -- the persistent stream-K kernel (mb_decode_persist.cu).  Both compute the
 // same thing.  overlap_previous: see launch_decode.
+// layers: consecutive layers from `layer` in one launch (q and out hold every
+// layer's n rows, layer after layer); the persistent kernel runs one launch per layer.
 cudaError_t run_decode(mb_ctx* c, bool append, int layer, int n, const int32_t* streams, const int32_t* positions,
-                       const float* q, int q_stride, float* out, cudaStream_t st, bool overlap_previous = false) {
-    const RingView v = ring_view(c, layer);
-    if (c->persistent && decode_persist_supported(v, n, q_stride))
-        return launch_decode_persist(c->cfg.dtype, append, v, c->scratch, n, streams, positions, q, q_stride, out, st);
-    return launch_decode(c->cfg.dtype, append, v, c->scratch, n, streams, positions, q, q_stride, out, st,
-                         overlap_previous);
+                       const float* q, int q_stride, float* out, cudaStream_t st, bool overlap_previous = false,
+                       int layers = 1) {
+    if (c->persistent && decode_persist_supported(ring_view(c, layer), n, q_stride)) {
+        for (int l = 0; l < layers; l++) {
+            const cudaError_t e = launch_decode_persist(c->cfg.dtype, append, ring_view(c, layer + l), c->scratch, n,
+                                                        streams, positions, q + (size_t)l * n * q_stride, q_stride,
+                                                        out + (size_t)l * n * c->cfg.heads * HD, st);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
+    return launch_decode(c->cfg.dtype, append, ring_view(c, layer), c->scratch, n, streams, positions, q, q_stride,
+                         out, st, overlap_previous, false, layers);
 }
 
 }  // namespace
@@ -190,8 +199,10 @@ MB_API int mb_create(const mb_config* cfg_in, mb_ctx** out) {
     const int part_slots = c->scratch.max_splits > persist_part_stride(cfg.dtype, cfg.capacity)
                                ? c->scratch.max_splits
                                : persist_part_stride(cfg.dtype, cfg.capacity);
-    const size_t part_bytes = (size_t)cfg.max_batch * cfg.heads * part_slots * (2 + HD) * sizeof(float);
-    const size_t cnt_bytes = (size_t)cfg.max_batch * cfg.heads * sizeof(int32_t);
+    // (one launch may cover every layer: items of all layers at once)
+    const size_t items = (size_t)cfg.max_batch * cfg.layers;
+    const size_t part_bytes = items * cfg.heads * part_slots * (2 + HD) * sizeof(float);
+    const size_t cnt_bytes = items * cfg.heads * sizeof(int32_t);
     c->scratch_bytes = part_bytes + cnt_bytes;
     if (cudaMalloc(&c->scratch.part, part_bytes) != cudaSuccess) return bail(MB_ERR_OOM);
     if (cudaMalloc(&c->scratch.counters, cnt_bytes) != cudaSuccess) return bail(MB_ERR_OOM);
@@ -253,7 +264,8 @@ MB_API int mb_reset(mb_ctx* c, int32_t stream, void* cuda_stream) {
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     CK(launch_reset(c, stream, st), "reset");
     if (stream < 0) {  // a full reset also re-arms the split-K tickets
-        CK(cudaMemsetAsync(c->scratch.counters, 0, (size_t)c->cfg.max_batch * c->cfg.heads * sizeof(int32_t), st),
+        CK(cudaMemsetAsync(c->scratch.counters, 0,
+                           (size_t)c->cfg.max_batch * c->cfg.layers * c->cfg.heads * sizeof(int32_t), st),
            "reset tickets");
     }
     return MB_OK;
@@ -315,10 +327,9 @@ MB_API int mb_decode_step(mb_ctx* c, int32_t n, const int32_t* streams, const in
     DeviceGuard g(c->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     const size_t hid = (size_t)c->cfg.heads * HD;
-    for (int layer = 0; layer < c->cfg.layers; layer++)
-        CK(run_decode(c, true, layer, n, streams, positions, qkv + (size_t)layer * n * 3 * hid, 3 * (int)hid,
-                      out + (size_t)layer * n * hid, st, layer > 0),
-           "append_attend launch");
+    // every layer in one launch: the layers touch disjoint rings
+    CK(run_decode(c, true, 0, n, streams, positions, qkv, 3 * (int)hid, out, st, false, c->cfg.layers),
+       "append_attend launch");
     return MB_OK;
 }
 
@@ -465,18 +476,23 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
         CK(cudaEventRecord(c->ev_in[gi], c->cp_in), "copy qkv");
         l = end;
     }
-    for (size_t l = 0, gi = 0, go = 0, first_out = 0; l < L; l++) {
+    // One launch per run of layers that no copy-group boundary splits: a run
+    // ends where an output group ends or the next input group starts.
+    for (size_t l = 0, gi = 0, go = 0, first_out = 0; l < L;) {
         if (in_start[l]) CK(cudaStreamWaitEvent(st, c->ev_in[gi++], 0), "wait qkv");
+        size_t e = l + 1;
+        while (e < L && !out_end[e - 1] && !in_start[e]) e++;
         CK(run_decode(c, true, (int)l, n, c->d_ids, c->d_ids + n, c->d_qkv + l * in_l, 3 * (int)hid,
-                      c->d_out + l * out_l, st, l > 0),
+                      c->d_out + l * out_l, st, l > 0, (int)(e - l)),
            "append_attend launch");
-        if (!out_end[l]) continue;
+        l = e;
+        if (!out_end[l - 1]) continue;
         CK(cudaEventRecord(c->ev_done[go++], st), "layer done");
         CK(cudaStreamWaitEvent(c->cp_out, c->ev_done[go - 1], 0), "wait layer");
         CK(cudaMemcpyAsync(out + first_out * out_l, c->d_out + first_out * out_l,
-                           (l + 1 - first_out) * out_l * sizeof(float), cudaMemcpyDeviceToHost, c->cp_out),
+                           (l - first_out) * out_l * sizeof(float), cudaMemcpyDeviceToHost, c->cp_out),
            "copy out");
-        first_out = l + 1;
+        first_out = l;
     }
     return finish_host_call(c, st, c->cp_out);
 }

@@ -118,8 +118,9 @@ struct DecodeShape {
     static constexpr int ROW_BYTES = HD * E;
 };
 
-// grid (max_splits, heads, n), 128 threads.  APPEND: q_in is the raw qkv row
-// (stride q_stride) and this launch also appends K/V; otherwise q_in holds an
+// grid (max_splits, heads, n * layers), 128 threads: blockIdx.z = layer * n +
+// item, layers consecutive from r's.  APPEND: q_in is the raw qkv row (stride
+// q_stride) and this launch also appends K/V; otherwise q_in holds an
 // already-roped query.
 // One context value of the output row: fp32, or bf16 when the caller feeds it
 // straight into a bf16 GEMM (the decoder step).
@@ -134,7 +135,7 @@ template <typename T, bool APPEND>
 __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, const int32_t* __restrict__ streams,
                                                      const int32_t* __restrict__ positions,
                                                      const float* __restrict__ q_in, int q_stride, void* out,
-                                                     int out_bf16, int pf_dist) {
+                                                     int out_bf16, int pf_dist, int n) {
     using S = DecodeShape<T>;
     constexpr int ROWS = S::ROWS, TPR = S::TPR, RB = S::ROW_BYTES;
     __shared__ __align__(128) unsigned char sk[ROWS * RB];
@@ -146,11 +147,16 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     __shared__ __align__(8) uint64_t bar[3];  // K chunk, V chunk, and one nothing signals (wait probe)
     __shared__ int ticket;
 
-    const int c = blockIdx.x, h = blockIdx.y, item = blockIdx.z, tid = threadIdx.x;
+    const int c = blockIdx.x, h = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
+    const int layer = z / n, item = z - layer * n;
     const int lane = tid & 31, warp = tid >> 5;
     const int s = streams[item], pos = positions[item];
     if (!item_ok(r, s, pos)) return;
     const int C = r.capacity, H = r.heads, HID = H * HD;
+    // this CTA's layer: its ring, slot positions, q rows and output rows
+    r.kv = reinterpret_cast<T*>(r.kv) + (size_t)layer * r.kv_layer;
+    r.slot_pos += (size_t)layer * r.slot_layer;
+    q_in += (size_t)layer * n * q_stride;
     const int count = min(pos + 1, C);
     const int nsplit = (count + ROWS - 1) / ROWS;
     if (c >= nsplit) return;
@@ -190,14 +196,16 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         const unsigned gx = gridDim.x, gy = gridDim.y;
         const unsigned t = blockIdx.x + gx * (blockIdx.y + gy * blockIdx.z) + (unsigned)pf_dist;
         if (t < gx * gy * gridDim.z) {
-            const int c2 = (int)(t % gx), h2 = (int)((t / gx) % gy), it2 = (int)(t / (gx * gy));
+            const int c2 = (int)(t % gx), h2 = (int)((t / gx) % gy), z2 = (int)(t / (gx * gy));
+            const int l2 = z2 / n, it2 = z2 - l2 * n;
             const int s2 = streams[it2], p2 = positions[it2];
             if (s2 >= 0 && s2 < r.streams && p2 >= 0) {
                 const int count2 = min(p2 + 1, C), j2 = c2 * ROWS;
                 if (j2 < count2) {
                     const uint32_t bytes2 = (uint32_t)min(ROWS, count2 - j2) * RB;
-                    const T* k2 = reinterpret_cast<const T*>(r.kv) + (((size_t)s2 * 2 + 0) * H + h2) * (size_t)C * HD;
-                    const T* v2 = reinterpret_cast<const T*>(r.kv) + (((size_t)s2 * 2 + 1) * H + h2) * (size_t)C * HD;
+                    const T* kv2 = reinterpret_cast<const T*>(r.kv) + ((ptrdiff_t)l2 - layer) * (ptrdiff_t)r.kv_layer;
+                    const T* k2 = kv2 + (((size_t)s2 * 2 + 0) * H + h2) * (size_t)C * HD;
+                    const T* v2 = kv2 + (((size_t)s2 * 2 + 1) * H + h2) * (size_t)C * HD;
                     bulk_prefetch_l2(k2 + (size_t)j2 * HD, bytes2);
                     bulk_prefetch_l2(v2 + (size_t)j2 * HD, bytes2);
                 }
@@ -322,14 +330,14 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     // never reaches further back than one kernel.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const size_t dst = (size_t)item * HID + h * HD;
+    const size_t dst = ((size_t)layer * n + item) * HID + h * HD;
     if (nsplit == 1) {
         if (tid < HD) store_ctx(out, out_bf16, dst + tid, l > 0.f ? acc / l : 0.f);
         return;
     }
 
     // ---- split-K: publish the partial; the last CTA of (item, head) combines
-    float* mine = sc.part + (((size_t)item * H + h) * sc.max_splits + c) * (2 + HD);
+    float* mine = sc.part + (((size_t)z * H + h) * sc.max_splits + c) * (2 + HD);
     if (tid < HD) mine[2 + tid] = acc;
     if (tid == 0) {
         mine[0] = m;
@@ -338,13 +346,13 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     __syncthreads();
     if (tid == 0) {  // one release for the whole CTA: the barrier orders the other threads' writes before it
         __threadfence();
-        ticket = atomicAdd(&sc.counters[(size_t)item * H + h], 1);
+        ticket = atomicAdd(&sc.counters[(size_t)z * H + h], 1);
     }
     __syncthreads();
     if (ticket != nsplit - 1) return;
     __threadfence();
     if (tid < HD) {
-        const float* base = sc.part + ((size_t)item * H + h) * sc.max_splits * (2 + HD);
+        const float* base = sc.part + ((size_t)z * H + h) * sc.max_splits * (2 + HD);
         float M = -INFINITY;
         for (int cc = 0; cc < nsplit; cc++) M = fmaxf(M, __ldcg(base + cc * (2 + HD)));
         float L = 0.f, o = 0.f;
@@ -357,7 +365,7 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         }
         store_ctx(out, out_bf16, dst + tid, L > 0.f ? o / L : 0.f);
     }
-    if (tid == 0) sc.counters[(size_t)item * H + h] = 0;
+    if (tid == 0) sc.counters[(size_t)z * H + h] = 0;
 }
 
 // ---------------------------------------------------------------- small rings (capacity <= 32)
@@ -366,18 +374,22 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
 // ring): one warp per (item, head), lane j scores slot j, warp shuffles for the
 // softmax, lane l owns dims 2l, 2l+1 of the query, the new row and the context.
 // No staging in shared memory and no split-K: a window is at most 32 slots.
-// grid (ceil(heads / 4), n), 128 threads.
+// grid (ceil(heads / 4), n * layers), 128 threads: blockIdx.y = layer * n + item.
 template <typename T, bool APPEND>
 __global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int32_t* __restrict__ streams,
                                                            const int32_t* __restrict__ positions,
                                                            const float* __restrict__ q_in, int q_stride, void* out,
-                                                           int out_bf16) {
+                                                           int out_bf16, int n) {
     __shared__ __align__(16) float qs[4][HD];  // the warp's roped query
     __shared__ __align__(16) float kn[4][HD];  // the warp's new K row (storage-rounded)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.x * 4 + warp, item = blockIdx.y;
+    const int layer = blockIdx.y / n, item = blockIdx.y - layer * n;
+    const int h = blockIdx.x * 4 + warp;
     const int s = streams[item], pos = positions[item];
     if (!item_ok(r, s, pos)) return;  // uniform over the CTA
+    r.kv = reinterpret_cast<T*>(r.kv) + (size_t)layer * r.kv_layer;
+    r.slot_pos += (size_t)layer * r.slot_layer;
+    q_in += (size_t)layer * n * q_stride;
     const int C = r.capacity, H = r.heads, HID = H * HD;
     const bool head_ok = h < H;
     const int count = min(pos + 1, C), newslot = pos % C;
@@ -476,7 +488,7 @@ __global__ void __launch_bounds__(128) decode_small_kernel(RingView r, const int
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (head_ok) {
-        const size_t dst = (size_t)item * HID + h * HD + 2 * lane;
+        const size_t dst = ((size_t)layer * n + item) * HID + h * HD + 2 * lane;
         const float inv = l > 0.f ? 1.f / l : 0.f;
         store_ctx(out, out_bf16, dst, a0 * inv);
         store_ctx(out, out_bf16, dst + 1, a1 * inv);
@@ -527,22 +539,24 @@ static int decode_prefetch_distance(int max_splits) {
 template <typename T>
 static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, int n, const int32_t* streams,
                             const int32_t* positions, const float* q, int q_stride, void* out, cudaStream_t st,
-                            bool overlap_previous, bool out_bf16) {
+                            bool overlap_previous, bool out_bf16, int layers) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(s.max_splits, r.heads, n);
+    cfg.gridDim = dim3(s.max_splits, r.heads, n * layers);
     cfg.blockDim = dim3(128);
     cfg.stream = st;
     const int ob = out_bf16 ? 1 : 0;
     if (r.capacity <= 32) {  // a window fits one warp
-        cfg.gridDim = dim3((r.heads + 3) / 4, n);
+        cfg.gridDim = dim3((r.heads + 3) / 4, n * layers);
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = overlap_previous ? 1 : 0;
         if (append)
-            return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, true>, r, streams, positions, q, q_stride, out, ob);
-        return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, false>, r, streams, positions, q, q_stride, out, ob);
+            return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, true>, r, streams, positions, q, q_stride, out, ob,
+                                      n);
+        return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, false>, r, streams, positions, q, q_stride, out, ob,
+                                  n);
     }
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -551,24 +565,24 @@ static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, in
     cfg.numAttrs = overlap_previous ? 1 : 0;
     if (append)
         return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out, ob,
-                                  decode_prefetch_distance(s.max_splits));
+                                  decode_prefetch_distance(s.max_splits), n);
     return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out, ob,
-                              decode_prefetch_distance(s.max_splits));
+                              decode_prefetch_distance(s.max_splits), n);
 }
 
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
                           const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
-                          void* out, cudaStream_t st, bool overlap_previous, bool out_bf16) {
+                          void* out, cudaStream_t st, bool overlap_previous, bool out_bf16, int layers) {
     switch (dtype) {
         case MB_F32:
             return decode_t<float>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous,
-                                   out_bf16);
+                                   out_bf16, layers);
         case MB_BF16:
             return decode_t<__nv_bfloat16>(append, r, s, n, streams, positions, q, q_stride, out, st,
-                                           overlap_previous, out_bf16);
+                                           overlap_previous, out_bf16, layers);
         default:
             return decode_t<__half>(append, r, s, n, streams, positions, q, q_stride, out, st, overlap_previous,
-                                    out_bf16);
+                                    out_bf16, layers);
     }
 }
 

@@ -35,6 +35,8 @@ struct RingView {
     const float2* rope;   // [max_position][32] (cos, sin)
     int32_t* err;         // device rejection bits
     int32_t streams, heads, capacity, wrap, max_position;
+    size_t kv_layer;      // elements of kv per layer (a launch over several layers steps by it)
+    size_t slot_layer;    // elements of slot_pos per layer
     long long wait_limit; // bound of the decode kernel's waits for its K/V chunk (cycles)
     int32_t wait_probe;   // 1: those waits target a barrier nothing signals (they run out; tests)
 };
@@ -82,6 +84,8 @@ inline RingView ring_view(const mb_ctx* c, int layer) {
     size_t per_layer = (size_t)c->cfg.streams * 2 * c->cfg.heads * (size_t)c->cfg.capacity * HD;
     v.kv = (char*)c->kv + per_layer * layer * c->esize;
     v.slot_pos = c->slot_pos + (size_t)layer * c->cfg.streams * c->cfg.capacity;
+    v.kv_layer = per_layer;
+    v.slot_layer = (size_t)c->cfg.streams * c->cfg.capacity;
     v.rope = c->rope;
     v.err = c->d_err;
     v.streams = c->cfg.streams;
@@ -115,9 +119,13 @@ cudaError_t launch_rope_append(int dtype, const RingView& r, int n, const int32_
 // (consecutive layers of one decode step): this launch's ring reads and append
 // may then run before that kernel has finished.
 // out_bf16: write the context rows as bf16 (out then points to __nv_bfloat16).
+// layers: the launch covers this many consecutive layers from r's (the same n
+// items in each): q and out of layer l at q + l*n*q_stride, out + l*n*heads*64;
+// the scratch must hold n * layers items.
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,
                           const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
-                          void* out, cudaStream_t st, bool overlap_previous = false, bool out_bf16 = false);
+                          void* out, cudaStream_t st, bool overlap_previous = false, bool out_bf16 = false,
+                          int layers = 1);
 bool decode_persist_supported(const RingView& r, int n, int q_stride);
 int persist_part_stride(int dtype, int capacity);  // split-K partial slots per (item, head)
 cudaError_t launch_decode_persist(int dtype, bool append, const RingView& r, const Scratch& s, int n,

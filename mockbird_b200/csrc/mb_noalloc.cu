@@ -86,6 +86,8 @@ extern "C" MB_API int mb_append_attend_noalloc(const mb_ring_ref* ring, int32_t 
     v.capacity = ring->capacity;
     v.wrap = ring->wrap;
     v.max_position = ring->max_position;
+    v.kv_layer = per_layer;
+    v.slot_layer = (size_t)ring->streams * ring->capacity;
     v.wait_limit = mb::WAIT_LIMIT;
     v.wait_probe = 0;
 

@@ -592,3 +592,30 @@ def test_bounded_wait_runs_out_and_the_context_recovers():
     ref, _ = orc.append_attend(0, items, [151] * S, qkv)
     ring.sync()
     assert max_err(out, ref) < TOL["f32"]
+
+
+@pytest.mark.parametrize("dtype,capacity", [("f32", 200), ("bf16", 300), ("f16", 24)])
+def test_decode_step_equals_layer_by_layer(dtype, capacity):
+    """mb_decode_step covers every layer in one launch (grid z = layer x item);
+    its contexts and rings equal mb_append_attend called layer by layer, bit for
+    bit, as windows grow past several split-K chunks and wrap (and on a ring of
+    at most 32 slots, the warp-per-head path)."""
+    S, L = 5, 4
+    a = KvRing(layers=L, streams=S, capacity=capacity, dtype=dtype, wrap=True)
+    b = KvRing(layers=L, streams=S, capacity=capacity, dtype=dtype, wrap=True)
+    order = [3, 0, 4, 1]
+    steps = capacity + 40
+    for step in range(steps):
+        qkv = torch.from_numpy(randn((L, len(order), QKV), seed=12000 + step)).to(DEV)
+        pos = [step + 2 * i for i in range(len(order))]
+        got = a.decode_step(order, pos, qkv)
+        for layer in range(L):
+            want = b.append_attend(layer, order, pos, qkv[layer].contiguous())
+            assert torch.equal(got[layer], want), (step, layer)
+    a.sync()
+    b.sync()
+    for layer in range(L):
+        for s, p in zip(order, pos):
+            ka, va, sa = a.gather(layer, s, p)
+            kb, vb, sb = b.gather(layer, s, p)
+            assert torch.equal(sa, sb) and torch.equal(ka, kb) and torch.equal(va, vb)
