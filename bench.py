@@ -3,8 +3,9 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|5] [--impl ours|reference]
 
-A *step* is one decode frame of every stream this GPU owns: 12 launches of the
-fused append+attend kernel (one per layer), through the C ABI (mb_decode_step).
+A *step* is one decode frame of every stream this GPU owns: all 12 layers'
+append + RoPE + attention in one launch of the fused kernel (grid over layer x
+item x head x chunk), through the C ABI (mb_decode_step).
 Workloads:
   2 (default)  64 streams/GPU, 12 layers x 12 heads x 64, fp32 ring of 512 slots;
                positions 0..1499 (the ring wraps twice), repeated, reset between passes.
@@ -75,11 +76,12 @@ def window_bytes(L, esize, layers=12):
 
 
 # DRAM read + write per launch over the algorithmic bytes, from the full ncu capture
-# of the fp32 decode kernel (32 streams, full 512-slot windows: 100.85 MB read +
-# 5.84 MB written, mean of 3 launches, for 101.25 MB algorithmic;
-# profiles/decode_kernel_f32_config2.md).  Traffic grows with the streams and the
-# window, so a launch's traffic is its algorithmic bytes times this ratio.
-DECODE_TRAFFIC_RATIO = {"f32": (100.85 + 5.84) / 101.25}
+# of the fp32 decode kernel (one launch over all 12 layers of 8 streams, full
+# 512-slot windows: 303.06 MB read + 6.68 MB written, mean of 2 launches, for
+# 303.76 MB algorithmic; profiles/decode_kernel_f32_config2.md).  Traffic grows
+# with the streams and the window, so a launch's traffic is its algorithmic bytes
+# times this ratio.
+DECODE_TRAFFIC_RATIO = {"f32": (303.06 + 6.68) / 303.76}
 
 
 def peaks():
@@ -297,7 +299,7 @@ def run_ours(args, cfg, rank, world, device):
         dist.barrier()
     ring.sync()
     ms_max = max_over_ranks(ms, device if dist else None)
-    launches = L * K
+    launches = K  # mb_decode_step: one launch covers every layer of the step
 
     # ---- end to end through the host-array C ABI call (pinned buffers), copies timed
     e2e = None
@@ -362,7 +364,7 @@ def run_ours(args, cfg, rank, world, device):
                                   "(profiles/decode_kernel_f32_config2.md)" if ratio else None,
                 "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
-                "kernel": "decode_kernel<fused append+RoPE+split-K attention>",
+                "kernel": "decode_kernel<fused append+RoPE+split-K attention>, all 12 layers of a step in one launch",
                 "algorithmic_bytes_per_launch": algo_bytes / launches,
                 "avg_launch_us": ms * 1e3 / launches,
                 "timing": ("CUDA events around each timed step on the launching stream (sum over the K steps); "
