@@ -129,7 +129,8 @@ MB_API int mb_append_attend(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t
                             void* cuda_stream);
 
 /* mb_append_attend for every layer of one decode step: the layer loop of
- * DecodeRunner.globalStep (decode.ts:735-748), one launch per layer from C.
+ * DecodeRunner.globalStep (decode.ts:735-748), all layers in ONE launch (they
+ * touch disjoint rings).
  * qkv: device f32 [layers][n][3*heads*64]; out: device f32 [layers][n][heads*64]. */
 MB_API int mb_decode_step(mb_ctx* ctx, int32_t n, const int32_t* streams, const int32_t* positions,
                           const float* qkv, float* out, void* cuda_stream);
@@ -142,10 +143,10 @@ MB_API int mb_append_attend_host(mb_ctx* ctx, int32_t layer, int32_t n, const in
                                  void* cuda_stream);
 
 /* One global decode step for n streams through ALL layers, HOST arrays:
- * qkv [layers][n][3*heads*64], out [layers][n][heads*64]; one launch per
- * layer; the rows are copied in and out in groups of consecutive layers on the
- * context's own copy streams, overlapping the other layers' decode; returns
- * once `out` is complete -- the granularity of DecodeRunner.globalStep
+ * qkv [layers][n][3*heads*64], out [layers][n][heads*64]; the layers run in a
+ * few launches of consecutive layers, whose rows are copied in and out as groups
+ * on the context's own copy streams, overlapping the other launches' decode;
+ * returns once `out` is complete -- the granularity of DecodeRunner.globalStep
  * (decode.ts:712-775: one submit, one readback). */
 MB_API int mb_decode_step_host(mb_ctx* ctx, int32_t n, const int32_t* streams, const int32_t* positions,
                                const float* qkv, float* out, void* cuda_stream);

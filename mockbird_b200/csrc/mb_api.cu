@@ -406,20 +406,16 @@ MB_API int mb_append_attend_host(mb_ctx* c, int32_t layer, int32_t n, const int3
     return finish_host_call(c, st, st);
 }
 
-// Copy groups of mb_decode_step_host.  A wait for a layer's inputs, and an event
-// that lets a layer's outputs leave, each end the programmatic overlap of two
-// consecutive decode launches (a few microseconds each).  When a layer's decode
-// takes several times as long as its copies, consecutive layers share one copy:
-// input groups grow from the front by the ratio, so each group lands while the
-// group before it decodes; output groups grow from the back by theirs, so each
-// group's copy ends while the group after it decodes and only the last layer's
-// rows are copied after the final launch.  Otherwise every layer is its own group.
-// The estimates: the decode streams its live windows at ~5 TB/s, a page-locked
-// copy moves ~50 GB/s each way; each ratio is divided by a margin of 1.5 and
-// rounded down, so copies up to 1.5 times slower than estimated still land in time.
-// in_start[l]: layer l begins an input group; out_end[l]: layer l ends an output group.
-static void host_step_groups(const mb_ctx* c, int n, const int32_t* positions, std::vector<char>& in_start,
-                             std::vector<char>& out_end) {
+// Segments of mb_decode_step_host: runs of consecutive layers [b_s, b_{s+1}),
+// each decoded by one launch, its qkv rows copied in as one group before it and
+// its context rows copied out as one group after it, on the context's two copy
+// streams, so that copies overlap the decode of other segments.  A launch
+// boundary costs the tail of a launch, and a copy group is waited for as a
+// whole, so the split is chosen by a small model: page-locked copies at ~50 GB/s
+// each way (serial per direction), the decode at ~5.5 TB/s of live-window bytes
+// per layer, and ~10 us per launch; every split into at most 4 segments is
+// tried and the one with the earliest estimated end is kept.
+static void host_step_plan(const mb_ctx* c, int n, const int32_t* positions, std::vector<int>& bounds) {
     const int L = c->cfg.layers;
     double window_bytes = 0;  // K and V windows one layer's decode reads
     for (int i = 0; i < n; i++) {
@@ -427,21 +423,39 @@ static void host_step_groups(const mb_ctx* c, int n, const int32_t* positions, s
         window_bytes += 2.0 * w * c->cfg.heads * HD * (double)c->esize;
     }
     const double hid = (double)c->cfg.heads * HD;
-    const double t_decode = window_bytes / 5.0e12, margin = 1.5;
-    const double rho_in = t_decode / (n * 3 * hid * 4 / 50.0e9) / margin;
-    const double rho_out = t_decode / (n * hid * 4 / 50.0e9) / margin;
-    in_start.assign(L, 0);
-    out_end.assign(L, 0);
-    double len = 1;
-    for (int l = 0; l < L; len = len * rho_in < 1 ? 1 : floor(len * rho_in)) {
-        in_start[l] = 1;
-        l += (int)(len < L ? len : L);
+    const double t_layer = window_bytes / 5.5e12, t_launch = 10e-6;
+    const double c_in = n * 3 * hid * 4 / 50e9, c_out = n * hid * 4 / 50e9;  // per layer
+    auto cost = [&](const std::vector<int>& b) {
+        double in_ready = 0, seg_end = 0, out_end = 0;
+        for (size_t s = 0; s + 1 < b.size(); s++) {
+            const int k = b[s + 1] - b[s];
+            in_ready += k * c_in;
+            seg_end = (seg_end > in_ready ? seg_end : in_ready) + k * t_layer + t_launch;
+            out_end = (out_end > seg_end ? out_end : seg_end) + k * c_out;
+        }
+        return out_end;
+    };
+    std::vector<int> best = {0, L}, cand;
+    double best_t = cost(best);
+    const int maxseg = L < 4 ? L : 4;
+    // every composition of L into 2..maxseg parts (cuts at increasing layers)
+    for (int parts = 2; parts <= maxseg; parts++) {
+        std::vector<int> cut(parts - 1);
+        for (int i = 0; i < parts - 1; i++) cut[i] = i + 1;
+        while (true) {
+            cand.assign(1, 0);
+            cand.insert(cand.end(), cut.begin(), cut.end());
+            cand.push_back(L);
+            const double t = cost(cand);
+            if (t < best_t) best_t = t, best = cand;
+            int i = parts - 2;
+            while (i >= 0 && cut[i] == L - (parts - 1 - i)) i--;
+            if (i < 0) break;
+            cut[i]++;
+            for (int j = i + 1; j < parts - 1; j++) cut[j] = cut[j - 1] + 1;
+        }
     }
-    len = 1;
-    for (int l = L - 1; l >= 0; len = len * rho_out < 1 ? 1 : floor(len * rho_out)) {
-        out_end[l] = 1;
-        l -= (int)(len < L ? len : L);
-    }
+    bounds = best;
 }
 
 MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, const int32_t* positions,
@@ -456,43 +470,34 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
     const size_t hid = (size_t)c->cfg.heads * HD, L = c->cfg.layers;
     const size_t in_l = (size_t)n * 3 * hid, out_l = (size_t)n * hid;  // floats per layer
-    std::vector<char> in_start, out_end;
-    host_step_groups(c, n, positions, in_start, out_end);
-    // Per input group: its qkv rows copied in on cp_in, and the decode of its
-    // first layer on `st` waits for them.  Per output group: its context rows
-    // copied out on cp_out once its last layer is done.  The copies of one group
-    // overlap the decode of the others.  Both copy streams start behind the work
-    // already queued on `st`, and `st` ends behind them.
+    std::vector<int> bounds;
+    host_step_plan(c, n, positions, bounds);
+    const size_t segs = bounds.size() - 1;
+    // Per segment: its qkv rows copied in on cp_in; its launch on `st` waits for
+    // them; its context rows copied out on cp_out once it is done.  Both copy
+    // streams start behind the work already queued on `st`, and `st` ends behind them.
     CK(cudaEventRecord(c->ev_start, st), "order copies");
     CK(cudaStreamWaitEvent(c->cp_in, c->ev_start, 0), "order copies");
     CK(cudaStreamWaitEvent(c->cp_out, c->ev_start, 0), "order copies");
     CK(stage_ids(c, n, streams, positions, c->cp_in), "copy streams and positions");
-    for (size_t l = 0, gi = 0; l < L; gi++) {
-        size_t end = l + 1;
-        while (end < L && !in_start[end]) end++;
-        CK(cudaMemcpyAsync(c->d_qkv + l * in_l, qkv + l * in_l, (end - l) * in_l * sizeof(float),
-                           cudaMemcpyHostToDevice, c->cp_in),
+    for (size_t g = 0; g < segs; g++) {
+        const size_t l = bounds[g], k = bounds[g + 1] - bounds[g];
+        CK(cudaMemcpyAsync(c->d_qkv + l * in_l, qkv + l * in_l, k * in_l * sizeof(float), cudaMemcpyHostToDevice,
+                           c->cp_in),
            "copy qkv");
-        CK(cudaEventRecord(c->ev_in[gi], c->cp_in), "copy qkv");
-        l = end;
+        CK(cudaEventRecord(c->ev_in[g], c->cp_in), "copy qkv");
     }
-    // One launch per run of layers that no copy-group boundary splits: a run
-    // ends where an output group ends or the next input group starts.
-    for (size_t l = 0, gi = 0, go = 0, first_out = 0; l < L;) {
-        if (in_start[l]) CK(cudaStreamWaitEvent(st, c->ev_in[gi++], 0), "wait qkv");
-        size_t e = l + 1;
-        while (e < L && !out_end[e - 1] && !in_start[e]) e++;
+    for (size_t g = 0; g < segs; g++) {
+        const size_t l = bounds[g], k = bounds[g + 1] - bounds[g];
+        CK(cudaStreamWaitEvent(st, c->ev_in[g], 0), "wait qkv");
         CK(run_decode(c, true, (int)l, n, c->d_ids, c->d_ids + n, c->d_qkv + l * in_l, 3 * (int)hid,
-                      c->d_out + l * out_l, st, l > 0, (int)(e - l)),
+                      c->d_out + l * out_l, st, false, (int)k),
            "append_attend launch");
-        l = e;
-        if (!out_end[l - 1]) continue;
-        CK(cudaEventRecord(c->ev_done[go++], st), "layer done");
-        CK(cudaStreamWaitEvent(c->cp_out, c->ev_done[go - 1], 0), "wait layer");
-        CK(cudaMemcpyAsync(out + first_out * out_l, c->d_out + first_out * out_l,
-                           (l - first_out) * out_l * sizeof(float), cudaMemcpyDeviceToHost, c->cp_out),
+        CK(cudaEventRecord(c->ev_done[g], st), "segment done");
+        CK(cudaStreamWaitEvent(c->cp_out, c->ev_done[g], 0), "wait segment");
+        CK(cudaMemcpyAsync(out + l * out_l, c->d_out + l * out_l, k * out_l * sizeof(float), cudaMemcpyDeviceToHost,
+                           c->cp_out),
            "copy out");
-        first_out = l;
     }
     return finish_host_call(c, st, c->cp_out);
 }

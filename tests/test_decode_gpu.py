@@ -282,9 +282,9 @@ def test_host_entry_points_match_device_path():
 
 
 def test_host_step_with_shared_copy_groups_matches_device_path():
-    """Windows long enough (64 streams x 512 fp32 slots) that the host step copies
-    several layers' rows in and out as one group; results equal the device path
-    bit for bit, layer by layer."""
+    """Windows long enough (64 streams x 512 fp32 slots) that the host step runs
+    several layers per launch and copies their rows in and out as one group;
+    results equal the device path bit for bit, layer by layer."""
     S, C, L = 64, 512, 12
     a = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
     b = KvRing(layers=L, streams=S, capacity=C, dtype="f32", wrap=True)
