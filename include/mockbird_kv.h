@@ -243,7 +243,8 @@ MB_API int mb_decoder_step_host(mb_decoder* dec, int32_t n, const int32_t* strea
  * (status 4-byte).  bn, splits: 0, 0 = the library's plan; else bn (32, 64 or
  * 128, dividing n) output columns per CTA and K split over `splits` (1..8, at
  * most k / 64) CTAs of a thread-block cluster, whose partials are summed in a
- * fixed order.  status: device int32 the kernel ORs 8 into when a bounded wait
+ * fixed order; splits = -1: a pair of CTAs per 128 x bn tile (one tcgen05 MMA
+ * over both, each CTA loading half of the rows of x and of W^T).  status: device int32 the kernel ORs 8 into when a bounded wait
  * gives up.  Async on cuda_stream. */
 MB_API int mb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void* x, const void* wt, const float* bias, void* y,
                         int32_t epi, int32_t bn, int32_t splits, int32_t* status, void* cuda_stream);

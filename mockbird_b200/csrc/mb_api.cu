@@ -468,7 +468,7 @@ MB_API int mb_decode_step_host(mb_ctx* c, int32_t n, const int32_t* streams, con
     if ((rc = check_items_host(c, n, streams, positions))) return rc;
     DeviceGuard g(c->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    const size_t hid = (size_t)c->cfg.heads * HD, L = c->cfg.layers;
+    const size_t hid = (size_t)c->cfg.heads * HD;
     const size_t in_l = (size_t)n * 3 * hid, out_l = (size_t)n * hid;  // floats per layer
     std::vector<int> bounds;
     host_step_plan(c, n, positions, bounds);

@@ -108,8 +108,8 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, cons
     auto pit = d->gemm_plans.find(pkey);
     if (pit == d->gemm_plans.end()) pit = d->gemm_plans.emplace(pkey, mb::gemm::choose(M, N, K, epi)).first;
     const mb::gemm::Plan p = pit->second;
-    const CUtensorMap* ta = operand_map(d, x, K, d->ctx->cfg.max_batch, mb::gemm::BM);
-    const CUtensorMap* tb = operand_map(d, Wt, K, N, p.bn);
+    const CUtensorMap* ta = operand_map(d, x, K, d->ctx->cfg.max_batch, mb::gemm::a_box_rows(p));
+    const CUtensorMap* tb = operand_map(d, Wt, K, N, mb::gemm::b_box_rows(p));
     if (!ta || !tb) return fail(d, MB_ERR_CUDA, "decoder: GEMM tensor map encoding failed");
     mb::gemm::Args a;
     a.M = M, a.N = N, a.K = K, a.splits = p.splits;

@@ -7,7 +7,7 @@
 // projection is one GEMM y[n][N] = x[n][K] W[K][N] on tcgen05:
 //   * W is stored transposed at upload (W^T [N][K], K-major), the activations
 //     x [n][K] are bf16 rows; both arrive by 2-D TMA (128-byte swizzle, no
-//     multicast) into a shared-memory ring of 6 stages;
+//     multicast) into a shared-memory ring of ~200 KB (6-12 stages);
 //   * one thread issues TMA, one thread issues tcgen05.mma (kind::f16, bf16 in,
 //     fp32 accumulate, M = 128 rows, N = 32, 64 or 128 columns) into TMEM,
 //     releasing each stage with tcgen05.commit;
@@ -44,15 +44,20 @@ constexpr int NTHREADS = 128;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int MAX_SPLITS = 8;         // the portable cluster size
 
+// Six stages in the ring: measured against 8-12 (rings of up to 200 KB) at the
+// decoder's shapes, deeper rings were no faster.
+constexpr int RING_STAGES = 6;
+
 template <int BN>
 struct Shape {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE = A_BYTES + B_BYTES;  // multiple of 1024: stage bases keep the swizzle alignment
-    static constexpr int STAGES = 6;
+    static constexpr int STAGES = RING_STAGES;
     static constexpr uint32_t TMEM_COLS = BN;        // a power of two >= 32
     static constexpr int TS = BN + 4;                // row stride (floats) of the staged output tile
-    static constexpr int BAR_OFF = STAGES * STAGE;   // barriers, TMEM address, bias after the ring
-    static constexpr int SMEM = BAR_OFF + 128 + BN * 4 + 1024;  // + alignment slack of the dynamic base
+    static constexpr int BAR_OFF = STAGES * STAGE;   // barriers, TMEM address, then the bias
+    static constexpr int BAR_BYTES = ((8 * (2 * STAGES + 1) + 4) + 127) / 128 * 128;
+    static constexpr int SMEM = BAR_OFF + BAR_BYTES + BN * 4 + 1024;  // + alignment slack of the dynamic base
     static_assert(BM * TS * 4 <= STAGES * STAGE, "the output tile is staged in the stage ring");
     static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
@@ -105,6 +110,19 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The two halves of a cluster-wide barrier, issued apart so its latency can hide
+// behind the work between them (every thread of every CTA arrives, then waits).
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
 // The epilogue of 4 consecutive columns n..n+3 of row m: v = acc (summed over
 // the splits), b = their bias (zero without one).
 template <int EPI>
@@ -141,7 +159,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t* empty = full + STAGES;
     uint64_t* done = empty + STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    float* sbias = reinterpret_cast<float*>(sm + S::BAR_OFF + 128);
+    float* sbias = reinterpret_cast<float*>(sm + S::BAR_OFF + S::BAR_BYTES);
     __shared__ int s_fail;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -314,6 +332,243 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------- CTA pairs
+
+template <int BN>
+struct PairShape {
+    static constexpr int A_H = 64 * BK * 2;            // this CTA's 64 rows of x per K block: 8 KB
+    static constexpr int B_H = (BN / 2) * BK * 2;      // its BN/2 rows of W^T per K block
+    static constexpr int STAGE = A_H + B_H;            // multiple of 1024 (swizzle-atom alignment)
+    static constexpr int STAGES = RING_STAGES;
+    static constexpr uint32_t TMEM_COLS = BN / 2 < 32 ? 32 : BN / 2;
+    static constexpr int TS = BN + 4;                  // row stride (floats) of the staged 64-row tile
+    static constexpr int BAR_OFF = STAGES * STAGE;
+    static constexpr int BAR_BYTES = ((8 * (3 * STAGES + 1) + 4) + 127) / 128 * 128;
+    // at least 120 KB: one CTA per SM, so that the pairs spread over the SMs
+    static constexpr int SMEM_NEED = BAR_OFF + BAR_BYTES + BN * 4 + 1024;
+    static constexpr int SMEM = SMEM_NEED < 120 * 1024 ? 120 * 1024 : SMEM_NEED;
+    static_assert(STAGE % 1024 == 0, "stage alignment");
+    static_assert(64 * TS * 4 <= STAGES * STAGE, "the output rows are staged in the stage ring");
+    static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+};
+
+// grid (2 * N / BN, ceil(M / 128)), clusters of (2, 1, 1), 128 threads.  A CTA
+// pair computes the 128 x BN output tile at rows m0.., columns n0..: CTA r (its
+// rank in the cluster) loads rows m0 + 64 r .. + 63 of x and rows
+// n0 + r BN/2 .. of W^T, and the even CTA issues tcgen05.mma.cta_group::2
+// (M = 128, N = BN) over both CTAs' tiles; each CTA's TMEM receives its own 64
+// output rows, columns [0, BN/2) in lanes 0-63 and [BN/2, BN) in lanes 64-127.
+// So each CTA streams 64 + BN/2 operand rows per K block where an unpaired
+// 128 x BN/2 tile would stream 128 + BN/2.
+// Stage protocol: the even CTA's producer waits for the stage to be free (its
+// `empty`, committed by the MMAs), sets the stage's byte count for both CTAs on
+// its `full`, signals the odd CTA's `go` for that stage, and loads its halves;
+// the odd CTA loads its halves only after `go`, so no copy is ever in flight that
+// the even CTA does not account for; both CTAs' copies complete on the even
+// CTA's `full`.  The MMAs' completion is multicast to both CTAs' `done`.
+template <int BN, int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Args a) {
+    using S = PairShape<BN>;
+    constexpr int STAGES = S::STAGES;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + S::BAR_OFF);
+    uint64_t* empty = full + STAGES;
+    uint64_t* go = empty + STAGES;
+    uint64_t* done = go + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    float* sbias = reinterpret_cast<float*>(sm + S::BAR_OFF + S::BAR_BYTES);
+    __shared__ int s_fail;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank();
+    const bool lead = rank == 0;
+    const int n0 = (blockIdx.x >> 1) * BN, m0 = blockIdx.y * BM;
+    const int a_row = m0 + 64 * (int)rank, b_row = n0 + (BN / 2) * (int)rank;
+    const int nkb = a.K / BK;
+    const int pre = nkb < STAGES ? nkb : STAGES;
+
+    if (warp == 0) tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    if (tid == 32) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&go[s], 1);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+        s_fail = 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // both CTAs' barriers exist before either touches the other's
+    cluster_arrive();
+    cluster_wait();
+    const uint32_t tbase = *tmem_slot;
+
+    int fills[STAGES] = {};  // even CTA's producer: fills accounted per stage (both CTAs' bytes)
+    const uint32_t full0 = peer_addr(full, 0);  // the even CTA's `full` barriers, in the cluster window
+    if (tid == 0) {
+        prefetch_tmap(&ta);
+        prefetch_tmap(&tb);
+        if (lead) {
+            const uint32_t peer_go = peer_addr(go, 1);
+            // stages of the first K blocks: weight tiles before waiting for the kernel ahead
+            for (int i = 0; i < pre; i++) {
+                mbar_expect_tx(&full[i], 2 * S::STAGE);
+                mbar_arrive_remote(peer_go + i * 8);
+                tma_load_2d_pair(sm + i * S::STAGE + S::A_H, &tb, i * BK, b_row, full0 + i * 8);
+                fills[i]++;
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int i = 0; i < pre; i++) tma_load_2d_pair(sm + i * S::STAGE, &ta, i * BK, a_row, full0 + i * 8);
+            for (int i = pre; i < nkb; i++) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, WAIT_LIMIT)) {
+                    atomicOr(&s_fail, 1);
+                    break;
+                }
+                mbar_expect_tx(&full[s], 2 * S::STAGE);
+                mbar_arrive_remote(peer_go + s * 8);
+                unsigned char* st = sm + s * S::STAGE;
+                tma_load_2d_pair(st + S::A_H, &tb, i * BK, b_row, full0 + s * 8);
+                tma_load_2d_pair(st, &ta, i * BK, a_row, full0 + s * 8);
+                fills[s]++;
+            }
+        } else {
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&go[s], (i / STAGES) & 1, WAIT_LIMIT)) {
+                    atomicOr(&s_fail, 1);
+                    break;
+                }
+                unsigned char* st = sm + s * S::STAGE;
+                tma_load_2d_pair(st + S::A_H, &tb, i * BK, b_row, full0 + s * 8);
+                if (i == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+                tma_load_2d_pair(st, &ta, i * BK, a_row, full0 + s * 8);
+            }
+        }
+    } else if (tid == 32 && lead) {
+        // ---- MMA issuer of the pair: D[128 x BN] (+)= A[128 x 64] B[BN x 64]^T per stage
+        constexpr uint32_t IDESC = idesc_f16(1u, 0u, 2 * 64, BN);
+        for (int i = 0; i < nkb; i++) {
+            const int s = i % STAGES;
+            if (!mbar_wait(&full[s], (i / STAGES) & 1, WAIT_LIMIT)) {
+                atomicOr(&s_fail, 1);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t aa = smem_u32(sm + s * S::STAGE), ba = aa + S::A_H;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; kk++)
+                umma_f16_pair(tbase, sdesc_sw128(aa + 32 * kk, 16, 1024), sdesc_sw128(ba + 32 * kk, 16, 1024), IDESC,
+                              (i > 0 || kk > 0) ? 1u : 0u);
+            umma_commit_pair(&empty[s]);
+        }
+        umma_commit_pair_mc(done, 0x3);  // both CTAs: every MMA issued above has completed
+    } else if (warp >= 2) {
+        for (int c = tid - 64; c < BN; c += 64) sbias[c] = a.bias ? a.bias[n0 + c] : 0.f;
+    }
+    __syncwarp();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    // ---- this CTA's 64 rows: warp w reads lanes 32w..32w+31, i.e. rows (w & 1) * 32 + lane
+    // and the column half (w >> 1)
+    if (!mbar_wait(done, 0, WAIT_LIMIT)) atomicOr(&s_fail, 1);
+    tc_fence_after();
+    float* tile = reinterpret_cast<float*>(sm);
+    {
+        const int r = (warp & 1) * 32 + lane, c0 = (warp >> 1) * (BN / 2);
+        const uint32_t taddr = tbase + ((uint32_t)(warp * 32) << 16);
+#pragma unroll
+        for (int c = 0; c < BN / 2; c += 16) {
+            float v[16];
+            tmem_ld16(taddr + c, v);  // warp-collective
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(tile + r * S::TS + c0 + c + j) =
+                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    tc_fence_before();
+    cluster_arrive();  // this CTA is done with its TMEM (the pair frees it together below)
+    __syncthreads();
+    constexpr int TPR = BN / 4, RPP = NTHREADS / TPR;
+    const int cq = (tid % TPR) * 4, rq = tid / TPR;
+    const float4 b4 = *reinterpret_cast<const float4*>(sbias + cq);
+    if (s_fail == 0) {
+#pragma unroll 4
+        for (int rr = rq; rr < 64; rr += RPP)
+            if (a_row + rr < a.M)
+                finish4<EPI>(a, a_row + rr, n0 + cq, *reinterpret_cast<const float4*>(tile + rr * S::TS + cq), b4);
+    } else if (tid == 0) {
+        atomicOr(a.err, DERR_TIMEOUT);
+        // the even CTA lets every copy it accounted for (its own and the odd CTA's) land
+        for (int s = 0; s < STAGES; s++)
+            if (fills[s] > 0) mbar_wait(&full[s], (fills[s] - 1) & 1, WAIT_LIMIT);
+    }
+    cluster_wait();
+    tc_fence_after();
+    if (warp == 0) tmem_free_pair(tbase, S::TMEM_COLS);
+}
+
+template <int BN, int EPI>
+cudaError_t prepare_pair(int dev) {
+    static bool attr_set[64] = {};
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             PairShape<BN>::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    return cudaSuccess;
+}
+
+template <int BN>
+void config_pair(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[2], const Args& a, cudaStream_t st, bool pdl) {
+    cfg = {};
+    cfg.gridDim = dim3(2 * (a.N / BN), (a.M + BM - 1) / BM, 1);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = PairShape<BN>::SMEM;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_pair_t(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, cudaStream_t st, bool pdl) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = prepare_pair<BN, EPI>(dev);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    config_pair<BN>(cfg, attr, a, st, pdl);
+    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, ta, tb, a);
+}
+
+template <int BN>
+cudaError_t launch_pair_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int epi, cudaStream_t st,
+                           bool pdl) {
+    switch (epi) {
+        case EPI_STORE: return launch_pair_t<BN, EPI_STORE>(ta, tb, a, st, pdl);
+        case EPI_ACCUM: return launch_pair_t<BN, EPI_ACCUM>(ta, tb, a, st, pdl);
+        case EPI_GELU_BF16: return launch_pair_t<BN, EPI_GELU_BF16>(ta, tb, a, st, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -420,15 +675,20 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Args& 
 
 }  // namespace
 
-// Cost of a plan in SM cycles, calibrated on B200 launches of this kernel at
+// Cost of a plan in SM cycles, calibrated on B200 launches of these kernels at
 // 256 rows: operand tiles stream from L2 at about 35 bytes per cycle per SM once
 // every SM loads; a split adds about 4 000 cycles of cluster barriers and
 // distributed-shared-memory latency, plus the partials each CTA reads (about 20
-// bytes per cycle).
+// bytes per cycle).  CTA pairs (cta_group::2) are not chosen: at 256 rows they
+// measured 1.5-2x slower than the best one-CTA plan (QKV 11.9 vs 7.2 us), and
+// are reached only by an explicit request (mb_gemm_bf16 with splits = -1).
 Plan choose(int M, int N, int K, int epi) {
     const int m_tiles = (M + BM - 1) / BM, kb = K / BK;
-    Plan best{32, 1};
+    Plan best{32, 1, 0};
     double best_cost = -1;
+    auto consider = [&](Plan p, double cost) {
+        if (best_cost < 0 || cost < best_cost) best_cost = cost, best = p;
+    };
     for (int bn : {128, 64, 32}) {
         if (N % bn) continue;
         const int tiles = m_tiles * (N / bn);  // one cluster per output tile
@@ -439,10 +699,7 @@ Plan choose(int M, int N, int K, int epi) {
             const double k_blocks = (kb + s - 1) / s;
             double cost = (double)(BM + bn) * k_blocks * BK * 2 / 35.0;
             if (s > 1) cost += 4000.0 + (double)BM * bn * 4 * (s - 1) / s / 20.0;
-            if (best_cost < 0 || cost < best_cost) {
-                best_cost = cost;
-                best = Plan{bn, s};
-            }
+            consider(Plan{bn, s, 0}, cost);
         }
     }
     return best;  // nothing fits one wave (very large M): 32-wide tiles, no split
@@ -462,10 +719,19 @@ bool make_map(CUtensorMap* m, const void* base, int k, int rows, int box_rows) {
 
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, const Plan& p, int epi,
                    cudaStream_t st, bool pdl) {
-    if (a.M <= 0 || a.K % BK || a.N % p.bn || p.splits < 1 || p.splits > MAX_SPLITS || a.K / BK < p.splits)
+    if (a.M <= 0 || a.K % BK || a.N % p.bn || p.splits < 1 || p.splits > MAX_SPLITS || a.K / BK < p.splits ||
+        (p.pair && p.splits != 1))
         return cudaErrorInvalidValue;
     Args b = a;
     b.splits = p.splits;
+    if (p.pair) {
+        switch (p.bn) {
+            case 128: return launch_pair_bn<128>(ta, tb, b, epi, st, pdl);
+            case 64: return launch_pair_bn<64>(ta, tb, b, epi, st, pdl);
+            case 32: return launch_pair_bn<32>(ta, tb, b, epi, st, pdl);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch (p.bn) {
         case 128: return launch_bn<128>(ta, tb, b, epi, st, pdl);
         case 64: return launch_bn<64>(ta, tb, b, epi, st, pdl);
@@ -485,16 +751,16 @@ MB_API int mb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void* x, const vo
                         int32_t epi, int32_t bn, int32_t splits, int32_t* status, void* cuda_stream) {
     using namespace mb::gemm;
     if (m < 0 || n <= 0 || k <= 0 || k % BK || n % 32 || epi < EPI_STORE || epi > EPI_GELU_BF16) return MB_ERR_ARG;
-    if ((bn != 0 && bn != 32 && bn != 64 && bn != 128) || splits < 0 || splits > MAX_SPLITS ||
+    if ((bn != 0 && bn != 32 && bn != 64 && bn != 128) || splits < -1 || splits > MAX_SPLITS ||
         (bn == 0) != (splits == 0) || (bn && n % bn) || splits > k / BK)
         return MB_ERR_ARG;
     if (m == 0) return MB_OK;
     auto mis = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; };
     if (!x || !wt || !y || !status || mis(x, 16) || mis(wt, 16) || mis(y, 16) || mis(bias, 16) || mis(status, 4))
         return MB_ERR_ARG;
-    const Plan p = bn ? Plan{bn, splits} : choose(m, n, k, epi);
+    const Plan p = bn ? (splits < 0 ? Plan{bn, 1, 1} : Plan{bn, splits, 0}) : choose(m, n, k, epi);
     CUtensorMap ta, tb;
-    if (!make_map(&ta, x, k, m, BM) || !make_map(&tb, wt, k, n, p.bn)) return MB_ERR_CUDA;
+    if (!make_map(&ta, x, k, m, a_box_rows(p)) || !make_map(&tb, wt, k, n, b_box_rows(p))) return MB_ERR_CUDA;
     Args a;
     a.M = m, a.N = n, a.K = k, a.splits = p.splits;
     a.bias = bias, a.y = y, a.ldy = n;

@@ -28,9 +28,13 @@ constexpr int BK = 64;   // K per stage: one 128-byte swizzle row of bf16
 // bytes per CTA (its operand tiles, plus the partial tiles it reads from the
 // other CTAs of its cluster) with all CTAs resident in one wave.
 struct Plan {
-    int bn;      // 32, 64 or 128 output columns per CTA
-    int splits;  // K split over this many CTAs of one thread-block cluster (1..8)
+    int bn;        // 32, 64 or 128 output columns per CTA (per CTA pair when `pair`)
+    int splits;    // K split over this many CTAs of one thread-block cluster (1..8)
+    int pair = 0;  // 1: a CTA pair (tcgen05 cta_group::2) per 128 x bn tile, K unsplit
 };
+// rows of the tensor-map boxes a plan loads: x rows per CTA, W^T rows per CTA
+inline int a_box_rows(const Plan& p) { return p.pair ? BM / 2 : BM; }
+inline int b_box_rows(const Plan& p) { return p.pair ? p.bn / 2 : p.bn; }
 Plan choose(int M, int N, int K, int epi);
 
 struct Args {
@@ -46,7 +50,7 @@ struct Args {
 // aligned base): box 64 x box_rows, 128-byte swizzle, zero fill past the last row.
 bool make_map(CUtensorMap* m, const void* base, int k, int rows, int box_rows);
 
-// ta: x [M][K] bf16 (box rows 128); tb: W^T [N][K] bf16 (box rows plan.bn).
+// ta: x [M][K] bf16 (box rows a_box_rows(plan)); tb: W^T [N][K] bf16 (box rows b_box_rows(plan)).
 // pdl: launch as a programmatic dependent of the previous kernel on `st` (the
 // kernel waits for it before its first read of x or access of y).
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, const Plan& p, int epi,

@@ -92,3 +92,18 @@ def test_rejects_bad_shapes():
     assert lib.mb_gemm_bf16(4, 96, 64, p, p, None, p, 0, 64, 1, p, None) == 1   # bn does not divide n
     assert lib.mb_gemm_bf16(4, 64, 640, p, p, None, p, 0, 64, 9, p, None) == 1  # more than 8 splits
     assert lib.mb_gemm_bf16(4, 64, 64, p, p, None, p, 0, 64, 0, p, None) == 1   # bn without splits
+
+
+# CTA pairs (splits = -1): one tcgen05 MMA over two CTAs, each loading half the
+# rows of x and of W^T; every tile width, rows around the 128-row tile and the
+# 64-row half, and the three epilogues
+@pytest.mark.parametrize("bn", [32, 64, 128])
+def test_cta_pairs(bn):
+    _run(256, 768, 768, 0, bn=bn, splits=-1)
+    _run(256, 384, 3072, 1, bn=bn, splits=-1)
+    _run(256, 1024, 768, 2, bn=bn, splits=-1)
+
+
+@pytest.mark.parametrize("m", [1, 63, 64, 65, 127, 129, 300])
+def test_cta_pair_row_edges(m):
+    _run(m, 256, 512, 1, bn=64, splits=-1)
