@@ -90,12 +90,12 @@ void transpose_to_bf16(const float* w, int K, int N, uint16_t* out) {
 }
 
 namespace {
-const CUtensorMap* operand_map(mb_decoder* d, const void* base, int k, int rows, int box_rows) {
-    const auto key = std::make_tuple(base, k, rows, box_rows);
+const CUtensorMap* operand_map(mb_decoder* d, const void* base, int k, int rows, int box_rows, int box_kb) {
+    const auto key = std::make_tuple(base, k, rows, box_rows, box_kb);
     auto it = d->maps.find(key);
     if (it == d->maps.end()) {
         CUtensorMap m;
-        if (!mb::gemm::make_map(&m, base, k, rows, box_rows)) return nullptr;
+        if (!mb::gemm::make_map(&m, base, k, rows, box_rows, box_kb)) return nullptr;
         it = d->maps.emplace(key, m).first;
     }
     return &it->second;
@@ -108,8 +108,8 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, cons
     auto pit = d->gemm_plans.find(pkey);
     if (pit == d->gemm_plans.end()) pit = d->gemm_plans.emplace(pkey, mb::gemm::choose(M, N, K, epi)).first;
     const mb::gemm::Plan p = pit->second;
-    const CUtensorMap* ta = operand_map(d, x, K, d->ctx->cfg.max_batch, mb::gemm::a_box_rows(p));
-    const CUtensorMap* tb = operand_map(d, Wt, K, N, mb::gemm::b_box_rows(p));
+    const CUtensorMap* ta = operand_map(d, x, K, d->ctx->cfg.max_batch, mb::gemm::a_box_rows(p), mb::gemm::box_kb(p));
+    const CUtensorMap* tb = operand_map(d, Wt, K, N, mb::gemm::b_box_rows(p), mb::gemm::box_kb(p));
     if (!ta || !tb) return fail(d, MB_ERR_CUDA, "decoder: GEMM tensor map encoding failed");
     mb::gemm::Args a;
     a.M = M, a.N = N, a.K = K, a.splits = p.splits;

@@ -27,9 +27,9 @@ struct mb_decoder {
     bf16* xb = nullptr;        // [max_batch][hid] GEMM input (LayerNorm output, context rows)
     float* qkv = nullptr;      // [max_batch][3*hid]
     bf16* h1 = nullptr;        // [max_batch][ffn] GELU(fc_in) output, fc_out's input
-    // tensor maps of the GEMM operands, built once per (base, k, rows, box rows),
+    // tensor maps of the GEMM operands, built once per (base, k, rows, box rows, box K blocks),
     // and the GEMM plans, once per (M, N, K, epilogue)
-    std::map<std::tuple<const void*, int, int, int>, CUtensorMap> maps;
+    std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> maps;
     std::map<std::tuple<int, int, int, int>, mb::gemm::Plan> gemm_plans;
     // mb_decoder_step replays one captured step per item count over staged inputs
     bool use_graph = true;

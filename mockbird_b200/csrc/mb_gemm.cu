@@ -6,8 +6,8 @@
 // streams decoding together the same weights serve n rows, so here each
 // projection is one GEMM y[n][N] = x[n][K] W[K][N] on tcgen05:
 //   * W is stored transposed at upload (W^T [N][K], K-major), the activations
-//     x [n][K] are bf16 rows; both arrive by 2-D TMA (128-byte swizzle, no
-//     multicast) into a shared-memory ring of ~200 KB (6-12 stages);
+//     x [n][K] are bf16 rows; both arrive by TMA (128-byte swizzle, no
+//     multicast; boxes of three or four K blocks) into a two-stage ring;
 //   * one thread issues TMA, one thread issues tcgen05.mma (kind::f16, bf16 in,
 //     fp32 accumulate, M = 128 rows, N = 32, 64 or 128 columns) into TMEM,
 //     releasing each stage with tcgen05.commit;
@@ -44,20 +44,30 @@ constexpr int NTHREADS = 128;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int MAX_SPLITS = 8;         // the portable cluster size
 
-// Six stages in the ring: measured against 8-12 (rings of up to 200 KB) at the
-// decoder's shapes, deeper rings were no faster.
+// Stages of the CTA-pair kernel's ring (one K block per stage).
 constexpr int RING_STAGES = 6;
 
+// One-CTA kernel: a ring stage is one TMA box of x and one of W^T, KB K blocks
+// deep each, and the ring holds two stages.  Measured on B200 (one thread
+// keeping a ring full, data in L2): a box costs the SM about the same time
+// whatever its size, so one K block per box moved 20-32 KB per ~640 cycles with
+// the MMAs running, and three to four K blocks per box ~330-400 cycles per K
+// block -- near the bound of shared memory itself, which every K block crosses
+// twice (TMA writes 16 KB of x and BN x 128 B of W^T, the MMAs read them).  A
+// deeper ring of the same boxes was no faster.
 template <int BN>
 struct Shape {
-    static constexpr int B_BYTES = BN * BK * 2;
-    static constexpr int STAGE = A_BYTES + B_BYTES;  // multiple of 1024: stage bases keep the swizzle alignment
-    static constexpr int STAGES = RING_STAGES;
-    static constexpr uint32_t TMEM_COLS = BN;        // a power of two >= 32
-    static constexpr int TS = BN + 4;                // row stride (floats) of the staged output tile
-    static constexpr int BAR_OFF = STAGES * STAGE;   // barriers, TMEM address, then the bias
+    static constexpr int KB = kb_per_box(BN);         // K blocks per box
+    static constexpr int B_BYTES = BN * BK * 2;       // one K block of W^T rows
+    static constexpr int A_STAGE = KB * A_BYTES;      // x: KB tiles [128][64]
+    static constexpr int STAGE = KB * (A_BYTES + B_BYTES);  // then W^T: KB tiles [BN][64]
+    static constexpr int STAGES = 2;
+    static constexpr uint32_t TMEM_COLS = BN;         // a power of two >= 32
+    static constexpr int TS = BN + 4;                 // row stride (floats) of the staged output tile
+    static constexpr int BAR_OFF = STAGES * STAGE;    // barriers, TMEM address, then the bias
     static constexpr int BAR_BYTES = ((8 * (2 * STAGES + 1) + 4) + 127) / 128 * 128;
     static constexpr int SMEM = BAR_OFF + BAR_BYTES + BN * 4 + 1024;  // + alignment slack of the dynamic base
+    static_assert(STAGE % 1024 == 0 && A_STAGE % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle-atom alignment");
     static_assert(BM * TS * 4 <= STAGES * STAGE, "the output tile is staged in the stage ring");
     static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
@@ -151,7 +161,7 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Args a) {
     using S = Shape<BN>;
-    constexpr int STAGES = S::STAGES;
+    constexpr int STAGES = S::STAGES, KB = S::KB;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~uintptr_t(1023));
@@ -168,10 +178,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int kb_total = a.K / BK;
     const int kb0 = split * kb_total / a.splits, kb1 = (split + 1) * kb_total / a.splits;
     const int nkb = kb1 - kb0;  // >= 1: the host keeps at least one K block per split
-    const int pre = nkb < STAGES ? nkb : STAGES;  // stages whose weight tiles load before the wait
+    const int nch = (nkb + KB - 1) / KB;          // boxes of KB K blocks (ring stages) this CTA multiplies
+    const int pre = nch < STAGES ? nch : STAGES;  // stages whose weight boxes load before the wait
 
-    if (warp == 0) tmem_alloc(tmem_slot, S::TMEM_COLS);
-    if (tid == 32) {
+    int fills[STAGES] = {};  // producer: loads issued per stage
+    if (tid == 0) {
+        // ---- TMA producer.  Its barriers first; the weight boxes of the first
+        // stages do not depend on the kernel before this one, so they are
+        // requested at once, ahead of the TMEM allocation and the block barrier.
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
@@ -179,62 +193,67 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(done, 1);
         fence_mbar_init();
         s_fail = 0;
+        prefetch_tmap(&ta);
+        prefetch_tmap(&tb);
+        for (int c = 0; c < pre; c++) {
+            mbar_expect_tx(&full[c], S::STAGE);
+            tma_load_3d(sm + c * S::STAGE + S::A_STAGE, &tb, 0, n0, kb0 + c * KB, &full[c]);
+        }
+    } else if (warp == 1) {
+        tmem_alloc(tmem_slot, S::TMEM_COLS);
+    } else if (warp >= 2) {
+        // the bias (a weight: no kernel writes it) into shared memory while the tiles are in flight
+        for (int c = tid - 64; c < BN; c += 64) sbias[c] = a.bias ? a.bias[n0 + c] : 0.f;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
 
-    int fills[STAGES] = {};  // producer: loads issued per stage
     if (tid == 0) {
-        // ---- TMA producer.  The weight tiles of the first stages do not depend
-        // on the kernel before this one, so they are requested before waiting
-        // for it (programmatic dependent launch); the activation tiles after.
-        prefetch_tmap(&ta);
-        prefetch_tmap(&tb);
-        for (int i = 0; i < pre; i++) {
-            mbar_expect_tx(&full[i], S::STAGE);
-            tma_load_2d(sm + i * S::STAGE + A_BYTES, &tb, (kb0 + i) * BK, n0, &full[i]);
-        }
+        // the activation boxes after the kernel ahead has finished (programmatic
+        // dependent launch).  A box may reach past this CTA's K range: the K
+        // blocks of the next split (read, never multiplied) or past K (zero fill).
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        for (int i = 0; i < pre; i++) {
-            tma_load_2d(sm + i * S::STAGE, &ta, (kb0 + i) * BK, m0, &full[i]);
-            fills[i]++;
+        for (int c = 0; c < pre; c++) {
+            tma_load_3d(sm + c * S::STAGE, &ta, 0, m0, kb0 + c * KB, &full[c]);
+            fills[c]++;
         }
-        // stage i % STAGES again once the MMAs reading it have completed
-        for (int i = pre; i < nkb; i++) {
-            const int s = i % STAGES;
-            if (!mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, WAIT_LIMIT)) {
+        // stage c % STAGES again once the MMAs reading it have completed
+        for (int c = pre; c < nch; c++) {
+            const int s = c % STAGES;
+            if (!mbar_wait(&empty[s], ((c / STAGES) - 1) & 1, WAIT_LIMIT)) {
                 atomicOr(&s_fail, 1);
                 break;
             }
             unsigned char* st = sm + s * S::STAGE;
             mbar_expect_tx(&full[s], S::STAGE);
-            tma_load_2d(st + A_BYTES, &tb, (kb0 + i) * BK, n0, &full[s]);
-            tma_load_2d(st, &ta, (kb0 + i) * BK, m0, &full[s]);
+            tma_load_3d(st + S::A_STAGE, &tb, 0, n0, kb0 + c * KB, &full[s]);
+            tma_load_3d(st, &ta, 0, m0, kb0 + c * KB, &full[s]);
             fills[s]++;
         }
     } else if (tid == 32) {
-        // ---- MMA issuer: D[128 x BN] (+)= A[128 x 64] B[BN x 64]^T per stage, 4 MMAs of K = 16
+        // ---- MMA issuer: D[128 x BN] (+)= A[128 x 64] B[BN x 64]^T per K block, 4 MMAs of K = 16
         constexpr uint32_t IDESC = idesc_f16(1u, 0u, BM, BN);
-        for (int i = 0; i < nkb; i++) {
-            const int s = i % STAGES;
-            if (!mbar_wait(&full[s], (i / STAGES) & 1, WAIT_LIMIT)) {
+        for (int c = 0; c < nch; c++) {
+            const int s = c % STAGES;
+            if (!mbar_wait(&full[s], (c / STAGES) & 1, WAIT_LIMIT)) {
                 atomicOr(&s_fail, 1);
                 break;
             }
             tc_fence_after();
-            const uint32_t aa = smem_u32(sm + s * S::STAGE), ba = aa + A_BYTES;
+            const uint32_t base = smem_u32(sm + s * S::STAGE);
+            const int nq = min(KB, nkb - c * KB);  // the box's K blocks inside this CTA's range
+            for (int q = 0; q < nq; q++) {
+                const uint32_t aa = base + q * A_BYTES, ba = base + S::A_STAGE + q * S::B_BYTES;
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; kk++)
-                umma_f16(tbase, sdesc_sw128(aa + 32 * kk, 16, 1024), sdesc_sw128(ba + 32 * kk, 16, 1024), IDESC,
-                         (i > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < BK / 16; kk++)
+                    umma_f16(tbase, sdesc_sw128(aa + 32 * kk, 16, 1024), sdesc_sw128(ba + 32 * kk, 16, 1024), IDESC,
+                             (c > 0 || q > 0 || kk > 0) ? 1u : 0u);
+            }
             umma_commit(&empty[s]);
         }
         umma_commit(done);  // arrives once every MMA issued above has completed
-    } else if (warp >= 2) {
-        // the bias (a weight: no kernel writes it) into shared memory while the tiles are in flight
-        for (int c = tid - 64; c < BN; c += 64) sbias[c] = a.bias ? a.bias[n0 + c] : 0.f;
     }
     // The other lanes of the producer and MMA warps wait here, at a warp barrier,
     // instead of polling the accumulator barrier beside their working lane.
@@ -420,11 +439,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int i = 0; i < pre; i++) {
                 mbar_expect_tx(&full[i], 2 * S::STAGE);
                 mbar_arrive_remote(peer_go + i * 8);
-                tma_load_2d_pair(sm + i * S::STAGE + S::A_H, &tb, i * BK, b_row, full0 + i * 8);
+                tma_load_3d_pair(sm + i * S::STAGE + S::A_H, &tb, 0, b_row, i, full0 + i * 8);
                 fills[i]++;
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            for (int i = 0; i < pre; i++) tma_load_2d_pair(sm + i * S::STAGE, &ta, i * BK, a_row, full0 + i * 8);
+            for (int i = 0; i < pre; i++) tma_load_3d_pair(sm + i * S::STAGE, &ta, 0, a_row, i, full0 + i * 8);
             for (int i = pre; i < nkb; i++) {
                 const int s = i % STAGES;
                 if (!mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, WAIT_LIMIT)) {
@@ -434,8 +453,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_expect_tx(&full[s], 2 * S::STAGE);
                 mbar_arrive_remote(peer_go + s * 8);
                 unsigned char* st = sm + s * S::STAGE;
-                tma_load_2d_pair(st + S::A_H, &tb, i * BK, b_row, full0 + s * 8);
-                tma_load_2d_pair(st, &ta, i * BK, a_row, full0 + s * 8);
+                tma_load_3d_pair(st + S::A_H, &tb, 0, b_row, i, full0 + s * 8);
+                tma_load_3d_pair(st, &ta, 0, a_row, i, full0 + s * 8);
                 fills[s]++;
             }
         } else {
@@ -446,9 +465,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     break;
                 }
                 unsigned char* st = sm + s * S::STAGE;
-                tma_load_2d_pair(st + S::A_H, &tb, i * BK, b_row, full0 + s * 8);
+                tma_load_3d_pair(st + S::A_H, &tb, 0, b_row, i, full0 + s * 8);
                 if (i == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
-                tma_load_2d_pair(st, &ta, i * BK, a_row, full0 + s * 8);
+                tma_load_3d_pair(st, &ta, 0, a_row, i, full0 + s * 8);
             }
         }
     } else if (tid == 32 && lead) {
@@ -676,8 +695,9 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Args& 
 }  // namespace
 
 // Cost of a plan in SM cycles, calibrated on B200 launches of these kernels at
-// 256 rows: operand tiles stream from L2 at about 35 bytes per cycle per SM once
-// every SM loads; a split adds about 4 000 cycles of cluster barriers and
+// 256 rows: a CTA's K blocks cost about (128 + bn) x 128 bytes of shared-memory
+// traffic each way (TMA writes, the MMAs read; whole boxes are written), at
+// ~128 bytes per cycle; a split adds about 4 000 cycles of cluster barriers and
 // distributed-shared-memory latency, plus the partials each CTA reads (about 20
 // bytes per cycle).  CTA pairs (cta_group::2) are not chosen: at 256 rows they
 // measured 1.5-2x slower than the best one-CTA plan (QKV 11.9 vs 7.2 us), and
@@ -696,8 +716,9 @@ Plan choose(int M, int N, int K, int epi) {
             // one wave: every cluster resident at once
             const int fit = active_clusters_of(bn, epi, s);
             if (fit <= 0 || tiles > fit) break;
-            const double k_blocks = (kb + s - 1) / s;
-            double cost = (double)(BM + bn) * k_blocks * BK * 2 / 35.0;
+            const int k_blocks = (kb + s - 1) / s, box = kb_per_box(bn);
+            const int written = (k_blocks + box - 1) / box * box;
+            double cost = (double)(BM + bn) * BK * 2 * (written + k_blocks) / 128.0;
             if (s > 1) cost += 4000.0 + (double)BM * bn * 4 * (s - 1) / s / 20.0;
             consider(Plan{bn, s, 0}, cost);
         }
@@ -705,14 +726,14 @@ Plan choose(int M, int N, int K, int epi) {
     return best;  // nothing fits one wave (very large M): 32-wide tiles, no split
 }
 
-bool make_map(CUtensorMap* m, const void* base, int k, int rows, int box_rows) {
+bool make_map(CUtensorMap* m, const void* base, int k, int rows, int box_rows, int box_kb) {
     auto fn = encode_fn();
-    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (k * 2) % 16) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || k % BK || box_kb < 1) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)BK, (cuuint64_t)rows, (cuuint64_t)(k / BK)};
+    cuuint64_t strides[2] = {(cuuint64_t)k * 2, (cuuint64_t)BK * 2};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)box_kb};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -760,7 +781,8 @@ MB_API int mb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void* x, const vo
         return MB_ERR_ARG;
     const Plan p = bn ? (splits < 0 ? Plan{bn, 1, 1} : Plan{bn, splits, 0}) : choose(m, n, k, epi);
     CUtensorMap ta, tb;
-    if (!make_map(&ta, x, k, m, a_box_rows(p)) || !make_map(&tb, wt, k, n, b_box_rows(p))) return MB_ERR_CUDA;
+    if (!make_map(&ta, x, k, m, a_box_rows(p), box_kb(p)) || !make_map(&tb, wt, k, n, b_box_rows(p), box_kb(p)))
+        return MB_ERR_CUDA;
     Args a;
     a.M = m, a.N = n, a.K = k, a.splits = p.splits;
     a.bias = bias, a.y = y, a.ldy = n;

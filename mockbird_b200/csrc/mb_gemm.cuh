@@ -32,9 +32,13 @@ struct Plan {
     int splits;    // K split over this many CTAs of one thread-block cluster (1..8)
     int pair = 0;  // 1: a CTA pair (tcgen05 cta_group::2) per 128 x bn tile, K unsplit
 };
-// rows of the tensor-map boxes a plan loads: x rows per CTA, W^T rows per CTA
+// The tensor-map boxes a plan loads: x rows per CTA, W^T rows per CTA, and K
+// blocks per box.  A TMA box costs about the same SM time whatever its size, so
+// the one-CTA kernel fetches several K blocks per box (3-D view of the matrix).
 inline int a_box_rows(const Plan& p) { return p.pair ? BM / 2 : BM; }
 inline int b_box_rows(const Plan& p) { return p.pair ? p.bn / 2 : p.bn; }
+constexpr int kb_per_box(int bn) { return bn == 128 ? 3 : 4; }  // one-CTA kernel (two stages of boxes)
+inline int box_kb(const Plan& p) { return p.pair ? 1 : kb_per_box(p.bn); }
 Plan choose(int M, int N, int K, int epi);
 
 struct Args {
@@ -46,11 +50,15 @@ struct Args {
     int* err;              // device status word: DERR_TIMEOUT is OR-ed in when a bounded wait gives up
 };
 
-// 2-D tensor map of a K-major bf16 matrix [rows][k] (rows k*2 bytes apart, 16-byte
-// aligned base): box 64 x box_rows, 128-byte swizzle, zero fill past the last row.
-bool make_map(CUtensorMap* m, const void* base, int k, int rows, int box_rows);
+// Tensor map of a K-major bf16 matrix [rows][k] (rows k*2 bytes apart, 16-byte
+// aligned base) viewed as [k / 64][rows][64]: dims (64, rows, k / 64), strides
+// (k*2, 128) bytes; box 64 x box_rows x box_kb, 128-byte swizzle, zero fill past
+// the last row and the last K block.  A box lands in shared memory as box_kb
+// consecutive [box_rows][64] tiles, each swizzled as a 2-D box of its own would be.
+bool make_map(CUtensorMap* m, const void* base, int k, int rows, int box_rows, int box_kb);
 
-// ta: x [M][K] bf16 (box rows a_box_rows(plan)); tb: W^T [N][K] bf16 (box rows b_box_rows(plan)).
+// ta: x [M][K] bf16 (box a_box_rows(plan) x box_kb(plan)); tb: W^T [N][K] bf16
+// (box b_box_rows(plan) x box_kb(plan)).
 // pdl: launch as a programmatic dependent of the previous kernel on `st` (the
 // kernel waits for it before its first read of x or access of y).
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, const Plan& p, int epi,

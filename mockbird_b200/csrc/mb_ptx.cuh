@@ -181,6 +181,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, in
         : "memory");
 }
 
+// 3-D form of tma_load_2d_pair (coordinates c0 innermost, always 0 here).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* tmap, int c0, int c1, int c2,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 // Arrive (release, cluster scope) on the mbarrier at `addr` of the cluster's shared window.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
