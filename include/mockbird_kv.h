@@ -342,8 +342,8 @@ MB_API int mb_argmax_penalty(int32_t n, int32_t codes, const float* logits, uint
 
 /* Maximum scratch of mb_append_attend_noalloc: a call needs
  * n * heads * ceil(capacity / chunk) * 66 * 4 bytes of partials (chunk = 64 slots
- * for fp32, 128 for 16-bit storage) plus n * heads * 4 bytes of counters,
- * each rounded up to 256 bytes; larger calls are rejected with MB_ERR_ARG. */
+ * for fp32, 128 for 16-bit storage), rounded up to 256 bytes; larger calls are
+ * rejected with MB_ERR_ARG. */
 #define MB_NOALLOC_SCRATCH_BYTES (8u << 20)
 
 /* A ring in caller-owned device memory, laid out as a context's (see above). */
@@ -361,10 +361,10 @@ typedef struct mb_ring_ref {
  * outputs and results as mb_append_attend; scratch comes from the library's
  * fixed device array.  The first call on each device looks that array up
  * (cudaGetSymbolAddress, with the caller's current device), so make that first
- * call before any stream capture.  Every call shares the one array and its
- * ticket counters are cleared at the start of each call: calls that overlap on
- * the GPU (other streams, other threads) race and must be serialised by the
- * caller.  Uses the current CUDA device, in its primary context; the looked-up
+ * call before any stream capture.  Every call shares the one array and keeps
+ * its partials there until the call's combine kernel has read them: calls that
+ * overlap on the GPU (other streams, other threads) race and must be serialised
+ * by the caller.  Uses the current CUDA device, in its primary context; the looked-up
  * address stays cached for the life of the process, so do not reset the device
  * (cudaDeviceReset) while using this entry point.  Returns MB_ERR_ARG for bad
  * arguments -- null or misaligned pointers (qkv, out and kv 16-byte aligned,

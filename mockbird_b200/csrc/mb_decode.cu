@@ -8,9 +8,10 @@
 // lane and six barriers per 64-slot tile.  Here every (item, head) window is cut
 // into 16 KB chunks of K and V; each CTA pulls its chunk into shared memory with
 // two bulk copies (cp.async.bulk, no multicast), scores it with bank-conflict-
-// free rotated 16-byte reads, and leaves an (m, l, acc[64]) partial.  The last
-// CTA of an (item, head) to finish folds the partials (online-softmax rescale)
-// and writes the context row.  No tensor cores: one query per head is a GEMV.
+// free rotated 16-byte reads, and leaves an (m, l, acc[64]) partial with plain
+// stores.  A small kernel launched right behind it (a programmatic dependent)
+// folds each window's partials (online-softmax rescale) and writes the context
+// row.  No tensor cores: one query per head is a GEMV.
 #include "mb_internal.cuh"
 #include "mb_ptx.cuh"
 
@@ -145,7 +146,6 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
     __shared__ float red[4][HD];
     __shared__ float wmax[4], wsum[4];
     __shared__ __align__(8) uint64_t bar[3];  // K chunk, V chunk, and one nothing signals (wait probe)
-    __shared__ int ticket;
 
     const int c = blockIdx.x, h = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
     const int layer = z / n, item = z - layer * n;
@@ -336,36 +336,86 @@ __global__ void __launch_bounds__(128) decode_kernel(RingView r, Scratch sc, con
         return;
     }
 
-    // ---- split-K: publish the partial; the last CTA of (item, head) combines
+    // ---- split-K: publish the partial and exit.  fold_kernel, launched right
+    // behind this kernel, combines the partials of every window once they are
+    // all written (its griddepcontrol.wait orders them), so no CTA waits on a
+    // fence or a ticket here.
     float* mine = sc.part + (((size_t)z * H + h) * sc.max_splits + c) * (2 + HD);
     if (tid < HD) mine[2 + tid] = acc;
     if (tid == 0) {
         mine[0] = m;
         mine[1] = l;
     }
-    __syncthreads();
-    if (tid == 0) {  // one release for the whole CTA: the barrier orders the other threads' writes before it
-        __threadfence();
-        ticket = atomicAdd(&sc.counters[(size_t)z * H + h], 1);
+}
+
+// The split-K combine: one warp per (item, head) window of more than one chunk.
+// Lane l reads split l's (m, l) (and every 32nd after it), the warp reduces the
+// maximum and the weighted sum, and lane l then sums dims 2l, 2l+1 of every
+// split's acc with that split's weight 2^(m_c - M), the loads of a batch of
+// splits in flight together.  Launched as a programmatic dependent of the decode
+// kernel: griddepcontrol.wait returns once that kernel has completed and its
+// partials are visible.  Dependents are released right away: the next decode
+// launch touches the scratch and the output only after its own wait, which
+// returns only once this kernel has completed.
+// grid (ceil(heads / 4), n * layers), 128 threads: blockIdx.y = layer * n + item.
+__global__ void __launch_bounds__(128) fold_kernel(RingView r, Scratch sc, const int32_t* __restrict__ streams,
+                                                   const int32_t* __restrict__ positions, void* out, int out_bf16,
+                                                   int rows_per_chunk, int n) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    constexpr int PS = 2 + HD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x * 4 + warp, z = blockIdx.y;
+    const int layer = z / n, item = z - layer * n;
+    const int H = r.heads;
+    if (h >= H) return;
+    const int s = streams[item], pos = positions[item];
+    // an item the decode kernel rejected (and flagged) has no partials
+    if (s < 0 || s >= r.streams || pos < 0 || pos >= r.max_position || (!r.wrap && pos >= r.capacity)) return;
+    const int count = min(pos + 1, r.capacity);
+    const int nsplit = (count + rows_per_chunk - 1) / rows_per_chunk;
+    if (nsplit <= 1) return;  // the decode kernel wrote the row itself
+    const float* base = sc.part + ((size_t)z * H + h) * sc.max_splits * PS;
+
+    float m0 = -INFINITY, l0 = 0.f;  // split `lane`
+    if (lane < nsplit) {
+        m0 = __ldcg(base + (size_t)lane * PS);
+        l0 = __ldcg(base + (size_t)lane * PS + 1);
     }
-    __syncthreads();
-    if (ticket != nsplit - 1) return;
-    __threadfence();
-    if (tid < HD) {
-        const float* base = sc.part + ((size_t)z * H + h) * sc.max_splits * (2 + HD);
-        float M = -INFINITY;
-        for (int cc = 0; cc < nsplit; cc++) M = fmaxf(M, __ldcg(base + cc * (2 + HD)));
-        float L = 0.f, o = 0.f;
-        for (int cc = 0; cc < nsplit; cc++) {
-            const float mc = __ldcg(base + cc * (2 + HD));
-            if (mc == -INFINITY) continue;
-            const float w = exp2f(mc - M);
-            L = fmaf(__ldcg(base + cc * (2 + HD) + 1), w, L);
-            o = fmaf(__ldcg(base + cc * (2 + HD) + 2 + tid), w, o);
+    float M = m0;
+    for (int cc = lane + 32; cc < nsplit; cc += 32) M = fmaxf(M, __ldcg(base + (size_t)cc * PS));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float w0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M);
+    float L = l0 * w0;
+    for (int cc = lane + 32; cc < nsplit; cc += 32) {
+        const float mc = __ldcg(base + (size_t)cc * PS), lc = __ldcg(base + (size_t)cc * PS + 1);
+        L = fmaf(lc, mc == -INFINITY ? 0.f : exp2f(mc - M), L);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+
+    float a0 = 0.f, a1 = 0.f;
+    for (int cb = 0; cb < nsplit; cb += 32) {
+        float w = w0;
+        if (cb > 0) {
+            const int cc = cb + lane;
+            const float mc = cc < nsplit ? __ldcg(base + (size_t)cc * PS) : -INFINITY;
+            w = mc == -INFINITY ? 0.f : exp2f(mc - M);
         }
-        store_ctx(out, out_bf16, dst + tid, L > 0.f ? o / L : 0.f);
+        const int nb = min(32, nsplit - cb);
+#pragma unroll 8
+        for (int k = 0; k < nb; k++) {
+            const float wk = __shfl_sync(0xffffffffu, w, k);
+            const float2 a = __ldcg(reinterpret_cast<const float2*>(base + (size_t)(cb + k) * PS + 2) + lane);
+            a0 = fmaf(a.x, wk, a0);
+            a1 = fmaf(a.y, wk, a1);
+        }
     }
-    if (tid == 0) sc.counters[(size_t)z * H + h] = 0;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const size_t dst = ((size_t)layer * n + item) * H * HD + h * HD + 2 * lane;
+    store_ctx(out, out_bf16, dst, a0 * inv);
+    store_ctx(out, out_bf16, dst + 1, a1 * inv);
 }
 
 // ---------------------------------------------------------------- small rings (capacity <= 32)
@@ -563,11 +613,23 @@ static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, in
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = overlap_previous ? 1 : 0;
-    if (append)
-        return cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride, out, ob,
-                                  decode_prefetch_distance(s.max_splits), n);
-    return cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride, out, ob,
-                              decode_prefetch_distance(s.max_splits), n);
+    const int pf = decode_prefetch_distance(s.max_splits);
+    cudaError_t e = append ? cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride,
+                                                out, ob, pf, n)
+                           : cudaLaunchKernelEx(&cfg, decode_kernel<T, false>, r, s, streams, positions, q, q_stride,
+                                                out, ob, pf, n);
+    if (e != cudaSuccess || s.max_splits <= 1) return e;
+    // the split-K combine, always a programmatic dependent of the decode launch
+    cudaLaunchConfig_t fcfg = {};
+    fcfg.gridDim = dim3((r.heads + 3) / 4, n * layers);
+    fcfg.blockDim = dim3(128);
+    fcfg.stream = st;
+    cudaLaunchAttribute fattr[1];
+    fattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    fattr[0].val.programmaticStreamSerializationAllowed = 1;
+    fcfg.attrs = fattr;
+    fcfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&fcfg, fold_kernel, r, s, streams, positions, out, ob, DecodeShape<T>::ROWS, n);
 }
 
 cudaError_t launch_decode(int dtype, bool append, const RingView& r, const Scratch& s, int n,

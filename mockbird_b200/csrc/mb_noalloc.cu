@@ -1,7 +1,7 @@
 // mb_append_attend_noalloc: the fused decode (append + RoPE + split-K attention)
 // for callers that cannot allocate device memory.  The caller owns the ring, the
-// RoPE table, the inputs, the outputs and a status word; the split-K partials and
-// ticket counters live in one fixed device array defined in this file.
+// RoPE table, the inputs, the outputs and a status word; the split-K partials
+// live in one fixed device array defined in this file.
 #include <mutex>
 
 #include "mb_internal.cuh"
@@ -56,12 +56,12 @@ extern "C" MB_API int mb_append_attend_noalloc(const mb_ring_ref* ring, int32_t 
         mis(positions, 4))
         return MB_ERR_ARG;
 
-    // scratch needed by this call: partials, then counters
+    // scratch needed by this call: the split-K partials (written by the decode
+    // kernel and read back by its combine kernel within the call)
     const int rows = mb::chunk_rows(ring->dtype);
     const int max_splits = (ring->capacity + rows - 1) / rows;
     const size_t part_bytes = round256((size_t)n * ring->heads * max_splits * (2 + mb::HD) * sizeof(float));
-    const size_t cnt_bytes = round256((size_t)n * ring->heads * sizeof(int32_t));
-    if (part_bytes + cnt_bytes > MB_NOALLOC_SCRATCH_BYTES) return MB_ERR_ARG;
+    if (part_bytes > MB_NOALLOC_SCRATCH_BYTES) return MB_ERR_ARG;
 
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return MB_ERR_CUDA;
@@ -71,7 +71,7 @@ extern "C" MB_API int mb_append_attend_noalloc(const mb_ring_ref* ring, int32_t 
 
     mb::Scratch sc;
     sc.part = static_cast<float*>(base);
-    sc.counters = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(base) + part_bytes);
+    sc.counters = nullptr;  // the per-chunk decode kernel takes no tickets
     sc.max_splits = max_splits;
 
     mb::RingView v;
@@ -92,9 +92,8 @@ extern "C" MB_API int mb_append_attend_noalloc(const mb_ring_ref* ring, int32_t 
     v.wait_probe = 0;
 
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    // the array keeps the previous call's contents: the tickets must start at zero
-    if (cudaMemsetAsync(sc.counters, 0, (size_t)n * ring->heads * sizeof(int32_t), st) != cudaSuccess)
-        return MB_ERR_CUDA;
+    // the array keeps the previous call's contents; every partial the combine
+    // reads is written by this call's decode kernel first, so nothing is cleared
     if (mb::launch_decode(ring->dtype, true, v, sc, n, streams, positions, qkv, 3 * ring->heads * mb::HD, out, st) !=
         cudaSuccess)
         return MB_ERR_CUDA;
