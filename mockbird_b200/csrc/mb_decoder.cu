@@ -103,7 +103,7 @@ const CUtensorMap* operand_map(mb_decoder* d, const void* base, int k, int rows,
 }  // namespace
 
 int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, const float* bias, void* y, int ldy,
-         int epi, cudaStream_t st) {
+         int epi, cudaStream_t st, const RingView* ring, const int32_t* streams, const int32_t* positions) {
     const auto pkey = std::make_tuple(M, N, K, epi);
     auto pit = d->gemm_plans.find(pkey);
     if (pit == d->gemm_plans.end()) pit = d->gemm_plans.emplace(pkey, mb::gemm::choose(M, N, K, epi)).first;
@@ -115,6 +115,9 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, cons
     a.M = M, a.N = N, a.K = K, a.splits = p.splits;
     a.bias = bias, a.y = y, a.ldy = ldy;
     a.err = d->ctx->d_err;
+    a.ring = ring ? *ring : RingView{};
+    a.streams = streams, a.positions = positions;
+    a.ring_dtype = d->ctx->cfg.dtype;
     // a programmatic dependent of the kernel before it (the GEMM loads its first
     // weight tiles while that kernel finishes)
     const cudaError_t e = mb::gemm::launch(*ta, *tb, a, p, epi, st, true);
@@ -123,7 +126,7 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, cons
 }
 
 int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
-        cudaStream_t st, bool ln1_ready) {
+        cudaStream_t st, bool ln1_ready, bool qkv_append) {
     mb_ctx* c = d->ctx;
     const int h = d->hid, f = d->ffn;
     int rc = MB_OK;
@@ -132,10 +135,18 @@ int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, 
         const auto& W = d->L[l];
         if (!(l == 0 && ln1_ready) && (e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess)
             break;
-        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, 3 * h, mb::gemm::EPI_STORE, st))) break;
-        // the context rows go straight to the bf16 input of the c_proj GEMM
-        if ((e = mb::launch_decode(c->cfg.dtype, true, mb::ring_view(c, l), c->scratch, n, streams, positions, d->qkv,
-                                   3 * h, d->xb, st, false, true)) != cudaSuccess)
+        // QKV with RoPE and the ring append in the GEMM's epilogue (the roped q
+        // rows land in d->qkv, the new K/V rows in the ring), or q|k|v stored
+        const RingView rv = mb::ring_view(c, l);
+        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, 3 * h,
+                       qkv_append ? mb::gemm::EPI_QKV_RING : mb::gemm::EPI_STORE, st, &rv, streams, positions)))
+            break;
+        // attention over each window, the new row included (appended here when
+        // the GEMM did not); launched without programmatic overlap, since its ring
+        // reads start at entry.  The context rows go straight to the bf16 input of
+        // the c_proj GEMM
+        if ((e = mb::launch_decode(c->cfg.dtype, !qkv_append, rv, c->scratch, n, streams, positions, d->qkv, 3 * h,
+                                   d->xb, st, false, true)) != cudaSuccess)
             break;
         if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, h, mb::gemm::EPI_ACCUM, st))) break;
         if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, d->xb, n, h, st)) != cudaSuccess) break;

@@ -56,8 +56,10 @@ uint16_t f32_to_bf16_bits(float f);
 // bf16 [M][ldy] after GELU(tanh).  x and Wt must be buffers whose tensor maps
 // this decoder may cache: x one of its own activation buffers (max_batch rows),
 // Wt a weight matrix it owns.
+// EPI_QKV_RING also takes the layer's ring and the rows' stream ids and positions.
 int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, const float* bias, void* y, int ldy,
-         int epi, cudaStream_t st);
+         int epi, cudaStream_t st, const RingView* ring = nullptr, const int32_t* streams = nullptr,
+         const int32_t* positions = nullptr);
 
 // W [K][N] fp32 (host, row-major) -> W^T [N][K] as bf16 bits, the layout the GEMM reads.
 void transpose_to_bf16(const float* w, int K, int N, uint16_t* out);
@@ -66,9 +68,14 @@ void transpose_to_bf16(const float* w, int K, int N, uint16_t* out);
 // [n][hid] (bf16) when it is non-null, else into `hidden` in place (fp32).
 // ln1_ready: the caller has already written layer 0's LN1 of `hidden` into
 // d->xb (bf16), so that LayerNorm is skipped.
+// qkv_append: RoPE and the ring append run in the QKV GEMM's epilogue
+// (EPI_QKV_RING) and the decode kernel only attends; otherwise the GEMM stores
+// q|k|v and the decode kernel ropes and appends (the local head: its GEMMs are
+// latency-bound, and the epilogue's position and RoPE-table loads cost it more
+// than the separate append does, 279k against 295k frames/s).
 // Arguments are the caller's to check; the current device must be the context's.
 int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
-        cudaStream_t st, bool ln1_ready = false);
+        cudaStream_t st, bool ln1_ready = false, bool qkv_append = true);
 
 // ---- LayerNorm of one row by one warp (LAYERNORM_1: mean, then the mean squared
 // deviation, out = (x - mean) * rsqrt(var + 1e-5) * w + b), width = 32 * PER.

@@ -138,7 +138,35 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 template <int EPI>
 __device__ __forceinline__ void finish4(const Args& a, int m, int n, float4 v, float4 b) {
     v.x += b.x, v.y += b.y, v.z += b.z, v.w += b.w;
-    if constexpr (EPI == EPI_GELU_BF16) {
+    if constexpr (EPI == EPI_QKV_RING) {
+        const RingView& r = a.ring;
+        const int hid = r.heads * HD, part = n / hid, w = n - part * hid;  // part 0 q, 1 k, 2 v
+        const int s = a.streams[m], pos = a.positions[m];
+        const bool ok = s >= 0 && s < r.streams && pos >= 0 && pos < r.max_position && (r.wrap || pos < r.capacity);
+        if (part < 2 && ok) {  // the two RoPE pairs of dims w .. w + 3 (the same arithmetic as the decode kernel)
+            const float2* cs = r.rope + (size_t)pos * 32 + ((w & (HD - 1)) >> 1);
+            const float2 lo = rope_pair(make_float2(v.x, v.y), cs[0]), hi = rope_pair(make_float2(v.z, v.w), cs[1]);
+            v = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+        if (part == 0) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + (size_t)m * a.ldy + n) = v;
+        } else if (ok) {
+            const int head = w / HD, slot = pos % r.capacity;
+            const size_t off = (((size_t)s * 2 + (part - 1)) * r.heads + head) * (size_t)r.capacity * HD +
+                               (size_t)slot * HD + (w & (HD - 1));
+            if (a.ring_dtype == MB_F32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(r.kv) + off) = v;
+            } else if (a.ring_dtype == MB_BF16) {
+                *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(r.kv) + off) =
+                    make_uint2(bf16x2(v.x, v.y), bf16x2(v.z, v.w));
+            } else {
+                const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+                *reinterpret_cast<uint2*>(static_cast<__half*>(r.kv) + off) =
+                    make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+            }
+        }
+        if (n == 0 && ok) r.slot_pos[(size_t)s * r.capacity + pos % r.capacity] = pos;
+    } else if constexpr (EPI == EPI_GELU_BF16) {
         *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy + n) =
             make_uint2(bf16x2(gelu_tanh(v.x), gelu_tanh(v.y)), bf16x2(gelu_tanh(v.z), gelu_tanh(v.w)));
     } else {
@@ -584,6 +612,7 @@ cudaError_t launch_pair_bn(const CUtensorMap& ta, const CUtensorMap& tb, const A
         case EPI_STORE: return launch_pair_t<BN, EPI_STORE>(ta, tb, a, st, pdl);
         case EPI_ACCUM: return launch_pair_t<BN, EPI_ACCUM>(ta, tb, a, st, pdl);
         case EPI_GELU_BF16: return launch_pair_t<BN, EPI_GELU_BF16>(ta, tb, a, st, pdl);
+        case EPI_QKV_RING: return launch_pair_t<BN, EPI_QKV_RING>(ta, tb, a, st, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -672,6 +701,7 @@ int active_clusters_bn(int epi, int splits) {
     switch (epi) {
         case EPI_STORE: return active_clusters<BN, EPI_STORE>(splits);
         case EPI_ACCUM: return active_clusters<BN, EPI_ACCUM>(splits);
+        case EPI_QKV_RING: return active_clusters<BN, EPI_QKV_RING>(splits);
         default: return active_clusters<BN, EPI_GELU_BF16>(splits);
     }
 }
@@ -688,6 +718,7 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Args& 
         case EPI_STORE: return launch_t<BN, EPI_STORE>(ta, tb, a, st, pdl);
         case EPI_ACCUM: return launch_t<BN, EPI_ACCUM>(ta, tb, a, st, pdl);
         case EPI_GELU_BF16: return launch_t<BN, EPI_GELU_BF16>(ta, tb, a, st, pdl);
+        case EPI_QKV_RING: return launch_t<BN, EPI_QKV_RING>(ta, tb, a, st, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "mb_internal.cuh"
+
 namespace mb {
 namespace gemm {
 
@@ -19,6 +21,13 @@ enum Epi : int {
     EPI_STORE = 0,      // y (fp32)  = acc + bias
     EPI_ACCUM = 1,      // y (fp32) += acc + bias      (the residual add of c_proj / fc_out)
     EPI_GELU_BF16 = 2,  // y (bf16)  = gelu_tanh(acc + bias)   (fc_in, GELU_TANH)
+    // The QKV projection of a decode step with RoPE and the ring append in its
+    // epilogue: the q columns [0, hid) are roped at the row's position and stored
+    // fp32 at y (the decode kernel's query input); the k columns are roped and,
+    // with the v columns, rounded to the ring's storage type and stored at slot
+    // position % capacity of the row's stream, whose slot position is recorded
+    // (ROPE_SPLIT_RING / ROPE_SPLIT_CODEC, kernels-decode.ts:216-241, 679-714).
+    EPI_QKV_RING = 3,
 };
 
 constexpr int BM = 128;  // rows (streams) per tile: the UMMA M, one TMEM lane per row
@@ -48,6 +57,14 @@ struct Args {
     void* y;               // fp32 [M][ldy] (EPI_STORE / EPI_ACCUM) or bf16 [M][ldy] (EPI_GELU_BF16)
     int ldy;
     int* err;              // device status word: DERR_TIMEOUT is OR-ed in when a bounded wait gives up
+    // EPI_QKV_RING only: the layer's ring (its kv, slot_pos and rope), the row's
+    // stream id and position, and the ring's storage type (MB_F32 / MB_BF16 /
+    // MB_F16).  A row whose stream or position the ring rejects appends nothing
+    // (the decode kernel that follows flags it).
+    RingView ring;
+    const int32_t* streams;
+    const int32_t* positions;
+    int ring_dtype;
 };
 
 // Tensor map of a K-major bf16 matrix [rows][k] (rows k*2 bytes apart, 16-byte

@@ -279,7 +279,7 @@ int enqueue_frame(mb_local_head* lh, int n, bool want_logits, cudaStream_t st) {
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return lfail(lh, MB_ERR_CUDA, std::string("local head: ") + cudaGetErrorString(e));
         int rc = mb::dec::run(lh->dec, n, lh->ids, lh->pos + (size_t)step * lh->max_batch, lh->x,
-                              step == 0 ? nullptr : lh->hb, st, /*ln1_ready=*/true);
+                              step == 0 ? nullptr : lh->hb, st, /*ln1_ready=*/true, /*qkv_append=*/false);
         if (rc) return rc;
         if (step == 0) {
             local_decide_kernel<<<wblocks, 32 * warps, 0, st>>>(n, h, lh->x, lh->cols, lh->cont);

@@ -29,7 +29,7 @@ def _weights(layers, h, ffn, seed):
     return w
 
 
-@pytest.mark.parametrize("dtype,layers,ffn", [("bf16", 2, 3072), ("f32", 1, 1024)])
+@pytest.mark.parametrize("dtype,layers,ffn", [("bf16", 2, 3072), ("f32", 1, 1024), ("f16", 1, 1024)])
 def test_decoder_step_matches_oracle(dtype, layers, ffn):
     h, S, C = 768, 5, 256
     w = _weights(layers, h, ffn, seed=layers)
@@ -47,6 +47,18 @@ def test_decoder_step_matches_oracle(dtype, layers, ffn):
         worst = max(worst, max_err(got, ref))
     ring.sync()
     assert worst < TOL, worst
+    # the K/V rows that the QKV GEMM's epilogue roped and appended: the windows
+    # hold the same positions in the same order as the oracle's ring, and the rows
+    # agree within the step's tolerance (the GEMM sums in another order)
+    for layer in range(layers):
+        for i, s in enumerate(order):
+            k, v, slots = ring.gather(layer, s, 39 + 7 * i)
+            ok, ov, oslots = orc.gather(layer, s, 39 + 7 * i)
+            assert np.array_equal(slots.cpu().numpy(), oslots), (layer, s)
+            for got_rows, want_bits in ((k, ok), (v, ov)):
+                want = {"f32": lambda b: b, "bf16": lambda b: (b.astype(np.uint32) << 16).view(np.float32),
+                        "f16": lambda b: b.view(np.float16).astype(np.float32)}[dtype](want_bits)
+                assert np.abs(got_rows.float().cpu().numpy() - want).max() < TOL, (layer, s)
 
 
 def test_decoder_rejects_bad_weights():
