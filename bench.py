@@ -77,11 +77,11 @@ def window_bytes(L, esize, layers=12):
 
 # DRAM read + write per launch over the algorithmic bytes, from the full ncu capture
 # of the fp32 decode kernel (one launch over all 12 layers of 8 streams, full
-# 512-slot windows: 303.06 MB read + 6.68 MB written, mean of 2 launches, for
+# 512-slot windows: 303.05 MB read + 6.28 MB written, mean of 2 launches, for
 # 303.76 MB algorithmic; profiles/decode_kernel_f32_config2.md).  Traffic grows
 # with the streams and the window, so a launch's traffic is its algorithmic bytes
 # times this ratio.
-DECODE_TRAFFIC_RATIO = {"f32": (303.06 + 6.68) / 303.76}
+DECODE_TRAFFIC_RATIO = {"f32": (303.05 + 6.28) / 303.76}
 # slots per split-K chunk of the decode kernel (16 KB of K per chunk); windows longer
 # than one chunk are combined by a second kernel launched behind the decode launch
 DECODE_CHUNK_ROWS = {"f32": 64, "bf16": 128, "f16": 128}
