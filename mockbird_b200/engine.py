@@ -50,9 +50,14 @@ class MockbirdError(RuntimeError):
 def _ptr(t) -> ctypes.c_void_p:
     if isinstance(t, torch.Tensor):
         return ctypes.c_void_p(t.data_ptr())
-    if isinstance(t, np.ndarray):
-        return t.ctypes.data_as(ctypes.c_void_p)
+    if isinstance(t, np.ndarray):  # the buffer address, without building a ctypes view of the array
+        return ctypes.c_void_p(t.__array_interface__["data"][0])
     raise TypeError(f"expected a torch tensor or numpy array, got {type(t).__name__}")
+
+
+# The raw handle of a device's current CUDA stream: torch's C accessor where
+# this torch has it (no Stream object per call), else the public API.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
 _TORCH_DTYPE = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
@@ -111,6 +116,8 @@ class KvRing:
 
     def _stream(self, stream) -> ctypes.c_void_p:
         if stream is None:
+            if _raw_stream is not None:
+                return ctypes.c_void_p(_raw_stream(self.device.index))
             stream = torch.cuda.current_stream(self.device)
         return ctypes.c_void_p(stream.cuda_stream if isinstance(stream, torch.cuda.Stream) else int(stream))
 
