@@ -906,11 +906,16 @@ def main():
                     help="config 2 profiling variant: begin at this position with full windows pre-written "
                          "(steady state, no resets) instead of the 1500-frame job")
     ap.add_argument("--streams", type=int, default=None, help="override streams per GPU (small profiling cases)")
+    ap.add_argument("--ring-dtype", default=None, choices=["f32", "bf16", "f16"],
+                    help="override the ring's storage type (e.g. config 3 on an fp32 ring)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.streams:
         cfg["streams"] = args.streams
         cfg["workload"] += f" [profiling case: {args.streams} streams/GPU]"
+    if args.ring_dtype and args.ring_dtype != cfg["dtype"]:
+        cfg["workload"] += f" [ring storage {args.ring_dtype} instead of {cfg['dtype']}]"
+        cfg["dtype"] = args.ring_dtype
     if args.start is not None:
         if cfg["job_steps"] is None or args.start < cfg["capacity"]:
             ap.error("--start applies to config 2 with a position >= capacity")

@@ -131,11 +131,16 @@ int persist_part_stride(int dtype, int capacity);  // split-K partial slots per 
 cudaError_t launch_decode_persist(int dtype, bool append, const RingView& r, const Scratch& s, int n,
                                   const int32_t* streams, const int32_t* positions, const float* q, int q_stride,
                                   float* out, cudaStream_t st);
+// stage: prefill_stage_bytes(dtype, n, heads, rows) bytes of device memory (none for 16-bit rings)
 cudaError_t launch_prefill(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
-                           const float* qkv, float* out, void* q_stage, cudaStream_t st);
+                           const float* qkv, float* out, void* stage, cudaStream_t st);
 size_t prefill_stage_bytes(int dtype, int n, int heads, int rows);
 cudaError_t launch_prefill_attn_tc(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
                                    const float* qkv, float* out, cudaStream_t st);
+// fp32 rings: the attention over the bf16 hi/lo parts of Q, K and V that the
+// RoPE/cache kernel wrote to `stage` ([6][n][heads][rows][64]).
+cudaError_t launch_prefill_attn_split(const RingView& r, int n, const int32_t* streams, int rows, const void* stage,
+                                      float* out, cudaStream_t st);
 cudaError_t launch_gather(int dtype, const RingView& r, int stream, int position, void* k_out, void* v_out,
                           int32_t* slots_out, cudaStream_t st);
 cudaError_t launch_ring_write(int dtype, const RingView& r, int stream, int first, int count, const void* k,

@@ -57,16 +57,31 @@ __device__ __forceinline__ void st4(T* p, float2 a, float2 b) {
 // ROPE_SPLIT_CACHE for all rows of n items: grid (ceil(rows / ROPE_ROWS), n),
 // heads * 16 threads, each owning 4 consecutive dims (two RoPE pairs) of one head
 // in ROPE_ROWS consecutive rows: 16-byte loads of q, k, v and the (cos, sin) pairs.
-// K roped and V raw go to slot = row.  For fp32 rings the roped Q goes to the
-// stage [n][heads][rows][64]; for 16-bit rings q_stage is null and the
-// tensor-core attention kernel ropes Q itself as it loads it.  Block 0 of an item
-// also marks the item's slots >= rows empty: a prefill starts an utterance at
+// K roped and V raw go to slot = row.  For fp32 rings the roped Q, the roped K
+// and V also go, each as two bf16 parts (hi = bf16(x), lo = bf16(x - hi)), to
+// the stage [6][n][heads][rows][64] (Q hi, Q lo, K hi, K lo, V hi, V lo) that
+// the tensor-core attention kernel loads; for 16-bit rings `split` is null and
+// the attention kernel ropes Q itself as it loads it.  Block 0 of an item also
+// marks the item's slots >= rows empty: a prefill starts an utterance at
 // position 0.
 constexpr int ROPE_ROWS = 4;
 
+// Four consecutive values as bf16 parts: hi = bf16(x), lo = bf16(x - hi).
+__device__ __forceinline__ void split4(float2 a, float2 b, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(b.x, b.y);
+    const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+    const __nv_bfloat162 l0 = __floats2bfloat162_rn(a.x - f0.x, a.y - f0.y);
+    const __nv_bfloat162 l1 = __floats2bfloat162_rn(b.x - f1.x, b.y - f1.y);
+    *reinterpret_cast<uint2*>(hi) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+    *reinterpret_cast<uint2*>(lo) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(1024) prefill_rope_kernel(RingView r, const int32_t* __restrict__ streams, int rows,
-                                                            const float* __restrict__ qkv, T* q_stage) {
+                                                            const float* __restrict__ qkv,
+                                                            __nv_bfloat16* __restrict__ split) {
     // the attention kernel that follows may start its Q prologue now; it reads
     // what this kernel writes only after this grid has completed
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -81,214 +96,58 @@ __global__ void __launch_bounds__(1024) prefill_rope_kernel(RingView r, const in
     const int rend = min(r0 + ROPE_ROWS, rows);
     T* kbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD + d4;
     T* vbase = reinterpret_cast<T*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD + d4;
-    T* qbase = q_stage ? q_stage + ((size_t)item * H + h) * rows * HD + d4 : nullptr;
+    // part p of this (item, head): plane p * n * H + item * H + h of the stage
+    const size_t plane = (size_t)rows * HD, pstride = (size_t)gridDim.y * H * plane;
+    __nv_bfloat16* sbase = sizeof(T) == 4 ? split + ((size_t)item * H + h) * plane + d4 : nullptr;
     for (int row = r0; row < rend; row++) {
         const float* src = qkv + ((size_t)item * rows + row) * 3 * HID + h * HD + d4;
         const float4 cs = *reinterpret_cast<const float4*>(r.rope + (size_t)row * 32 + d4 / 2);
         const float4 k = *reinterpret_cast<const float4*>(src + HID);
         const float4 v = *reinterpret_cast<const float4*>(src + 2 * HID);
         const float2 c0 = make_float2(cs.x, cs.y), c1 = make_float2(cs.z, cs.w);
-        if (q_stage) {
-            const float4 q = *reinterpret_cast<const float4*>(src);
-            st4(qbase + (size_t)row * HD, rope_pair(make_float2(q.x, q.y), c0), rope_pair(make_float2(q.z, q.w), c1));
-        }
-        st4(kbase + (size_t)row * HD, rope_pair(make_float2(k.x, k.y), c0), rope_pair(make_float2(k.z, k.w), c1));
+        const float2 k0 = rope_pair(make_float2(k.x, k.y), c0), k1 = rope_pair(make_float2(k.z, k.w), c1);
+        st4(kbase + (size_t)row * HD, k0, k1);
         st4(vbase + (size_t)row * HD, make_float2(v.x, v.y), make_float2(v.z, v.w));
+        if constexpr (sizeof(T) == 4) {  // only fp32 rings have a stage (16-bit rings keep 32 registers)
+            const float4 q = *reinterpret_cast<const float4*>(src);
+            __nv_bfloat16* o = sbase + (size_t)row * HD;
+            split4(rope_pair(make_float2(q.x, q.y), c0), rope_pair(make_float2(q.z, q.w), c1), o, o + pstride);
+            split4(k0, k1, o + 2 * pstride, o + 3 * pstride);
+            split4(make_float2(v.x, v.y), make_float2(v.z, v.w), o + 4 * pstride, o + 5 * pstride);
+        }
     }
     if (t < rend - r0) r.slot_pos[(size_t)s * C + r0 + t] = r0 + t;
     if (blockIdx.x == 0)
         for (int j = rows + t; j < C; j += blockDim.x) r.slot_pos[(size_t)s * C + j] = -1;
 }
 
-// Causal flash attention on CUDA cores for fp32 rings (kind::f16 tensor cores
-// take 16-bit operands, and tf32 would not meet the fp32 tolerance), blocked the
-// way a CUDA-core GEMM is: grid (ceil(rows/64), heads, n), 256 threads; thread
-// (tq, tk) = (t / 16, t % 16) owns a 4 x 4 block of the 64 x 64 score tile (query
-// rows 4tq.., key columns 4tk..) and a 4 x 4 block of the 64 x 64 output (query
-// rows 4tq.., dims 4tk..).  Q and K are staged transposed ([dim][row]) and V
-// as rows, so each dimension (key) step of QK^T (PV) is two 16-byte shared
-// loads and 16 FMAs.  Row maxima and sums reduce over the 16 threads of a
-// half-warp; P goes through shared memory transposed ([key][query]).
-namespace simt {
-constexpr int BQ = 64, BK = 64, LD = 68;  // tile rows; padded row length (floats)
-struct Smem {
-    float q[HD][LD];   // Q^T, pre-scaled by 0.125 * log2(e)
-    float k[HD][LD];   // K^T of the key tile
-    float v[BK][LD];   // V rows of the key tile
-    float p[BK][LD];   // P^T
-};
-}  // namespace simt
-
-__global__ void __launch_bounds__(256) prefill_attn_simt_kernel(RingView r, const int32_t* __restrict__ streams,
-                                                                int rows, const float* __restrict__ q_stage,
-                                                                float* __restrict__ out) {
-    using namespace simt;
-    extern __shared__ __align__(16) unsigned char simt_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>(simt_raw);
-    const int qt = blockIdx.x, h = blockIdx.y, item = blockIdx.z, t = threadIdx.x;
-    const int s = streams[item];
-    if (s < 0 || s >= r.streams) return;
-    const int H = r.heads, C = r.capacity, q0 = qt * BQ;
-    const int tq = t >> 4, tk = t & 15;
-    const float* qg = q_stage + ((size_t)item * H + h) * rows * HD;
-    const float* kb = reinterpret_cast<const float*>(r.kv) + (((size_t)s * 2 + 0) * H + h) * (size_t)C * HD;
-    const float* vb = reinterpret_cast<const float*>(r.kv) + (((size_t)s * 2 + 1) * H + h) * (size_t)C * HD;
-
-    // Q^T, scaled (rows past `rows` read as 0).  A warp covers 8 rows x 4 chunks
-    // of 16 bytes: 64-byte global segments, 2-way conflicts on the transposed stores.
-    for (int e = t; e < BQ * HD / 4; e += 256) {
-        const int row = ((e >> 5) & 7) * 8 + (e & 7), d = (((e >> 8) * 4) + ((e >> 3) & 3)) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q0 + row < rows) v = *reinterpret_cast<const float4*>(qg + (size_t)(q0 + row) * HD + d);
-        const float sc = SCALE * LOG2E;
-        sm.q[d][row] = v.x * sc;
-        sm.q[d + 1][row] = v.y * sc;
-        sm.q[d + 2][row] = v.z * sc;
-        sm.q[d + 3][row] = v.w * sc;
-    }
-    float o[4][4], m[4], l[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        m[i] = -INFINITY;
-        l[i] = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; j++) o[i][j] = 0.f;
-    }
-    const int last_key = min(rows, q0 + BQ);  // keys [0, last_key) are needed by this tile
-    for (int k0 = 0; k0 < last_key; k0 += BK) {
-        __syncthreads();  // the previous tile's K, V and P are consumed (and Q^T is written)
-        for (int e = t; e < BK * HD / 4; e += 256) {
-            const int j = ((e >> 5) & 7) * 8 + (e & 7), d = (((e >> 8) * 4) + ((e >> 3) & 3)) * 4;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (k0 + j < rows) {
-                kv = *reinterpret_cast<const float4*>(kb + (size_t)(k0 + j) * HD + d);
-                vv = *reinterpret_cast<const float4*>(vb + (size_t)(k0 + j) * HD + d);
-            }
-            sm.k[d][j] = kv.x;
-            sm.k[d + 1][j] = kv.y;
-            sm.k[d + 2][j] = kv.z;
-            sm.k[d + 3][j] = kv.w;
-            *reinterpret_cast<float4*>(&sm.v[j][d]) = vv;
-        }
-        __syncthreads();
-        // ---- S block: rows 4tq.., keys 4tk..
-        float sc[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
-#pragma unroll 8
-        for (int d = 0; d < HD; d++) {
-            const float4 qa = *reinterpret_cast<const float4*>(&sm.q[d][4 * tq]);
-            const float4 ka = *reinterpret_cast<const float4*>(&sm.k[d][4 * tk]);
-            const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {ka.x, ka.y, ka.z, ka.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) sc[i][j] = fmaf(qv[i], kv[j], sc[i][j]);
-        }
-        // ---- causal mask (key <= query, key < rows), row maxima over the half-warp
-        float mnew[4], corr[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int qi = q0 + 4 * tq + i;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int kj = k0 + 4 * tk + j;
-                if (kj > qi || kj >= rows) sc[i][j] = -INFINITY;
-                mx = fmaxf(mx, sc[i][j]);
-            }
-#pragma unroll
-            for (int o2 = 8; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
-            mnew[i] = fmaxf(m[i], mx);
-            // a row with nothing live yet keeps m = -inf: its p and corr stay 0
-            corr[i] = mnew[i] == -INFINITY ? 1.f : exp2f(m[i] - mnew[i]);
-        }
-        // ---- P = 2^(s - m), row sums, P^T to shared memory
-        float ps[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float sum = 0.f;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                ps[i][j] = sc[i][j] == -INFINITY ? 0.f : exp2f(sc[i][j] - mnew[i]);
-                sum += ps[i][j];
-            }
-#pragma unroll
-            for (int o2 = 8; o2 > 0; o2 >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
-            l[i] = l[i] * corr[i] + sum;
-            m[i] = mnew[i];
-#pragma unroll
-            for (int j = 0; j < 4; j++) o[i][j] *= corr[i];
-        }
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-            *reinterpret_cast<float4*>(&sm.p[4 * tk + j][4 * tq]) = make_float4(ps[0][j], ps[1][j], ps[2][j], ps[3][j]);
-        __syncthreads();
-        // ---- O block += P V: rows 4tq.., dims 4tk..
-        const int kend = min(BK, last_key - k0);
-#pragma unroll 8
-        for (int kk = 0; kk < kend; kk++) {
-            const float4 pa = *reinterpret_cast<const float4*>(&sm.p[kk][4 * tq]);
-            const float4 va = *reinterpret_cast<const float4*>(&sm.v[kk][4 * tk]);
-            const float pv[4] = {pa.x, pa.y, pa.z, pa.w}, vv[4] = {va.x, va.y, va.z, va.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) o[i][j] = fmaf(pv[i], vv[j], o[i][j]);
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int qi = q0 + 4 * tq + i;
-        if (qi < rows) {
-            const float inv = 1.f / l[i];
-            *reinterpret_cast<float4*>(out + ((size_t)item * rows + qi) * H * HD + h * HD + 4 * tk) =
-                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
-        }
-    }
-}
-
 size_t prefill_stage_bytes(int dtype, int n, int heads, int rows) {
-    return dtype == MB_F32 ? (size_t)n * heads * rows * HD * 4 : 0;  // 16-bit rings rope Q in the attention kernel
+    // fp32 rings: Q, K and V as bf16 hi/lo parts; 16-bit rings rope Q in the attention kernel
+    return dtype == MB_F32 ? (size_t)6 * n * heads * rows * HD * 2 : 0;
 }
 
 template <typename T>
 static cudaError_t prefill_t(const RingView& r, int n, const int32_t* streams, int rows, const float* qkv,
-                             float* out, void* q_stage, cudaStream_t st) {
+                             float* out, void* stage, cudaStream_t st) {
     if (r.heads * 16 > 1024) return cudaErrorInvalidConfiguration;
+    constexpr bool F32 = sizeof(T) == 4;
     prefill_rope_kernel<T><<<dim3((rows + ROPE_ROWS - 1) / ROPE_ROWS, n), r.heads * 16, 0, st>>>(
-        r, streams, rows, qkv, sizeof(T) == 4 ? reinterpret_cast<T*>(q_stage) : nullptr);
+        r, streams, rows, qkv, F32 ? static_cast<__nv_bfloat16*>(stage) : nullptr);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if constexpr (sizeof(T) == 2)  // 16-bit rings: tensor cores (mb_prefill_tc.cu), Q roped there
-        return launch_prefill_attn_tc(std::is_same<T, __nv_bfloat16>::value ? MB_BF16 : MB_F16, r, n, streams, rows,
-                                      qkv, out, st);
-    if constexpr (sizeof(T) == 4) {
-        static bool attr_set[64] = {};  // per device
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
-        if (e != cudaSuccess) return e;
-        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-        if (!attr_set[dev]) {
-            e = cudaFuncSetAttribute(prefill_attn_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)sizeof(simt::Smem));
-            if (e != cudaSuccess) return e;
-            attr_set[dev] = true;
-        }
-        prefill_attn_simt_kernel<<<dim3((rows + simt::BQ - 1) / simt::BQ, r.heads, n), 256, sizeof(simt::Smem), st>>>(
-            r, streams, rows, reinterpret_cast<const float*>(q_stage), out);
-    }
-    return cudaGetLastError();
+    if constexpr (F32)  // split bf16 parts on the tensor cores (mb_prefill_tc.cu)
+        return launch_prefill_attn_split(r, n, streams, rows, stage, out, st);
+    // 16-bit rings: tensor cores (mb_prefill_tc.cu), Q roped there
+    return launch_prefill_attn_tc(std::is_same<T, __nv_bfloat16>::value ? MB_BF16 : MB_F16, r, n, streams, rows,
+                                  qkv, out, st);
 }
 
 cudaError_t launch_prefill(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
-                           const float* qkv, float* out, void* q_stage, cudaStream_t st) {
+                           const float* qkv, float* out, void* stage, cudaStream_t st) {
     switch (dtype) {
-        case MB_F32: return prefill_t<float>(r, n, streams, rows, qkv, out, q_stage, st);
-        case MB_BF16: return prefill_t<__nv_bfloat16>(r, n, streams, rows, qkv, out, q_stage, st);
-        default: return prefill_t<__half>(r, n, streams, rows, qkv, out, q_stage, st);
+        case MB_F32: return prefill_t<float>(r, n, streams, rows, qkv, out, stage, st);
+        case MB_BF16: return prefill_t<__nv_bfloat16>(r, n, streams, rows, qkv, out, stage, st);
+        default: return prefill_t<__half>(r, n, streams, rows, qkv, out, stage, st);
     }
 }
 

@@ -435,12 +435,302 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
     return cudaLaunchKernelEx(&cfg, prefill_attn_tc_kernel<BF16>, (const float*)qkv, tkv, tout, r, streams, rows);
 }
 
+
+// ---------------------------------------------------------------- fp32 rings: split operands
+//
+// fp32 rings on the same tensor cores: every fp32 operand x is carried as two
+// bf16 parts, hi = bf16(x) and lo = bf16(x - hi), and each product as
+// hi*hi + hi*lo + lo*hi (the lo*lo term, ~2^-18 of the product, is dropped), all
+// accumulated in fp32 in TMEM: ~2^-17 relative error per product, against 2^-9
+// for plain bf16 operands.  The RoPE/cache kernel writes the parts of the roped
+// Q, the roped K and V into a stage [6][items][heads][rows][64] bf16 (Q hi, Q
+// lo, K hi, K lo, V hi, V lo) next to the fp32 ring, and this kernel loads them
+// by TMA.  The softmax splits P the same way.  Otherwise the kernel is the
+// 16-bit one above: one CTA = 128 queries of an (item, head), 64-key tiles, S
+// and O in TMEM, PV_j then S_{j+1} back to back on the tensor pipe; 12 MMAs per
+// product instead of 4, and twice the shared memory (two CTAs per SM).
+struct alignas(1024) X3Smem {
+    unsigned char qh[QTILE], ql[QTILE];   // Q parts
+    unsigned char ph[QTILE], pl[QTILE];   // P parts; at the end O (dims 0-31 over ph, 32-63 over pl)
+    unsigned char kh[KTILE], kl[KTILE];   // K_j parts
+    unsigned char vh[KTILE], vl[KTILE];   // V_j parts
+    uint64_t bar_q, bar_k, bar_v, bar_s, bar_o;
+    uint32_t tmem_base;
+};
+constexpr size_t X3_SMEM_BYTES = sizeof(X3Smem) + 1024;
+
+// Two products' worth of P parts: hi = bf16(p), lo = bf16(p - hi), packed in pairs.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// D (+)= A B over three part products: A_hi B_hi + A_hi B_lo + A_lo B_hi, K = 16
+// per instruction, `steps` instructions along K; A K-major, B K-major (S) or
+// MN-major (PV) with the given per-step offsets.
+__device__ __forceinline__ void umma_x3(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl, int steps,
+                                        uint32_t a_step, uint32_t b_step, uint32_t b_lbo, uint32_t idesc,
+                                        bool accumulate) {
+    for (int kk = 0; kk < steps; kk++) {
+        const uint64_t dah = sdesc_sw128(ah + a_step * kk, 16, 1024), dal = sdesc_sw128(al + a_step * kk, 16, 1024);
+        const uint64_t dbh = sdesc_sw128(bh + b_step * kk, b_lbo, 1024),
+                       dbl = sdesc_sw128(bl + b_step * kk, b_lbo, 1024);
+        umma_f16(d, dah, dbh, idesc, (accumulate || kk > 0) ? 1u : 0u);
+        umma_f16(d, dah, dbl, idesc, 1u);
+        umma_f16(d, dal, dbh, idesc, 1u);
+    }
+}
+
+__global__ void __launch_bounds__(NTHREADS, 2)
+    prefill_attn_x3_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
+                           const __grid_constant__ CUtensorMap tout, RingView r, const int32_t* __restrict__ streams,
+                           int rows) {
+    extern __shared__ unsigned char smem_raw[];
+    X3Smem& sm = *reinterpret_cast<X3Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (most key tiles) first
+    const int h = blockIdx.y, item = blockIdx.z, n = gridDim.z;
+    const int s = streams[item];
+    if (s < 0 || s >= r.streams) return;        // the RoPE/cache kernel has flagged it
+    const int H = r.heads, q0 = qt * BM;
+    const int ntiles = (min(q0 + BM, rows) + BN - 1) / BN;
+    // planes of the stage: part p of (item, head) is plane p * n * H + item * H + h
+    const int pq = item * H + h, np = n * H;
+
+    if (warp == 0) tmem_alloc(&sm.tmem_base, TMEM_COLS);
+    if (tid == 0) {
+        mbar_init(&sm.bar_q, 1);
+        mbar_init(&sm.bar_k, 1);
+        mbar_init(&sm.bar_v, 1);
+        mbar_init(&sm.bar_s, 1);
+        mbar_init(&sm.bar_o, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tq);
+        prefetch_tmap(&tkv);
+        prefetch_tmap(&tout);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = sm.tmem_base;
+
+    int k_issued = 1, k_done = 0, v_issued = 1, v_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
+    if (tid == 0) {
+        // a programmatic dependent of the RoPE/cache kernel, which writes the stage
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        mbar_expect_tx(&sm.bar_q, 2 * QTILE);
+        tma_load_3d(sm.qh, &tq, 0, q0, 0 * np + pq, &sm.bar_q);
+        tma_load_3d(sm.ql, &tq, 0, q0, 1 * np + pq, &sm.bar_q);
+        mbar_expect_tx(&sm.bar_k, 2 * KTILE);
+        tma_load_3d(sm.kh, &tkv, 0, 0, 2 * np + pq, &sm.bar_k);
+        tma_load_3d(sm.kl, &tkv, 0, 0, 3 * np + pq, &sm.bar_k);
+        mbar_expect_tx(&sm.bar_v, 2 * KTILE);
+        tma_load_3d(sm.vh, &tkv, 0, 0, 4 * np + pq, &sm.bar_v);
+        tma_load_3d(sm.vl, &tkv, 0, 0, 5 * np + pq, &sm.bar_v);
+    }
+
+    constexpr uint32_t IDESC_QK = idesc_f16(1u, 0u, BM, BN);
+    constexpr uint32_t IDESC_PV = idesc_f16(1u, 1u, BM, HD);
+    const float scale = SCALE * LOG2E;
+    const int row = tid, qg = q0 + row;
+    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    const uint32_t qha = smem_u32(sm.qh), qla = smem_u32(sm.ql), pha = smem_u32(sm.ph), pla = smem_u32(sm.pl);
+    const uint32_t kha = smem_u32(sm.kh), kla = smem_u32(sm.kl), vha = smem_u32(sm.vh), vla = smem_u32(sm.vl);
+
+    // S_0 = Q K_0^T
+    bool ok = __syncthreads_and(mbar_wait(&sm.bar_q, 0, WAIT_LIMIT) && mbar_wait(&sm.bar_k, 0, WAIT_LIMIT));
+    if (ok) {
+        k_done++;
+        if (tid == 0) {
+            tc_fence_after();
+            umma_x3(tbase + S_COL, qha, qla, kha, kla, HD / 16, 32, 32, 16, IDESC_QK, false);
+            umma_commit(&sm.bar_s);
+        }
+        s_issued++;
+    }
+    for (int j = 0; j < ntiles && ok; j++) {
+        const int k0 = j * BN;
+        const bool more = j + 1 < ntiles;
+        // ---- S_j landed: K_j is consumed, and so is V_{j-1} (PV_{j-1} was issued before S_j)
+        ok = __syncthreads_and(mbar_wait(&sm.bar_s, s_done & 1, WAIT_LIMIT));
+        if (!ok) break;
+        s_done++;
+        if (tid == 0) {
+            if (more) {
+                mbar_expect_tx(&sm.bar_k, 2 * KTILE);
+                tma_load_3d(sm.kh, &tkv, 0, k0 + BN, 2 * np + pq, &sm.bar_k);
+                tma_load_3d(sm.kl, &tkv, 0, k0 + BN, 3 * np + pq, &sm.bar_k);
+            }
+            if (j > 0) {
+                mbar_expect_tx(&sm.bar_v, 2 * KTILE);
+                tma_load_3d(sm.vh, &tkv, 0, k0, 4 * np + pq, &sm.bar_v);
+                tma_load_3d(sm.vl, &tkv, 0, k0, 5 * np + pq, &sm.bar_v);
+            }
+        }
+        if (more) k_issued++;
+        if (j > 0) v_issued++;
+        tc_fence_after();
+
+        // ---- this row's 64 scores (the 16-bit kernel's softmax, P split into parts)
+        float sv[64];
+        tmem_ld64(lane_addr + S_COL, sv);
+        const bool full = (k0 + BN <= q0) && (k0 + BN <= rows);
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        if (!full) {
+            const int lim = min(qg, rows - 1) - k0;
+#pragma unroll
+            for (int i = 0; i < 64; i++) sv[i] = i <= lim ? sv[i] : -INFINITY;
+        }
+#pragma unroll
+        for (int i = 0; i < 64; i += 4) {
+            mx0 = fmaxf(mx0, sv[i]);
+            mx1 = fmaxf(mx1, sv[i + 1]);
+            mx2 = fmaxf(mx2, sv[i + 2]);
+            mx3 = fmaxf(mx3, sv[i + 3]);
+        }
+        const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale;
+        const bool grow = m_tile > m_run + RESCALE_LOG2;
+        const float m_new = grow ? m_tile : m_run;
+        const float corr = grow ? ex2(m_run - m_new) : 1.f;
+        float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < 8; ch++) {
+            float pv[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) pv[e] = ex2(fmaf(sv[8 * ch + e], scale, -m_new));
+            ls0 += pv[0] + pv[4];
+            ls1 += pv[1] + pv[5];
+            ls2 += pv[2] + pv[6];
+            ls3 += pv[3] + pv[7];
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) split2(pv[2 * e], pv[2 * e + 1], hi[e], lo[e]);
+            *reinterpret_cast<uint4*>(swz(sm.ph, row, ch)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(swz(sm.pl, row, ch)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        l_run = l_run * corr + ((ls0 + ls1) + (ls2 + ls3));
+        m_run = m_new;
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+            float o[64];
+            tmem_ld64(lane_addr + O_COL, o);
+#pragma unroll
+            for (int i = 0; i < 64; i++) o[i] *= corr;
+            tmem_st64(lane_addr + O_COL, o);
+        }
+        fence_async_smem();
+        tc_fence_before();
+
+        // ---- O += P_j V_j, then S_{j+1} = Q K_{j+1}^T behind it
+        ok = __syncthreads_and(mbar_wait(&sm.bar_v, v_done & 1, WAIT_LIMIT) &&
+                               (!more || mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT)));
+        if (!ok) break;
+        v_done++;
+        if (more) k_done++;
+        if (tid == 0) {
+            tc_fence_after();
+            umma_x3(tbase + O_COL, pha, pla, vha, vla, BN / 16, 32, 2048, KTILE, IDESC_PV, j > 0);
+            if (more) {
+                umma_x3(tbase + S_COL, qha, qla, kha, kla, HD / 16, 32, 32, 16, IDESC_QK, false);
+                umma_commit(&sm.bar_s);
+            } else {
+                umma_commit(&sm.bar_o);
+            }
+        }
+        if (more)
+            s_issued++;
+        else
+            o_issued++;
+    }
+    if (ok) {
+        ok = __syncthreads_and(mbar_wait(&sm.bar_o, 0, WAIT_LIMIT));
+        if (ok) o_done++;
+    }
+
+    if (ok) {
+        // normalise, stage O (dims 0-31 over ph, 32-63 over pl, 128-byte
+        // swizzled) and write it with two TMA tile stores
+        tc_fence_after();
+        float o[64];
+        tmem_ld64(lane_addr + O_COL, o);
+        const float inv = 1.f / l_run;
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+            *reinterpret_cast<float4*>(swz(sm.ph, row, c)) =
+                make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+            *reinterpret_cast<float4*>(swz(sm.pl, row, c)) =
+                make_float4(o[32 + 4 * c] * inv, o[33 + 4 * c] * inv, o[34 + 4 * c] * inv, o[35 + 4 * c] * inv);
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tma_store_3d(&tout, sm.ph, h * HD, q0, item);
+            tma_store_3d(&tout, sm.pl, h * HD + 32, q0, item);
+            bulk_store_drain();
+        }
+    } else if (tid == 0) {
+        atomicOr(r.err, DERR_TIMEOUT);
+        if (!mbar_wait(&sm.bar_q, 0, WAIT_LIMIT)) {}
+        for (; k_done < k_issued; k_done++) mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT);
+        for (; v_done < v_issued; v_done++) mbar_wait(&sm.bar_v, v_done & 1, WAIT_LIMIT);
+        for (; s_done < s_issued; s_done++) mbar_wait(&sm.bar_s, s_done & 1, WAIT_LIMIT);
+        for (; o_done < o_issued; o_done++) mbar_wait(&sm.bar_o, o_done & 1, WAIT_LIMIT);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_free(tbase, TMEM_COLS);
+    }
+}
+
+cudaError_t launch_x3(const RingView& r, int n, const int32_t* streams, int rows, const void* stage, float* out,
+                      cudaStream_t st) {
+    CUtensorMap tq, tkv, tout;
+    const int planes = 6 * n * r.heads;
+    const size_t pstride = (size_t)rows * HD * 2;
+    if (!make_map(&tq, true, stage, rows, planes, pstride, BM) ||
+        !make_map(&tkv, true, stage, rows, planes, pstride, BN) || !make_out_map(&tout, out, rows, n, r.heads * HD))
+        return cudaErrorInvalidValue;
+    static bool attr_set[64] = {};  // per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(prefill_attn_x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)X3_SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows + BM - 1) / BM, r.heads, n);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = X3_SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_attn_x3_kernel, tq, tkv, tout, r, streams, rows);
+}
+
 }  // namespace
 
 cudaError_t launch_prefill_attn_tc(int dtype, const RingView& r, int n, const int32_t* streams, int rows,
                                      const float* qkv, float* out, cudaStream_t st) {
     return dtype == MB_BF16 ? launch_tc<true>(r, n, streams, rows, qkv, out, st)
                             : launch_tc<false>(r, n, streams, rows, qkv, out, st);
+}
+
+cudaError_t launch_prefill_attn_split(const RingView& r, int n, const int32_t* streams, int rows, const void* stage,
+                                      float* out, cudaStream_t st) {
+    return launch_x3(r, n, streams, rows, stage, out, st);
 }
 
 }  // namespace mb

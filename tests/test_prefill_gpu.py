@@ -30,10 +30,11 @@ def test_prefill_f32_195_rows():
         assert_window_equal(ring, orc, 0, s, 0, s, 194)
 
 
-@pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_prefill_16bit_444_rows(dtype):
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
+def test_prefill_444_rows(dtype):
     """BASELINE config 3's shape: 188-frame prompt + 256 text = 444 positions,
-    q/k/v ~ N(0, 0.5), 16-bit storage with fp32 accumulation, ring capacity 2048."""
+    q/k/v ~ N(0, 0.5), 16-bit storage with fp32 accumulation (and the fp32 ring,
+    attended over bf16 hi/lo operand parts), ring capacity 2048."""
     ring, orc, out, ref = _prefill_both(dtype, [3, 0, 2], 444, 2048, 4, seed=12, scale=0.5)
     ring.sync()
     assert max_err(out, ref) < TOL[dtype]
@@ -45,7 +46,7 @@ def test_prefill_16bit_444_rows(dtype):
 @pytest.mark.parametrize("rows", [1, 2, 63, 64, 65, 128, 257])
 def test_prefill_row_edges(rows, dtype):
     """Tile edges of both attention kernels: 128-query / 64-key tiles on tensor
-    cores (16-bit rings), 64 x 64 tiles on CUDA cores (fp32 rings)."""
+    cores (16-bit rings; the fp32 ring over bf16 hi/lo operand parts)."""
     ring, orc, out, ref = _prefill_both(dtype, [0], rows, 300, 1, seed=rows, scale=0.5)
     ring.sync()
     assert max_err(out, ref) < TOL[dtype]
@@ -104,7 +105,7 @@ def test_prefill_errors():
     ring.sync()
 
 
-@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
 def test_prefill_rising_scores_rescale_every_tile(dtype):
     """Scores that rise along the keys, so that every row's running maximum jumps
     by more than 2^8 (log2 units) on every 64-key tile: the tensor-core kernel
@@ -124,7 +125,7 @@ def test_prefill_rising_scores_rescale_every_tile(dtype):
         qkv[0, :, HID + h * 64 + 62: HID + h * 64 + 64] = (0.1 * np.arange(rows))[:, None]  # k
     qkv[0, :, 2 * HID:] = rng.standard_normal((rows, HID)).astype(np.float32)      # v
     out = ring.prefill(0, [0], torch.from_numpy(qkv).to(DEV))
-    ref, _ = orc.prefill(0, [0], qkv, q_round=True)
+    ref, _ = orc.prefill(0, [0], qkv, q_round=(dtype != "f32"))
     ring.sync()
     assert max_err(out, ref) < TOL[dtype]
     assert_window_equal(ring, orc, 0, 0, 0, 0, rows - 1)
