@@ -121,16 +121,17 @@ MB_API int mb_attend(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* strea
                      const int32_t* positions, const float* q, int32_t q_stride, float* out,
                      void* cuda_stream);
 
-/* The hot path: mb_rope_append followed by mb_attend in ONE launch
- * (decode.ts:527-552 for n streams at once).  qkv is read-only here (the
- * roped Q stays on chip); out: device f32 [n][heads*64]. */
+/* The hot path: mb_rope_append followed by mb_attend in ONE decode launch
+ * (decode.ts:527-552 for n streams at once), plus a small combine launch behind
+ * it when windows exceed one split-K chunk (64 fp32 / 128 16-bit slots).  qkv
+ * is read-only here (the roped Q stays on chip); out: device f32 [n][heads*64]. */
 MB_API int mb_append_attend(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* streams,
                             const int32_t* positions, const float* qkv, float* out,
                             void* cuda_stream);
 
 /* mb_append_attend for every layer of one decode step: the layer loop of
- * DecodeRunner.globalStep (decode.ts:735-748), all layers in ONE launch (they
- * touch disjoint rings).
+ * DecodeRunner.globalStep (decode.ts:735-748), all layers in ONE decode launch
+ * (they touch disjoint rings) and one combine launch.
  * qkv: device f32 [layers][n][3*heads*64]; out: device f32 [layers][n][heads*64]. */
 MB_API int mb_decode_step(mb_ctx* ctx, int32_t n, const int32_t* streams, const int32_t* positions,
                           const float* qkv, float* out, void* cuda_stream);
