@@ -70,6 +70,14 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// One normalised context row (64 fp32) from registers to global memory.
+__device__ __forceinline__ void store_row(float* dst, const float* o, float inv) {
+#pragma unroll
+    for (int c = 0; c < 16; c++)
+        reinterpret_cast<float4*>(dst)[c] =
+            make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+}
+
 // 128-byte-swizzled row of 128 B: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
 __device__ __forceinline__ unsigned char* swz(unsigned char* base, int r, int c) {
     return base + r * 128 + ((c ^ (r & 7)) << 4);
@@ -487,7 +495,7 @@ __device__ __forceinline__ void umma_x3(uint32_t d, uint32_t ah, uint32_t al, ui
 __global__ void __launch_bounds__(NTHREADS, 2)
     prefill_attn_x3_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
                            const __grid_constant__ CUtensorMap tout, RingView r, const int32_t* __restrict__ streams,
-                           int rows) {
+                           int rows, float* __restrict__ out) {
     extern __shared__ unsigned char smem_raw[];
     X3Smem& sm = *reinterpret_cast<X3Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -495,8 +503,13 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     const int h = blockIdx.y, item = blockIdx.z, n = gridDim.z;
     const int s = streams[item];
     if (s < 0 || s >= r.streams) return;        // the RoPE/cache kernel has flagged it
-    const int H = r.heads, q0 = qt * BM;
-    const int ntiles = (min(q0 + BM, rows) + BN - 1) / BN;
+    // Query tiles are laid out from the end: tile qt > 0 covers rows [q0, q0 + 128)
+    // ending at `rows`, and tile 0 the remainder [0, q_end), so the partial tile
+    // is the one with the fewest keys (444 rows: 1 + 3 + 5 + 7 key tiles, not
+    // 2 + 4 + 6 + 7 with the partial tile last; 3-4 % faster here)
+    const int first = rows - (gridDim.x - 1) * BM;  // rows of tile 0: 1..128
+    const int H = r.heads, q0 = qt == 0 ? 0 : first + (qt - 1) * BM, q_end = qt == 0 ? first : q0 + BM;
+    const int ntiles = (q_end + BN - 1) / BN;
     // planes of the stage: part p of (item, head) is plane p * n * H + item * H + h
     const int pq = item * H + h, np = n * H;
 
@@ -650,7 +663,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         if (ok) o_done++;
     }
 
-    if (ok) {
+    if (ok && q_end - q0 < BM) {
+        tc_fence_after();
+        float o[64];
+        tmem_ld64(lane_addr + O_COL, o);
+        if (row < q_end - q0) store_row(out + ((size_t)item * rows + q0 + row) * H * HD + h * HD, o, 1.f / l_run);
+    } else if (ok) {
         // normalise, stage O (dims 0-31 over ph, 32-63 over pl, 128-byte
         // swizzled) and write it with two TMA tile stores
         tc_fence_after();
@@ -717,7 +735,7 @@ cudaError_t launch_x3(const RingView& r, int n, const int32_t* streams, int rows
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_attn_x3_kernel, tq, tkv, tout, r, streams, rows);
+    return cudaLaunchKernelEx(&cfg, prefill_attn_x3_kernel, tq, tkv, tout, r, streams, rows, out);
 }
 
 }  // namespace

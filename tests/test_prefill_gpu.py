@@ -43,10 +43,12 @@ def test_prefill_444_rows(dtype):
 
 
 @pytest.mark.parametrize("dtype", ["f16", "f32"])
-@pytest.mark.parametrize("rows", [1, 2, 63, 64, 65, 128, 257])
+@pytest.mark.parametrize("rows", [1, 2, 63, 64, 65, 128, 191, 257, 300])
 def test_prefill_row_edges(rows, dtype):
     """Tile edges of both attention kernels: 128-query / 64-key tiles on tensor
-    cores (16-bit rings; the fp32 ring over bf16 hi/lo operand parts)."""
+    cores (16-bit rings; the fp32 ring over bf16 hi/lo operand parts).  Query
+    tiles are laid out from the last row back, so the partial tile is the first
+    (rows 191, 257 and 300 leave 63, 1 and 44 rows in it)."""
     ring, orc, out, ref = _prefill_both(dtype, [0], rows, 300, 1, seed=rows, scale=0.5)
     ring.sync()
     assert max_err(out, ref) < TOL[dtype]
