@@ -355,6 +355,35 @@ def run_ours(args, cfg, rank, world, device):
                "steps": K, "api": "mb_decode_step_host (C ABI, pinned host buffers, blocking per step)"
                + ("; the same K sampled job positions, wall clock per call, L2 flushed before each" if sampled
                   else "")}
+        if sampled:
+            # The engine's own call shape as well: DecodeRunner.runLayer hands one
+            # layer's qkv rows to the KV path at a time, so a frame is 12 blocking
+            # host-array calls (mb_append_attend_host), the same K job positions.
+            ring.reset()
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize(device)
+            lay_s, k = 0.0, 0
+            for t in range(J):
+                if k < K and t == timed[k]:
+                    flush.zero_()
+                    stream.synchronize()
+                    t0 = time.perf_counter()
+                    for layer in range(L):
+                        ring.append_attend_host(layer, ids, pos_host[t], host_qkv[t % sets][layer],
+                                                host_out[layer])
+                    lay_s += time.perf_counter() - t0
+                    k += 1
+                else:
+                    step(t)
+            torch.cuda.synchronize(device)
+            lay_s = max_over_ranks(lay_s, device if dist else None)
+            e2e["per_layer_calls"] = {
+                "value": round(world * n * K / lay_s, 1), "unit": "frames/s",
+                "h2d_bytes_per_step": int(L * (n * QKV * 4 + 2 * n * 4)), "d2h_bytes_per_step": int(L * n * HID * 4),
+                "api": "12 x mb_append_attend_host per frame (one blocking host-array call per layer, the shape "
+                       "of DecodeRunner.runLayer), the same K sampled job positions, wall clock, L2 flushed "
+                       "before each frame"}
     clk = clocks.stop()
 
     value = world * n * K / (ms_max / 1e3)
