@@ -42,6 +42,18 @@ def test_prefill_444_rows(dtype):
         assert_window_equal(ring, orc, 0, s, 0, s, 443)
 
 
+def test_prefill_config3_full_batch():
+    """BASELINE config 3 at its batch: 32 streams x 444 rows in one call (1 536
+    attention CTAs, several waves of them), fp16 ring of 2048 slots, q/k/v ~
+    N(0, 0.5); every context row against the oracle, windows bit-exact for a
+    sample of streams."""
+    ring, orc, out, ref = _prefill_both("f16", list(range(32)), 444, 2048, 32, seed=33, scale=0.5)
+    ring.sync()
+    assert max_err(out, ref) < TOL["f16"]
+    for s in (0, 17, 31):
+        assert_window_equal(ring, orc, 0, s, 0, s, 443)
+
+
 @pytest.mark.parametrize("dtype", ["f16", "f32"])
 @pytest.mark.parametrize("rows", [1, 2, 63, 64, 65, 128, 191, 257, 300])
 def test_prefill_row_edges(rows, dtype):
