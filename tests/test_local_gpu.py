@@ -272,3 +272,29 @@ def test_local_frame_host_arrays_match_device_arrays(graph, monkeypatch):
     assert np.array_equal(tok_a.cpu().numpy(), tok_b) and np.array_equal(cont_a.cpu().numpy(), cont_b)
     a.dispose()
     b.dispose()
+
+
+def test_local_frame_at_config6_batch():
+    """The local head at the bench's batch: 256 streams in one frame (16 audio
+    channels of 1024 codes, hidden 768, FFN 3072, graph replay), every logit row
+    against the oracle and every pick against the penalised argmax of the
+    kernel's own logits."""
+    h, ffn, codes, channels, penalty, S = HID, 3072, 1024, 16, 1.2, 256
+    w = local_weights(h, ffn, codes, channels, seed=12)
+    ring = KvRing(layers=1, heads=H, capacity=channels + 1, streams=S, dtype="f32", wrap=False,
+                  max_position=channels + 1)
+    head = LocalHead(ring, w, ffn, codes, channels, penalty)
+    orc = oracle.Ring(layers=1, streams=S, heads=H, capacity=channels + 1, dtype="f32", wrap=False,
+                      max_position=channels + 1)
+    order = list(np.random.default_rng(3).permutation(S))
+    seen = np.zeros((S, channels, codes // 32), np.uint32)
+    x = np.random.default_rng(4).standard_normal((S, h)).astype(np.float32)
+    tok, cont, lg = head.frame(order, torch.from_numpy(x).to(DEV), logits=True)
+    tok, lg = tok.cpu().numpy(), lg.cpu().numpy()
+    for i in range(S):
+        for ch in range(channels):
+            assert tok[i, ch] == oracle.argmax_penalty(lg[i, ch], seen[order[i], ch], penalty), (i, ch)
+    _, _, lg_o, _ = oracle.local_frame(orc, w, ffn, codes, channels, penalty, order, x, seen.copy(), forced=tok)
+    ring.sync()
+    assert float(np.abs(lg - lg_o).max()) < TOL_LOGIT
+    head.dispose()
