@@ -157,9 +157,12 @@ MB_API int mb_decode_step_host(mb_ctx* ctx, int32_t n, const int32_t* streams, c
  * dispatched at prefill.ts:424-462).  The item's slots >= rows are marked empty
  * first (a prefill starts an utterance).  qkv: device f32 [n][rows][3*heads*64]
  * (read-only), out: device f32 [n][rows][heads*64].  rows <= capacity.
- * fp32 rings also take a stream-ordered stage of 6 * n * heads * rows * 128
- * bytes (cudaMallocAsync on `cuda_stream`, freed behind the call): the bf16
- * hi/lo parts of Q, K and V that the tensor-core attention reads. */
+ * fp32 rings also use a stage of 6 * n * heads * rows * 128 bytes: the bf16
+ * hi/lo parts of Q, K and V that the tensor-core attention reads.  The context
+ * keeps it and grows it when a call needs more (a cudaFree / cudaMalloc pair,
+ * which synchronise the device; make the largest call first, outside any stream
+ * capture).  Like the decode scratch it is shared by the context's calls:
+ * prefill calls on one context run in order on one stream. */
 MB_API int mb_prefill(mb_ctx* ctx, int32_t layer, int32_t n, const int32_t* streams, int32_t rows,
                       const float* qkv, float* out, void* cuda_stream);
 

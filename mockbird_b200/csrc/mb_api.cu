@@ -239,7 +239,7 @@ MB_API int mb_destroy(mb_ctx* c) {
     {
         DeviceGuard g(c->cfg.device);
         void* ptrs[] = {c->kv, c->slot_pos, c->rope, c->d_err, c->scratch.part, c->scratch.counters,
-                        c->d_ids, c->d_qkv, c->d_out};
+                        c->d_ids, c->d_qkv, c->d_out, c->pf_stage};
         for (void* p : ptrs)
             if (p) cudaFree(p);
         for (auto* evs : {&c->ev_in, &c->ev_done})
@@ -516,13 +516,23 @@ MB_API int mb_prefill(mb_ctx* c, int32_t layer, int32_t n, const int32_t* stream
         return fail(c, MB_ERR_ARG, "null or misaligned device pointer");
     DeviceGuard g(c->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    void* stage = nullptr;
+    // fp32 rings: the stage is the context's own, grown when a call needs more
+    // (cudaFree then cudaMalloc, both synchronising the device, so no earlier
+    // call still uses the old one); it stays allocated for the next calls
     const size_t stage_bytes = prefill_stage_bytes(c->cfg.dtype, n, c->cfg.heads, rows);
-    if (stage_bytes) CK(cudaMallocAsync(&stage, stage_bytes, st), "prefill stage");
-    cudaError_t e = launch_prefill(c->cfg.dtype, ring_view(c, layer), n, streams, rows, qkv, out, stage, st);
-    cudaError_t e2 = stage ? cudaFreeAsync(stage, st) : cudaSuccess;
-    if (e != cudaSuccess) return cuda_fail(c, e, "prefill launch");
-    if (e2 != cudaSuccess) return cuda_fail(c, e2, "prefill stage free");
+    if (stage_bytes > c->pf_stage_bytes) {
+        if (c->pf_stage) CK(cudaFree(c->pf_stage), "prefill stage free");
+        c->pf_stage = nullptr;
+        c->pf_stage_bytes = 0;
+        if (cudaMalloc(&c->pf_stage, stage_bytes) != cudaSuccess) {
+            c->pf_stage = nullptr;
+            cudaGetLastError();
+            return fail(c, MB_ERR_OOM, "prefill stage of %zu bytes", stage_bytes);
+        }
+        c->pf_stage_bytes = stage_bytes;
+    }
+    CK(launch_prefill(c->cfg.dtype, ring_view(c, layer), n, streams, rows, qkv, out, c->pf_stage, st),
+       "prefill launch");
     return MB_OK;
 }
 

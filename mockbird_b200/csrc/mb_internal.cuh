@@ -65,6 +65,9 @@ struct mb_ctx {
     cudaEvent_t ev_ids = nullptr;  // recorded behind the copy out of h_ids
     float* d_qkv = nullptr;   // [layers][max_batch][3*H*64]
     float* d_out = nullptr;   // [layers][max_batch][H*64]
+    // mb_prefill's stage on fp32 rings (bf16 hi/lo parts of Q, K, V), grown on demand
+    void* pf_stage = nullptr;
+    size_t pf_stage_bytes = 0;
     // mb_decode_step_host's copy pipeline: inputs in and outputs out in groups of
     // layers on their own streams, so that the copies overlap the decode of others
     cudaStream_t cp_in = nullptr, cp_out = nullptr;

@@ -3,8 +3,13 @@
 // _APPLY passes of the reference (kernels-batch.ts:246-350) as one
 // flash-attention kernel.
 //
-// One CTA = 128 queries of one (item, head); 4 warps, thread t owns query row t,
-// which is also its TMEM lane.  The CTA reads its Q rows straight from the fp32
+// A work item = 128 queries of one (item, head); 4 warps, thread t owns query
+// row t, which is also its TMEM lane.  The grid is four CTAs per SM (at most one
+// per work item), each staying resident over several work items: they are
+// handed out longest first, round by round, in snake order across the CTAs, so
+// the CTAs' totals stay close, and the TMEM allocation, the barriers and the
+// tensor-map prefetch are paid once per CTA (5 % faster at config 3 than one CTA
+// per item, whose last wave ran part-empty).  The CTA reads its Q rows straight from the fp32
 // QKV input and ropes them itself (the RoPE/cache kernel writes only K and V),
 // so Q never makes a round trip through HBM.  TMEM holds S (64 columns) and the running O (64
 // columns): 128 columns, so four CTAs share an SM's 512, and 48 KB of shared
@@ -127,19 +132,23 @@ template <bool BF16>
 __global__ void __launch_bounds__(NTHREADS, 4)
     prefill_attn_tc_kernel(const float* __restrict__ qkv, const __grid_constant__ CUtensorMap tkv,
                              const __grid_constant__ CUtensorMap tout, RingView r,
-                             const int32_t* __restrict__ streams, int rows) {
+                             const int32_t* __restrict__ streams, int rows, int n, int qtiles) {
     extern __shared__ unsigned char smem_raw[];
     TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (most key tiles) first
-    const int h = blockIdx.y, item = blockIdx.z;
-    const int s = streams[item];
-    if (s < 0 || s >= r.streams) return;        // the RoPE/cache kernel has flagged it
+    const int H = r.heads;
+    // Work items: the query tiles of every (item, head), sorted longest first
+    // (item index w: tile qtiles - 1 - w / (heads * n)).  CTA b takes one item per
+    // round, in snake order (b in even rounds, G - 1 - b in odd ones), so the
+    // CTAs' totals stay close and none is left with a long tile at the end.
+    const int G = gridDim.x, W = qtiles * H * n;
+    auto work = [&](int rnd) { return rnd * G + ((rnd & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x); };
+    int w = work(0);  // < W: the grid is at most W CTAs
+    int qt = qtiles - 1 - w / (H * n), h = (w % (H * n)) % H, item = (w % (H * n)) / H;
+    int s = streams[item];
     // (query tiles from row 0: laid out from the last row back, as the fp32-ring
     // kernel below has them, this kernel measured 3 % slower)
-    const int H = r.heads, q0 = qt * BM;
-    const int ntiles = (min(q0 + BM, rows) + BN - 1) / BN;
-    const int kplane = (s * 2 + 0) * H + h, vplane = (s * 2 + 1) * H + h;
+    int q0 = qt * BM;
 
     // Q: the CTA's 128 rows come straight from the fp32 QKV input and are roped
     // here (position = row), with the cache kernel's rope_pair so they round
@@ -152,7 +161,9 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     const int HID = H * HD, lane = tid & 31, l16 = lane & 15;
     const float* qkv_row0 = qkv + (size_t)item * rows * 3 * HID + h * HD + 4 * l16;
     float4 qv[8], cs[8];
-    q_rows_load(qkv_row0, r.rope, q0 + warp * 32 + (lane >> 4), rows, l16, HID, qv, cs, 0);
+    // the first item's Q rows are requested into L2 before the setup (its loads,
+    // at the top of the item loop, then find them there)
+    q_rows_prefetch(qkv_row0, q0 + warp * 32 + (lane >> 4), rows, HID, 0);
     q_rows_prefetch(qkv_row0, q0 + warp * 32 + (lane >> 4), rows, HID, 8);
 
     if (warp == 0) tmem_alloc(&sm.tmem_base, TMEM_COLS);
@@ -170,26 +181,45 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     tc_fence_after();
     const uint32_t tbase = sm.tmem_base;
 
-    // issue/complete counts per barrier (identical in every thread: the control flow is uniform)
-    int k_issued = 1, k_done = 0, v_issued = 1, v_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
+    // issue/complete counts per barrier (identical in every thread: the control
+    // flow is uniform); they run on from one work item to the next
+    int k_issued = 0, k_done = 0, v_issued = 0, v_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
+    constexpr uint32_t IDESC_QK = idesc_f16(BF16 ? 1u : 0u, 0u, BM, BN);
+    constexpr uint32_t IDESC_PV = idesc_f16(BF16 ? 1u : 0u, 1u, BM, HD);
+    const float scale = SCALE * LOG2E;
+    const int row = tid;
+    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    bool ok = true;
+    for (int rnd = 0; ok; rnd++) {
+    if (rnd > 0) {
+        w = work(rnd);
+        if (w >= W) break;
+        qt = qtiles - 1 - w / (H * n), h = (w % (H * n)) % H, item = (w % (H * n)) / H;
+        s = streams[item];
+        q0 = qt * BM;
+        qkv_row0 = qkv + (size_t)item * rows * 3 * HID + h * HD + 4 * l16;
+    }
+    if (s < 0 || s >= r.streams) continue;  // the RoPE/cache kernel has flagged it
+    q_rows_load(qkv_row0, r.rope, q0 + warp * 32 + (lane >> 4), rows, l16, HID, qv, cs, 0);
+    q_rows_prefetch(qkv_row0, q0 + warp * 32 + (lane >> 4), rows, HID, 8);
+    const int ntiles = (min(q0 + BM, rows) + BN - 1) / BN;
+    const int kplane = (s * 2 + 0) * H + h, vplane = (s * 2 + 1) * H + h;
+    const int qg = q0 + row;
     if (tid == 0) {
-        // The kernel is a programmatic dependent of the RoPE/cache kernel: all of
-        // the above (Q loads, setup) may run during that kernel's tail, but the
-        // K/V it writes are read only after it has completed.  Thread 0 is the
-        // only thread that reads or writes global memory from here on (the K/V
-        // loads and the output stores are its TMA copies).
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        // The kernel is a programmatic dependent of the RoPE/cache kernel: the
+        // first item's Q loads and the setup may run during that kernel's tail,
+        // but the K/V it writes are read only after it has completed.  Thread 0
+        // is the only thread that reads or writes global memory between an
+        // item's Q load and its end (the K/V loads and the output stores are its
+        // TMA copies; it has let the previous item's stores read their staging).
+        if (rnd == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
         mbar_expect_tx(&sm.bar_k, KTILE);
         tma_load_3d(sm.k, &tkv, 0, 0, kplane, &sm.bar_k);
         mbar_expect_tx(&sm.bar_v, KTILE);
         tma_load_3d(sm.v, &tkv, 0, 0, vplane, &sm.bar_v);
     }
-
-    constexpr uint32_t IDESC_QK = idesc_f16(BF16 ? 1u : 0u, 0u, BM, BN);
-    constexpr uint32_t IDESC_PV = idesc_f16(BF16 ? 1u : 0u, 1u, BM, HD);
-    const float scale = SCALE * LOG2E;
-    const int row = tid, qg = q0 + row;
-    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    k_issued++;
+    v_issued++;
     float m_run = -INFINITY, l_run = 0.f;
 
     // Q: the first half of the rows roped and stored, then the second half
@@ -200,7 +230,7 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     fence_async_smem();  // the Q stores, seen by the tensor core
 
     // S_0 = Q K_0^T
-    bool ok = __syncthreads_and(mbar_wait(&sm.bar_k, 0, WAIT_LIMIT));
+    ok = __syncthreads_and(mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT));
     if (ok) {
         k_done++;
         if (tid == 0) {
@@ -326,7 +356,7 @@ __global__ void __launch_bounds__(NTHREADS, 4)
             o_issued++;
     }
     if (ok) {  // the last PV: O is final
-        ok = __syncthreads_and(mbar_wait(&sm.bar_o, 0, WAIT_LIMIT));
+        ok = __syncthreads_and(mbar_wait(&sm.bar_o, o_done & 1, WAIT_LIMIT));
         if (ok) o_done++;
     }
 
@@ -352,7 +382,9 @@ __global__ void __launch_bounds__(NTHREADS, 4)
             tma_store_3d(&tout, sm.k, h * HD + 32, q0, item);
             bulk_store_drain();
         }
-    } else if (tid == 0) {
+    }
+    }  // work items
+    if (!ok && tid == 0) {
         // gave up: record it, then let everything in flight land before the
         // shared memory and TMEM of this CTA are released
         atomicOr(r.err, DERR_TIMEOUT);
@@ -431,9 +463,14 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
+    // four CTAs per SM (the TMEM limit), each over several query tiles
+    static int sms[64] = {};  // per device
+    if (!sms[dev] && (e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    const int qtiles = (rows + BM - 1) / BM, work = qtiles * r.heads * n;
     // programmatic dependent of the RoPE/cache kernel launched just before it
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((rows + BM - 1) / BM, r.heads, n);
+    cfg.gridDim = dim3(work < 4 * sms[dev] ? work : 4 * sms[dev]);
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = SMEM_BYTES;
     cfg.stream = st;
@@ -442,7 +479,8 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_attn_tc_kernel<BF16>, (const float*)qkv, tkv, tout, r, streams, rows);
+    return cudaLaunchKernelEx(&cfg, prefill_attn_tc_kernel<BF16>, (const float*)qkv, tkv, tout, r, streams, rows, n,
+                              qtiles);
 }
 
 
