@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(NTHREADS, 4)
     const float scale = SCALE * LOG2E;
     const int row = tid;
     const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
-    bool ok = true;
+    bool ok = true, waited = false;  // waited: thread 0 has passed griddepcontrol.wait
     for (int rnd = 0; ok; rnd++) {
     if (rnd > 0) {
         w = work(rnd);
@@ -212,7 +212,8 @@ __global__ void __launch_bounds__(NTHREADS, 4)
         // is the only thread that reads or writes global memory between an
         // item's Q load and its end (the K/V loads and the output stores are its
         // TMA copies; it has let the previous item's stores read their staging).
-        if (rnd == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+        waited = true;
         mbar_expect_tx(&sm.bar_k, KTILE);
         tma_load_3d(sm.k, &tkv, 0, 0, kplane, &sm.bar_k);
         mbar_expect_tx(&sm.bar_v, KTILE);
@@ -496,7 +497,8 @@ cudaError_t launch_tc(const RingView& r, int n, const int32_t* streams, int rows
 // by TMA.  The softmax splits P the same way.  Otherwise the kernel is the
 // 16-bit one above: one CTA = 128 queries of an (item, head), 64-key tiles, S
 // and O in TMEM, PV_j then S_{j+1} back to back on the tensor pipe; 12 MMAs per
-// product instead of 4, and twice the shared memory (two CTAs per SM).
+// product instead of 4, and twice the shared memory (two CTAs per SM, each
+// resident over several work items as in the 16-bit kernel).
 struct alignas(1024) X3Smem {
     unsigned char qh[QTILE], ql[QTILE];   // Q parts
     unsigned char ph[QTILE], pl[QTILE];   // P parts; at the end O (dims 0-31 over ph, 32-63 over pl)
@@ -535,23 +537,19 @@ __device__ __forceinline__ void umma_x3(uint32_t d, uint32_t ah, uint32_t al, ui
 __global__ void __launch_bounds__(NTHREADS, 2)
     prefill_attn_x3_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
                            const __grid_constant__ CUtensorMap tout, RingView r, const int32_t* __restrict__ streams,
-                           int rows, float* __restrict__ out) {
+                           int rows, float* __restrict__ out, int n, int qtiles) {
     extern __shared__ unsigned char smem_raw[];
     X3Smem& sm = *reinterpret_cast<X3Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (most key tiles) first
-    const int h = blockIdx.y, item = blockIdx.z, n = gridDim.z;
-    const int s = streams[item];
-    if (s < 0 || s >= r.streams) return;        // the RoPE/cache kernel has flagged it
+    const int H = r.heads, np = n * H;
+    // persistent over the work items as the 16-bit kernel (longest first, snake order)
+    const int G = gridDim.x, W = qtiles * np;
+    auto work = [&](int rnd) { return rnd * G + ((rnd & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x); };
     // Query tiles are laid out from the end: tile qt > 0 covers rows [q0, q0 + 128)
     // ending at `rows`, and tile 0 the remainder [0, q_end), so the partial tile
     // is the one with the fewest keys (444 rows: 1 + 3 + 5 + 7 key tiles, not
     // 2 + 4 + 6 + 7 with the partial tile last; 3-4 % faster here)
-    const int first = rows - (gridDim.x - 1) * BM;  // rows of tile 0: 1..128
-    const int H = r.heads, q0 = qt == 0 ? 0 : first + (qt - 1) * BM, q_end = qt == 0 ? first : q0 + BM;
-    const int ntiles = (q_end + BN - 1) / BN;
-    // planes of the stage: part p of (item, head) is plane p * n * H + item * H + h
-    const int pq = item * H + h, np = n * H;
+    const int first = rows - (qtiles - 1) * BM;  // rows of tile 0: 1..128
 
     if (warp == 0) tmem_alloc(&sm.tmem_base, TMEM_COLS);
     if (tid == 0) {
@@ -570,10 +568,31 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     tc_fence_after();
     const uint32_t tbase = sm.tmem_base;
 
-    int k_issued = 1, k_done = 0, v_issued = 1, v_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
+    int q_issued = 0, q_done = 0, k_issued = 0, k_done = 0, v_issued = 0, v_done = 0, s_issued = 0, s_done = 0,
+        o_issued = 0, o_done = 0;
+    constexpr uint32_t IDESC_QK = idesc_f16(1u, 0u, BM, BN);
+    constexpr uint32_t IDESC_PV = idesc_f16(1u, 1u, BM, HD);
+    const float scale = SCALE * LOG2E;
+    const int row = tid;
+    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    const uint32_t qha = smem_u32(sm.qh), qla = smem_u32(sm.ql), pha = smem_u32(sm.ph), pla = smem_u32(sm.pl);
+    const uint32_t kha = smem_u32(sm.kh), kla = smem_u32(sm.kl), vha = smem_u32(sm.vh), vla = smem_u32(sm.vl);
+    bool ok = true, waited = false;  // waited: thread 0 has passed griddepcontrol.wait
+    for (int rnd = 0; ok; rnd++) {
+    const int w = work(rnd);
+    if (w >= W) break;
+    const int qt = qtiles - 1 - w / np, h = (w % np) % H, item = (w % np) / H;
+    const int s = streams[item];
+    if (s < 0 || s >= r.streams) continue;  // the RoPE/cache kernel has flagged it
+    const int q0 = qt == 0 ? 0 : first + (qt - 1) * BM, q_end = qt == 0 ? first : q0 + BM;
+    const int ntiles = (q_end + BN - 1) / BN;
+    // planes of the stage: part p of (item, head) is plane p * n * H + item * H + h
+    const int pq = item * H + h;
     if (tid == 0) {
-        // a programmatic dependent of the RoPE/cache kernel, which writes the stage
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        // a programmatic dependent of the RoPE/cache kernel, which writes the
+        // stage; the previous item's stores have read their staging (drained)
+        if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+        waited = true;
         mbar_expect_tx(&sm.bar_q, 2 * QTILE);
         tma_load_3d(sm.qh, &tq, 0, q0, 0 * np + pq, &sm.bar_q);
         tma_load_3d(sm.ql, &tq, 0, q0, 1 * np + pq, &sm.bar_q);
@@ -584,19 +603,17 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         tma_load_3d(sm.vh, &tkv, 0, 0, 4 * np + pq, &sm.bar_v);
         tma_load_3d(sm.vl, &tkv, 0, 0, 5 * np + pq, &sm.bar_v);
     }
-
-    constexpr uint32_t IDESC_QK = idesc_f16(1u, 0u, BM, BN);
-    constexpr uint32_t IDESC_PV = idesc_f16(1u, 1u, BM, HD);
-    const float scale = SCALE * LOG2E;
-    const int row = tid, qg = q0 + row;
-    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    q_issued++;
+    k_issued++;
+    v_issued++;
+    const int qg = q0 + row;
     float m_run = -INFINITY, l_run = 0.f;
-    const uint32_t qha = smem_u32(sm.qh), qla = smem_u32(sm.ql), pha = smem_u32(sm.ph), pla = smem_u32(sm.pl);
-    const uint32_t kha = smem_u32(sm.kh), kla = smem_u32(sm.kl), vha = smem_u32(sm.vh), vla = smem_u32(sm.vl);
 
     // S_0 = Q K_0^T
-    bool ok = __syncthreads_and(mbar_wait(&sm.bar_q, 0, WAIT_LIMIT) && mbar_wait(&sm.bar_k, 0, WAIT_LIMIT));
+    ok = __syncthreads_and(mbar_wait(&sm.bar_q, q_done & 1, WAIT_LIMIT) &&
+                           mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT));
     if (ok) {
+        q_done++;
         k_done++;
         if (tid == 0) {
             tc_fence_after();
@@ -699,7 +716,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             o_issued++;
     }
     if (ok) {
-        ok = __syncthreads_and(mbar_wait(&sm.bar_o, 0, WAIT_LIMIT));
+        ok = __syncthreads_and(mbar_wait(&sm.bar_o, o_done & 1, WAIT_LIMIT));
         if (ok) o_done++;
     }
 
@@ -730,9 +747,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             tma_store_3d(&tout, sm.pl, h * HD + 32, q0, item);
             bulk_store_drain();
         }
-    } else if (tid == 0) {
+        __syncthreads();  // the staging is free again before the next item's P parts
+    }
+    }  // work items
+    if (!ok && tid == 0) {
         atomicOr(r.err, DERR_TIMEOUT);
-        if (!mbar_wait(&sm.bar_q, 0, WAIT_LIMIT)) {}
+        for (; q_done < q_issued; q_done++) mbar_wait(&sm.bar_q, q_done & 1, WAIT_LIMIT);
         for (; k_done < k_issued; k_done++) mbar_wait(&sm.bar_k, k_done & 1, WAIT_LIMIT);
         for (; v_done < v_issued; v_done++) mbar_wait(&sm.bar_v, v_done & 1, WAIT_LIMIT);
         for (; s_done < s_issued; s_done++) mbar_wait(&sm.bar_s, s_done & 1, WAIT_LIMIT);
@@ -765,8 +785,13 @@ cudaError_t launch_x3(const RingView& r, int n, const int32_t* streams, int rows
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
+    // two CTAs per SM (the shared-memory limit), each over several query tiles
+    static int sms[64] = {};  // per device
+    if (!sms[dev] && (e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    const int qtiles = (rows + BM - 1) / BM, work = qtiles * r.heads * n;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((rows + BM - 1) / BM, r.heads, n);
+    cfg.gridDim = dim3(work < 2 * sms[dev] ? work : 2 * sms[dev]);
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = X3_SMEM_BYTES;
     cfg.stream = st;
@@ -775,7 +800,7 @@ cudaError_t launch_x3(const RingView& r, int n, const int32_t* streams, int rows
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_attn_x3_kernel, tq, tkv, tout, r, streams, rows, out);
+    return cudaLaunchKernelEx(&cfg, prefill_attn_x3_kernel, tq, tkv, tout, r, streams, rows, out, n, qtiles);
 }
 
 }  // namespace
