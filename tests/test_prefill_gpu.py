@@ -119,6 +119,28 @@ def test_prefill_errors():
     ring.sync()
 
 
+@pytest.mark.parametrize("dtype", ["f16", "f32"])
+def test_prefill_skips_rejected_items(dtype):
+    """A call whose first item names a stream the ring does not have: that item is
+    rejected on the device (MB_ERR_DEVICE at the next sync), and the other items
+    of the same call still match the oracle -- the persistent attention CTAs skip
+    the rejected item's query tiles (for some CTAs their first work item) and
+    carry on with the next ones."""
+    rows = 200
+    ring = KvRing(layers=1, streams=3, capacity=256, dtype=dtype, wrap=True)
+    orc = oracle.Ring(layers=1, streams=3, heads=H, capacity=256, dtype=dtype, wrap=True)
+    qkv = randn((3, rows, QKV), seed=41, scale=0.5)
+    ids = torch.tensor([7, 0, 2], dtype=torch.int32, device=DEV)  # no stream 7
+    out = ring.prefill(0, ids, torch.from_numpy(qkv).to(DEV))
+    with pytest.raises(MockbirdError) as e:
+        ring.sync()
+    assert e.value.status == "MB_ERR_DEVICE"
+    ref, _ = orc.prefill(0, [0, 2], qkv[1:], q_round=(dtype != "f32"))
+    assert max_err(out[1:], ref) < TOL[dtype]
+    for s in (0, 2):
+        assert_window_equal(ring, orc, 0, s, 0, s, rows - 1)
+
+
 @pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
 def test_prefill_rising_scores_rescale_every_tile(dtype):
     """Scores that rise along the keys, so that every row's running maximum jumps
