@@ -488,6 +488,15 @@ def run_prefill(args, cfg, rank, world, device):
     flops = prefill_flops(S, n, L) * args.steps
     tpeak, tkind = tensor_peak()
     achieved = flops / (ms / 1e3) / 1e12
+    # The step's compulsory HBM traffic per row and layer: q, k, v read (fp32),
+    # K and V written to the ring (storage type), the context written (fp32).  At
+    # config 3 that is ~218 MB per layer (~34 us at the measured copy bandwidth)
+    # against ~6 us of tensor work at the bf16 peak: the step is HBM-bound, and
+    # the tensor pipe's share is reported beside it.
+    es = _esize(cfg["dtype"])
+    hbm_bytes = float(n * S * L * (QKV * 4 + 2 * HID * es + HID * 4)) * args.steps
+    hpeak, hkind = peaks()
+    hbm_achieved = hbm_bytes / (ms / 1e3) / 1e9
     result = {
         "metric": "causal prefill attention TFLOP/s (config 3; RoPE+cache write and attention, all 12 layers)",
         "value": round(world * flops / (ms_max / 1e3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
@@ -497,11 +506,16 @@ def run_prefill(args, cfg, rank, world, device):
         "config": {"workload": cfg["workload"], "streams_per_gpu": n, "rows": S, "layers": L,
                    "l2": "inputs larger than L2: 1.57 GB of qkv per step",
                    "positions_per_s": round(world * n * S * args.steps / (ms_max / 1e3), 1)},
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tpeak, "unit": "TFLOP/s",
-                     "frac": round(achieved / tpeak, 4), "traffic": None,
-                     "peak_source": f"{tkind} bf16_tflops (burst)",
-                     "timing": "CUDA events over the whole prefill calls (RoPE/cache kernel + attention kernel); "
-                               "algorithmic FLOPs are the causal QK^T + PV only"},
+        "roofline": {"bound": "hbm", "achieved": round(hbm_achieved, 1), "peak": hpeak, "unit": "GB/s",
+                     "frac": round(hbm_achieved / hpeak, 4), "traffic": None,
+                     "peak_source": f"{hkind} hbm_gbs (MEASURED_PEAKS.json)",
+                     "algorithmic_bytes_per_step": hbm_bytes / args.steps,
+                     "bytes": "per row and layer: q, k, v read (fp32), K and V written to the ring, context written "
+                              "(fp32)",
+                     "tensor": {"achieved": round(achieved, 2), "peak": tpeak, "unit": "TFLOP/s",
+                                "frac": round(achieved / tpeak, 4), "peak_source": f"{tkind} bf16_tflops (burst)",
+                                "flops": "causal QK^T + PV only"},
+                     "timing": "CUDA events over the whole prefill calls (RoPE/cache kernel + attention kernel)"},
         "gpu_launches": 2 * L * args.steps, "clocks": clk, "e2e": None,
     }
     return result, ring
