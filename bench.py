@@ -720,6 +720,8 @@ def run_decoder(args, cfg, rank, world, device):
     n, L, C, F = cfg["streams"], cfg["layers"], cfg["capacity"], cfg["ffn"]
     ring = KvRing(layers=L, capacity=C, streams=n, dtype=cfg["dtype"], wrap=True, device=device.index)
     dec = Decoder(ring, decoder_weights(L, HID, F), F)
+    # the step's kernel chains: two half batches from 128 items up (MOCKBIRD_DECODER_SPLIT=0: one)
+    chains = 2 if n >= 128 and os.environ.get("MOCKBIRD_DECODER_SPLIT", "1") != "0" else 1
     pos0 = config4_positions(n * world, C)[rank * n:(rank + 1) * n].astype(np.int64)
 
     def fill():
@@ -814,11 +816,13 @@ def run_decoder(args, cfg, rank, world, device):
                 "h2d_bytes_per_step": n * HID * 4, "d2h_bytes_per_step": n * HID * 4,
                 "api": "mb_decoder_step_host (C ABI): the embedded rows from pinned host memory in, the ln_f rows "
                        "back to it, one synchronisation per step"},
-        "gpu_launches": K * (L * 8 + 1),
+        "gpu_launches": K * chains * (L * 8 + 1),
         "clocks": clk,
     }
     result["gpu_launches_note"] = ("8 of this library's kernels per layer (LN1, QKV GEMM, attention, its split-K "
-                                   "combine, c_proj GEMM, LN2, fc_in GEMM + GELU, fc_out GEMM) + ln_f")
+                                   "combine, c_proj GEMM, LN2, fc_in GEMM + GELU, fc_out GEMM) + ln_f, per "
+                                   f"half-batch chain ({chains} chain{'s' if chains > 1 else ''}: a step of >= 128 "
+                                   "items runs as two, on two CUDA streams)")
     dec.dispose()
     return result, ring
 

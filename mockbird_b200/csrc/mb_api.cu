@@ -335,6 +335,8 @@ MB_API int mb_decode_step(mb_ctx* c, int32_t n, const int32_t* streams, const in
 
 }  // extern "C"
 
+thread_local mb::LaunchPriority mb::launch_priority;
+
 // The status of device rejection bits read back (clearing them on the device).
 int mb::report_bits(mb_ctx* c, int32_t bits) {
     if (!bits) return MB_OK;

@@ -597,22 +597,22 @@ static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, in
     const int ob = out_bf16 ? 1 : 0;
     if (r.capacity <= 32) {  // a window fits one warp
         cfg.gridDim = dim3((r.heads + 3) / 4, n * layers);
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = overlap_previous ? 1 : 0;
+        cfg.numAttrs = with_priority(attr, overlap_previous ? 1 : 0, true);
         if (append)
             return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, true>, r, streams, positions, q, q_stride, out, ob,
                                       n);
         return cudaLaunchKernelEx(&cfg, decode_small_kernel<T, false>, r, streams, positions, q, q_stride, out, ob,
                                   n);
     }
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = overlap_previous ? 1 : 0;
+    cfg.numAttrs = with_priority(attr, overlap_previous ? 1 : 0, true);
     const int pf = decode_prefetch_distance(s.max_splits);
     cudaError_t e = append ? cudaLaunchKernelEx(&cfg, decode_kernel<T, true>, r, s, streams, positions, q, q_stride,
                                                 out, ob, pf, n)
@@ -624,11 +624,11 @@ static cudaError_t decode_t(bool append, const RingView& r, const Scratch& s, in
     fcfg.gridDim = dim3((r.heads + 3) / 4, n * layers);
     fcfg.blockDim = dim3(128);
     fcfg.stream = st;
-    cudaLaunchAttribute fattr[1];
+    cudaLaunchAttribute fattr[2];
     fattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     fattr[0].val.programmaticStreamSerializationAllowed = 1;
     fcfg.attrs = fattr;
-    fcfg.numAttrs = 1;
+    fcfg.numAttrs = with_priority(fattr, 1);
     return cudaLaunchKernelEx(&fcfg, fold_kernel, r, s, streams, positions, out, ob, DecodeShape<T>::ROWS, n);
 }
 

@@ -48,11 +48,11 @@ cudaError_t layernorm_t(const float* x, const float* w, const float* b, TO* y, i
     cfg.gridDim = dim3((rows + warps - 1) / warps);
     cfg.blockDim = dim3(32 * warps);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = mb::with_priority(attr, 1);
     return cudaLaunchKernelEx(&cfg, layernorm_rows<TO, PER>, x, w, b, y, rows, width);
 }
 
@@ -103,12 +103,14 @@ const CUtensorMap* operand_map(mb_decoder* d, const void* base, int k, int rows,
 }  // namespace
 
 int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, const float* bias, void* y, int ldy,
-         int epi, cudaStream_t st, const RingView* ring, const int32_t* streams, const int32_t* positions) {
+         int epi, cudaStream_t st, const RingView* ring, const int32_t* streams, const int32_t* positions,
+         int x_row0) {
     const auto pkey = std::make_tuple(M, N, K, epi);
     auto pit = d->gemm_plans.find(pkey);
     if (pit == d->gemm_plans.end()) pit = d->gemm_plans.emplace(pkey, mb::gemm::choose(M, N, K, epi)).first;
     const mb::gemm::Plan p = pit->second;
-    const CUtensorMap* ta = operand_map(d, x, K, d->ctx->cfg.max_batch, mb::gemm::a_box_rows(p), mb::gemm::box_kb(p));
+    const CUtensorMap* ta =
+        operand_map(d, x, K, d->ctx->cfg.max_batch - x_row0, mb::gemm::a_box_rows(p), mb::gemm::box_kb(p));
     const CUtensorMap* tb = operand_map(d, Wt, K, N, mb::gemm::b_box_rows(p), mb::gemm::box_kb(p));
     if (!ta || !tb) return fail(d, MB_ERR_CUDA, "decoder: GEMM tensor map encoding failed");
     mb::gemm::Args a;
@@ -125,33 +127,51 @@ int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, cons
     return MB_OK;
 }
 
-int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
-        cudaStream_t st, bool ln1_ready, bool qkv_append) {
+namespace {
+// The layers and ln_f for items [row0, row0 + n) of the step: `streams`,
+// `positions`, `hidden` and `lnf_bf16` already point at row row0; the
+// activation buffers and the split-K scratch are offset here.  after_qkv0, when
+// non-null, is recorded on `st` right after layer 0's QKV GEMM.
+int run_rows(mb_decoder* d, int row0, int n, const int32_t* streams, const int32_t* positions, float* hidden,
+             bf16* lnf_bf16, cudaStream_t st, bool ln1_ready, bool qkv_append, cudaEvent_t after_qkv0) {
     mb_ctx* c = d->ctx;
     const int h = d->hid, f = d->ffn;
+    bf16* xb = d->xb + (size_t)row0 * h;
+    float* qkv = d->qkv + (size_t)row0 * 3 * h;
+    bf16* h1 = d->h1 + (size_t)row0 * f;
+    Scratch sc = c->scratch;  // partials of these items only: [row0 + item][head][split]
+    sc.part += (size_t)row0 * c->cfg.heads * sc.max_splits * (2 + HD);
     int rc = MB_OK;
     cudaError_t e = cudaSuccess;
     for (int l = 0; l < d->layers && rc == MB_OK && e == cudaSuccess; l++) {
         const auto& W = d->L[l];
-        if (!(l == 0 && ln1_ready) && (e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, d->xb, n, h, st)) != cudaSuccess)
+        if (!(l == 0 && ln1_ready) && (e = layernorm<bf16>(hidden, W.ln1_w, W.ln1_b, xb, n, h, st)) != cudaSuccess)
             break;
         // QKV with RoPE and the ring append in the GEMM's epilogue (the roped q
-        // rows land in d->qkv, the new K/V rows in the ring), or q|k|v stored
+        // rows land in qkv, the new K/V rows in the ring), or q|k|v stored
         const RingView rv = mb::ring_view(c, l);
-        if ((rc = gemm(d, n, 3 * h, h, d->xb, W.w_attn, W.b_attn, d->qkv, 3 * h,
-                       qkv_append ? mb::gemm::EPI_QKV_RING : mb::gemm::EPI_STORE, st, &rv, streams, positions)))
+        if ((rc = gemm(d, n, 3 * h, h, xb, W.w_attn, W.b_attn, qkv, 3 * h,
+                       qkv_append ? mb::gemm::EPI_QKV_RING : mb::gemm::EPI_STORE, st, &rv, streams, positions,
+                       row0)))
             break;
+        if (l == 0 && after_qkv0 && (e = cudaEventRecord(after_qkv0, st)) != cudaSuccess) break;
         // attention over each window, the new row included (appended here when
         // the GEMM did not); launched without programmatic overlap, since its ring
         // reads start at entry.  The context rows go straight to the bf16 input of
         // the c_proj GEMM
-        if ((e = mb::launch_decode(c->cfg.dtype, !qkv_append, rv, c->scratch, n, streams, positions, d->qkv, 3 * h,
-                                   d->xb, st, false, true)) != cudaSuccess)
+        if ((e = mb::launch_decode(c->cfg.dtype, !qkv_append, rv, sc, n, streams, positions, qkv, 3 * h, xb, st,
+                                   false, true)) != cudaSuccess)
             break;
-        if ((rc = gemm(d, n, h, h, d->xb, W.w_proj, W.b_proj, hidden, h, mb::gemm::EPI_ACCUM, st))) break;
-        if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, d->xb, n, h, st)) != cudaSuccess) break;
-        if ((rc = gemm(d, n, f, h, d->xb, W.w_in, W.b_in, d->h1, f, mb::gemm::EPI_GELU_BF16, st))) break;
-        if ((rc = gemm(d, n, h, f, d->h1, W.w_out, W.b_out, hidden, h, mb::gemm::EPI_ACCUM, st))) break;
+        if ((rc = gemm(d, n, h, h, xb, W.w_proj, W.b_proj, hidden, h, mb::gemm::EPI_ACCUM, st, nullptr, nullptr,
+                       nullptr, row0)))
+            break;
+        if ((e = layernorm<bf16>(hidden, W.ln2_w, W.ln2_b, xb, n, h, st)) != cudaSuccess) break;
+        if ((rc = gemm(d, n, f, h, xb, W.w_in, W.b_in, h1, f, mb::gemm::EPI_GELU_BF16, st, nullptr, nullptr, nullptr,
+                       row0)))
+            break;
+        if ((rc = gemm(d, n, h, f, h1, W.w_out, W.b_out, hidden, h, mb::gemm::EPI_ACCUM, st, nullptr, nullptr,
+                       nullptr, row0)))
+            break;
         e = cudaGetLastError();
     }
     if (rc == MB_OK && e == cudaSuccess)
@@ -160,6 +180,38 @@ int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, 
     if (rc) return rc;
     if (e != cudaSuccess) return fail(d, MB_ERR_CUDA, std::string("decoder: ") + cudaGetErrorString(e));
     return MB_OK;
+}
+}  // namespace
+
+int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
+        cudaStream_t st, bool ln1_ready, bool qkv_append, bool split) {
+    const int n0 = n / 2;
+    if (!split || !d->split || !d->side || n0 < SPLIT_MIN_ROWS)
+        return run_rows(d, 0, n, streams, positions, hidden, lnf_bf16, st, ln1_ready, qkv_append, nullptr);
+    const int h = d->hid;
+    const mb::LaunchPriority saved = mb::launch_priority;
+    mb::launch_priority.set = true;
+    mb::launch_priority.value = d->prio_high;
+    mb::launch_priority.decode_value = d->prio_low;
+    int rc = MB_OK;
+    cudaError_t e = cudaEventRecord(d->ev_fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d->side, d->ev_fork, 0);
+    const bool forked = e == cudaSuccess;
+    if (!forked) rc = fail(d, MB_ERR_CUDA, std::string("decoder fork: ") + cudaGetErrorString(e));
+    if (rc == MB_OK)
+        rc = run_rows(d, 0, n0, streams, positions, hidden, lnf_bf16, st, ln1_ready, qkv_append, d->ev_stagger);
+    if (rc == MB_OK && (e = cudaStreamWaitEvent(d->side, d->ev_stagger, 0)) != cudaSuccess)
+        rc = fail(d, MB_ERR_CUDA, std::string("decoder fork: ") + cudaGetErrorString(e));
+    if (rc == MB_OK)
+        rc = run_rows(d, n0, n - n0, streams + n0, positions + n0, hidden + (size_t)n0 * h,
+                      lnf_bf16 ? lnf_bf16 + (size_t)n0 * h : nullptr, d->side, ln1_ready, qkv_append, nullptr);
+    if (forked) {  // the caller's stream ends behind both chains, whatever happened
+        e = cudaEventRecord(d->ev_join, d->side);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, d->ev_join, 0);
+        if (e != cudaSuccess && rc == MB_OK) rc = fail(d, MB_ERR_CUDA, std::string("decoder join: ") + cudaGetErrorString(e));
+    }
+    mb::launch_priority = saved;
+    return rc;
 }
 
 }  // namespace dec
@@ -181,6 +233,9 @@ MB_API int mb_decoder_destroy(mb_decoder* d) {
     cudaSetDevice(d->ctx->cfg.device);
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
     if (d->cap) cudaStreamDestroy(d->cap);
+    if (d->side) cudaStreamDestroy(d->side);
+    for (cudaEvent_t ev : {d->ev_fork, d->ev_stagger, d->ev_join})
+        if (ev) cudaEventDestroy(ev);
     void* ptrs[] = {d->wmem, d->xb, d->qkv, d->h1, d->g_streams, d->g_positions, d->g_hidden};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -269,11 +324,18 @@ MB_API int mb_decoder_create(mb_ctx* c, int32_t ffn, const float* w, size_t coun
         cudaMalloc(&d->g_positions, mb * 4) != cudaSuccess ||
         cudaMalloc(&d->g_hidden, mb * h * sizeof(float)) != cudaSuccess)
         return bail(MB_ERR_OOM, "decoder: activation allocation failed");
-    if (cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) != cudaSuccess)
+    if (cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&d->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d->ev_stagger, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d->ev_join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaDeviceGetStreamPriorityRange(&d->prio_low, &d->prio_high) != cudaSuccess)
         return bail(MB_ERR_CUDA, "decoder: stream creation failed");
     {
         const char* v = getenv("MOCKBIRD_DECODER_GRAPH");
         d->use_graph = !(v && strcmp(v, "0") == 0);
+        v = getenv("MOCKBIRD_DECODER_SPLIT");
+        d->split = !(v && strcmp(v, "0") == 0);
     }
     if (prev >= 0) cudaSetDevice(prev);
     *out = d;
@@ -290,22 +352,25 @@ namespace {
 // are loaded and tensor maps built outside any capture), after which the step is
 // captured, without running, for the next calls.
 int step_staged(mb_decoder* d, int n, cudaStream_t st) {
-    if (!d->use_graph) return mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st);
+    if (!d->use_graph)
+        return mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st, false, true, true);
     auto it = d->graphs.find(n);
     cudaError_t e;
     if (it != d->graphs.end()) {
         e = cudaGraphLaunch(it->second, st);
         return e == cudaSuccess ? MB_OK : mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder graph: ") + cudaGetErrorString(e));
     }
-    int rc = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st);
+    int rc = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, st, false, true, true);
     if (rc) return rc;
     cudaGraph_t g = nullptr;
     if ((e = cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
         return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
-    const int rc2 = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, d->cap);
+    const int rc2 = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, d->cap, false, true, true);
     e = cudaStreamEndCapture(d->cap, &g);
     cudaGraphExec_t ex = nullptr;
-    if (rc2 == MB_OK && e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+    // (a split step's kernel nodes carry the priorities they were launched with)
+    if (rc2 == MB_OK && e == cudaSuccess)
+        e = cudaGraphInstantiate(&ex, g, d->split ? cudaGraphInstantiateFlagUseNodePriority : 0);
     if (g) cudaGraphDestroy(g);
     if (rc2 != MB_OK) return rc2;
     if (e != cudaSuccess) return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
@@ -341,7 +406,7 @@ MB_API int mb_decoder_step(mb_decoder* d, int32_t n, const int32_t* streams, con
     DevGuard g(c->cfg.device);
     if (!g.ok) return MB_ERR_CUDA;
     cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
-    if (!d->use_graph) return mb::dec::run(d, n, streams, positions, hidden, nullptr, st);
+    if (!d->use_graph) return mb::dec::run(d, n, streams, positions, hidden, nullptr, st, false, true, true);
     // the captured step reads and writes this object's own buffers only
     const size_t hb = (size_t)n * d->hid * sizeof(float);
     cudaError_t e = cudaMemcpyAsync(d->g_streams, streams, n * 4, cudaMemcpyDeviceToDevice, st);

@@ -37,6 +37,14 @@ struct mb_decoder {
     int32_t *g_streams = nullptr, *g_positions = nullptr;  // [max_batch]
     float* g_hidden = nullptr;                              // [max_batch][hid]
     std::map<int, cudaGraphExec_t> graphs;
+    // A step of at least 2 * SPLIT_MIN_ROWS items runs as two half-batch chains:
+    // the second on `side`, forked from and joined to the caller's stream by
+    // events, started once the first has launched its layer-0 QKV GEMM
+    // (mb::dec::run).  MOCKBIRD_DECODER_SPLIT=0 keeps one chain.
+    bool split = true;
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_stagger = nullptr, ev_join = nullptr;
+    int prio_high = 0, prio_low = 0;  // the device's greatest and least stream priority
 };
 
 namespace mb {
@@ -57,9 +65,11 @@ uint16_t f32_to_bf16_bits(float f);
 // this decoder may cache: x one of its own activation buffers (max_batch rows),
 // Wt a weight matrix it owns.
 // EPI_QKV_RING also takes the layer's ring and the rows' stream ids and positions.
+// x_row0: x starts that many rows into its buffer (the tensor map then spans the
+// max_batch - x_row0 rows left in it).
 int gemm(mb_decoder* d, int M, int N, int K, const bf16* x, const bf16* Wt, const float* bias, void* y, int ldy,
          int epi, cudaStream_t st, const RingView* ring = nullptr, const int32_t* streams = nullptr,
-         const int32_t* positions = nullptr);
+         const int32_t* positions = nullptr, int x_row0 = 0);
 
 // W [K][N] fp32 (host, row-major) -> W^T [N][K] as bf16 bits, the layout the GEMM reads.
 void transpose_to_bf16(const float* w, int K, int N, uint16_t* out);
@@ -73,9 +83,17 @@ void transpose_to_bf16(const float* w, int K, int N, uint16_t* out);
 // q|k|v and the decode kernel ropes and appends (the local head: its GEMMs are
 // latency-bound, and the epilogue's position and RoPE-table loads cost it more
 // than the separate append does, 279k against 295k frames/s).
+// split: with d->split on and at least 2 * SPLIT_MIN_ROWS items, the items run as
+// two half-batch chains on `st` and d->side, the second started after the
+// first's layer-0 QKV GEMM, every GEMM, LayerNorm and combine launched at the
+// device's greatest priority and the decode attention at its least, so that one
+// half's latency-bound GEMMs run while the other half's HBM-bound decode does.
+// Each chain has its own rows of the activation buffers and of the split-K
+// scratch.
 // Arguments are the caller's to check; the current device must be the context's.
+constexpr int SPLIT_MIN_ROWS = 64;
 int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, float* hidden, bf16* lnf_bf16,
-        cudaStream_t st, bool ln1_ready = false, bool qkv_append = true);
+        cudaStream_t st, bool ln1_ready = false, bool qkv_append = true, bool split = false);
 
 // ---- LayerNorm of one row by one warp (LAYERNORM_1: mean, then the mean squared
 // deviation, out = (x - mean) * rsqrt(var + 1e-5) * w + b), width = 32 * PER.

@@ -577,7 +577,7 @@ cudaError_t prepare_pair(int dev) {
 }
 
 template <int BN>
-void config_pair(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[2], const Args& a, cudaStream_t st, bool pdl) {
+void config_pair(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[3], const Args& a, cudaStream_t st, bool pdl) {
     cfg = {};
     cfg.gridDim = dim3(2 * (a.N / BN), (a.M + BM - 1) / BM, 1);
     cfg.blockDim = dim3(NTHREADS);
@@ -590,7 +590,7 @@ void config_pair(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[2], const 
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 2 : 1;
+    cfg.numAttrs = with_priority(attr, pdl ? 2 : 1);
 }
 
 template <int BN, int EPI>
@@ -600,7 +600,7 @@ cudaError_t launch_pair_t(const CUtensorMap& ta, const CUtensorMap& tb, const Ar
     if (e == cudaSuccess) e = prepare_pair<BN, EPI>(dev);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     config_pair<BN>(cfg, attr, a, st, pdl);
     return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, ta, tb, a);
 }
@@ -630,7 +630,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <int BN>
-void config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[2], const Args& a, int splits, cudaStream_t st,
+void config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[3], const Args& a, int splits, cudaStream_t st,
             bool pdl) {
     cfg = {};
     cfg.gridDim = dim3(a.N / BN, (a.M + BM - 1) / BM, splits);
@@ -644,7 +644,7 @@ void config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[2], const Args&
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 2 : 1;
+    cfg.numAttrs = with_priority(attr, pdl ? 2 : 1);
 }
 
 template <int BN, int EPI>
@@ -667,7 +667,7 @@ cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a
     if (e == cudaSuccess) e = prepare<BN, EPI>(dev);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     config<BN>(cfg, attr, a, a.splits, st, pdl);
     return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI>, ta, tb, a);
 }
@@ -687,8 +687,9 @@ int active_clusters(int splits) {
         Args a{};
         a.M = BM, a.N = BN, a.K = BK * splits, a.splits = splits;
         cudaLaunchConfig_t cfg;
-        cudaLaunchAttribute attr[2];
+        cudaLaunchAttribute attr[3];
         config<BN>(cfg, attr, a, splits, nullptr, false);
+        cfg.numAttrs = 1;  // the cluster shape only
         if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, EPI>, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();  // a failed query leaves no error behind for the next call

@@ -156,4 +156,24 @@ cudaError_t launch_reset(const mb_ctx* c, int stream, cudaStream_t st);
 int check_items_host(mb_ctx* c, int n, const int32_t* streams, const int32_t* positions);
 int report_bits(mb_ctx* c, int32_t bits);
 
+// Execution priority (cudaLaunchAttributePriority) of the kernels this thread
+// launches while `set`: `value` for every kernel but the decode attention, which
+// gets `decode_value`.  Unset, a launch carries no priority and runs at its
+// stream's.  The decoder step sets it around its two half-batch chains so that
+// one half's GEMMs and LayerNorms are dispatched ahead of the other half's
+// pending decode CTAs (mb_decoder.cu).
+struct LaunchPriority {
+    bool set = false;
+    int value = 0, decode_value = 0;
+};
+extern thread_local LaunchPriority launch_priority;
+// Appends the priority attribute (when set) after the `n` attributes in `attrs`
+// (room for one more); returns the new count.
+inline unsigned int with_priority(cudaLaunchAttribute* attrs, unsigned int n, bool decode = false) {
+    if (!launch_priority.set) return n;
+    attrs[n].id = cudaLaunchAttributePriority;
+    attrs[n].val.priority = decode ? launch_priority.decode_value : launch_priority.value;
+    return n + 1;
+}
+
 }  // namespace mb
