@@ -157,3 +157,51 @@ def test_decoder_step_at_config4_shape():
             k, v, slots = ring.gather(layer, s, int(pos[s]) + 1)
             ok, ov, oslots = orc.gather(layer, i, int(pos[s]) + 1)
             assert np.array_equal(slots.cpu().numpy(), oslots), (layer, s)
+
+
+@pytest.mark.parametrize("S", [256, 131])
+def test_decoder_split_matches_one_chain(S, monkeypatch):
+    """A step of 128 items or more runs as two half-batch chains on two CUDA
+    streams, each over its own rows of the activations and of the split-K
+    scratch.  The same two steps with the split off (MOCKBIRD_DECODER_SPLIT=0,
+    read when the decoder is created) give every row within the decoder
+    tolerance (the GEMMs' plans differ with M, so their sums may round
+    differently).  The appended K/V rows land in the same slots.  131 items split
+    65 + 66, so the second chain starts at a row that is not a tile boundary."""
+    h, ffn, L, C = 768, 3072, 2, 1024
+    w = _weights(L, h, ffn, seed=6)
+    rings, decs = [], []
+    for split in ("1", "0"):
+        monkeypatch.setenv("MOCKBIRD_DECODER_SPLIT", split)
+        ring = KvRing(layers=L, streams=S, capacity=C, dtype="bf16", wrap=True)
+        rings.append(ring)
+        decs.append(Decoder(ring, w, ffn))
+    monkeypatch.delenv("MOCKBIRD_DECODER_SPLIT")
+    pos = np.random.default_rng(7).integers(300, C, size=S)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(7)
+    for s in range(S):
+        kv = torch.randn(2, 12, int(pos[s]), 64, generator=gen, device=DEV).to(torch.bfloat16)
+        for layer in range(L):
+            for ring in rings:
+                ring.ring_write(layer, s, 0, kv[0], kv[1])
+    rng = np.random.default_rng(8)
+    worst = 0.0
+    for step in range(2):
+        x = torch.from_numpy(rng.standard_normal((S, h)).astype(np.float32)).to(DEV)
+        outs = [dec.step(list(range(S)), pos + step, x.clone()).cpu().numpy() for dec in decs]
+        assert np.isfinite(outs[0]).all()
+        worst = max(worst, max_err(outs[0], outs[1]))
+    for ring in rings:
+        ring.sync()
+    assert worst < TOL, worst
+    for s in (0, S // 2 - 1, S // 2, S // 2 + 1, S - 1):
+        for layer in range(L):
+            a = rings[0].gather(layer, s, int(pos[s]) + 1)
+            b = rings[1].gather(layer, s, int(pos[s]) + 1)
+            assert torch.equal(a[2], b[2]), (layer, s)
+            assert (a[0].float() - b[0].float()).abs().max().item() < TOL, (layer, s)
+    for dec in decs:
+        dec.dispose()
+    for ring in rings:
+        ring.dispose()
