@@ -222,7 +222,10 @@ MB_API int mb_decoder_destroy(mb_decoder* dec);
 /* One global decode step for n streams: hidden [n][H*64] fp32 (device) holds the
  * embedded rows on entry and ln_f of the last layer on return
  * (DecodeRunner.globalStep, decode.ts:712-775, without the embedding).  Each
- * stream appends at its position in every layer's ring. */
+ * stream appends at its position in every layer's ring.  From 128 items on, the
+ * second half of the items runs on a stream the decoder owns, forked from
+ * `cuda_stream` and joined back to it by events: work queued on `cuda_stream`
+ * after the call still starts only once the whole step is done. */
 MB_API int mb_decoder_step(mb_decoder* dec, int32_t n, const int32_t* streams, const int32_t* positions,
                            float* hidden, void* cuda_stream);
 
