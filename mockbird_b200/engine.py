@@ -50,8 +50,8 @@ class MockbirdError(RuntimeError):
 def _ptr(t) -> ctypes.c_void_p:
     if isinstance(t, torch.Tensor):
         return ctypes.c_void_p(t.data_ptr())
-    if isinstance(t, np.ndarray):  # the buffer address, without building a ctypes view of the array
-        return ctypes.c_void_p(t.__array_interface__["data"][0])
+    if isinstance(t, np.ndarray):
+        return ctypes.c_void_p(t.ctypes.data)
     raise TypeError(f"expected a torch tensor or numpy array, got {type(t).__name__}")
 
 
@@ -63,17 +63,48 @@ _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 _TORCH_DTYPE = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
 
 
+_NP_HOST = {"float32": np.dtype(np.float32), "int32": np.dtype(np.int32)}
+_TORCH_HOST = {"float32": torch.float32, "int32": torch.int32}
+
+
 def _host_array(name: str, a, shape: tuple, dtype: str):
     """Check a host buffer that the C ABI reads or writes in place through its
     address: a C-contiguous numpy array or CPU torch tensor of `dtype` and
     `shape` (anything else would be read or written at the wrong places)."""
-    if isinstance(a, torch.Tensor):
-        ok = not a.is_cuda and a.is_contiguous() and a.dtype == getattr(torch, dtype) and tuple(a.shape) == shape
+    if isinstance(a, np.ndarray):
+        ok = a.dtype == _NP_HOST[dtype] and a.shape == shape and a.flags.c_contiguous
+    elif isinstance(a, torch.Tensor):
+        ok = not a.is_cuda and a.dtype is _TORCH_HOST[dtype] and a.shape == shape and a.is_contiguous()
     else:
-        ok = isinstance(a, np.ndarray) and a.flags["C_CONTIGUOUS"] and a.dtype == np.dtype(dtype) and a.shape == shape
+        ok = False
     if not ok:
         raise TypeError(f"{name} must be a contiguous host {dtype} array of shape {shape}")
     return a
+
+
+def _host_addr(name: str, a, shape: tuple, dtype: str) -> int:
+    """The address of a host buffer that passes _host_array."""
+    _host_array(name, a, shape, dtype)
+    return a.data_ptr() if isinstance(a, torch.Tensor) else a.ctypes.data
+
+
+def _host_input(a):
+    """An fp32 input read through its address: `a` itself when it is already a
+    C-contiguous fp32 numpy array or CPU tensor, else a contiguous fp32 copy."""
+    if isinstance(a, torch.Tensor) and not a.is_cuda:
+        return a if a.dtype is torch.float32 and a.is_contiguous() else a.to(torch.float32).contiguous()
+    if isinstance(a, np.ndarray) and a.dtype == _NP_HOST["float32"] and a.flags.c_contiguous:
+        return a
+    return np.ascontiguousarray(a, np.float32)
+
+
+def _host_ids(streams, positions):
+    """Stream ids and positions as int32 arrays of one length."""
+    s = np.ascontiguousarray(streams, np.int32)
+    p = np.ascontiguousarray(positions, np.int32)
+    if s.ndim != 1 or p.shape != s.shape:
+        raise ValueError(f"streams and positions must be 1-D of one length (got {s.shape} and {p.shape})")
+    return s, p
 
 
 class KvRing:
@@ -183,15 +214,17 @@ class KvRing:
 
     def append_attend_host(self, layer: int, streams, positions, qkv: np.ndarray,
                            out: np.ndarray | None = None, stream=None) -> np.ndarray:
-        """append_attend on host arrays (validated on the host; blocks until `out` is ready)."""
-        s = np.ascontiguousarray(streams, np.int32)
-        p = np.ascontiguousarray(positions, np.int32)
-        q = np.ascontiguousarray(qkv, np.float32)
+        """append_attend on host arrays (validated on the host; blocks until `out` is ready).
+
+        `qkv` / `out` may be numpy arrays or (pinned) CPU torch tensors."""
+        s, p = _host_ids(streams, positions)
+        n = len(s)
+        q = _host_input(qkv)
         if out is None:
-            out = np.empty((len(s), self.hidden), np.float32)
-        _host_array("qkv", q, (len(s), 3 * self.hidden), "float32")
-        _host_array("out", out, (len(s), self.hidden), "float32")
-        self._check(self.lib.mb_append_attend_host(self.ctx, layer, len(s), _ptr(s), _ptr(p), _ptr(q), _ptr(out),
+            out = np.empty((n, self.hidden), np.float32)
+        qa = _host_addr("qkv", q, (n, 3 * self.hidden), "float32")
+        oa = _host_addr("out", out, (n, self.hidden), "float32")
+        self._check(self.lib.mb_append_attend_host(self.ctx, layer, n, s.ctypes.data, p.ctypes.data, qa, oa,
                                                    self._stream(stream)))
         return out
 
@@ -199,15 +232,14 @@ class KvRing:
         """All layers of one decode step on host buffers: qkv [layers][n][3*H*64] -> [layers][n][H*64].
 
         `qkv` / `out` may be numpy arrays or (pinned) CPU torch tensors."""
-        s = np.ascontiguousarray(streams, np.int32)
-        p = np.ascontiguousarray(positions, np.int32)
-        if isinstance(qkv, np.ndarray):
-            qkv = np.ascontiguousarray(qkv, np.float32)
+        s, p = _host_ids(streams, positions)
+        n = len(s)
+        q = _host_input(qkv)
         if out is None:
-            out = np.empty((self.layers, len(s), self.hidden), np.float32)
-        _host_array("qkv", qkv, (self.layers, len(s), 3 * self.hidden), "float32")
-        _host_array("out", out, (self.layers, len(s), self.hidden), "float32")
-        self._check(self.lib.mb_decode_step_host(self.ctx, len(s), _ptr(s), _ptr(p), _ptr(qkv), _ptr(out),
+            out = np.empty((self.layers, n, self.hidden), np.float32)
+        qa = _host_addr("qkv", q, (self.layers, n, 3 * self.hidden), "float32")
+        oa = _host_addr("out", out, (self.layers, n, self.hidden), "float32")
+        self._check(self.lib.mb_decode_step_host(self.ctx, n, s.ctypes.data, p.ctypes.data, qa, oa,
                                                  self._stream(stream)))
         return out
 

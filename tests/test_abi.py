@@ -129,3 +129,31 @@ def test_noalloc_checks_pass_for_aligned_pointers(lib):
     base = 0x10000
     ring = _lib.MbRingRef(base, base, base, base, 1, 12, 64, 1, _lib.MB_F32, 1, 64)
     assert lib.mb_append_attend_noalloc(ctypes.byref(ring), 0, 1, base, base, base, base, None) == 6  # MB_ERR_CUDA
+
+
+def test_host_buffer_helpers():
+    """The host-array wrappers read buffers through their addresses: inputs are
+    used in place when they are C-contiguous fp32 (numpy or CPU torch) and copied
+    otherwise; outputs are never copied; stream ids and positions must have one
+    length (the C call reads n of each)."""
+    import numpy as np
+    import torch
+
+    from mockbird_b200.engine import _host_addr, _host_ids, _host_input
+
+    a = np.zeros((2, 3), np.float32)
+    assert _host_input(a) is a and _host_addr("x", a, (2, 3), "float32") == a.ctypes.data
+    t = torch.zeros(2, 3)
+    assert _host_input(t) is t and _host_addr("x", t, (2, 3), "float32") == t.data_ptr()
+    for conv in (np.zeros((2, 3)), np.zeros((3, 2), np.float32).T, torch.zeros(3, 2).t(), [[1, 2, 3], [4, 5, 6]]):
+        c = _host_input(conv)
+        assert _host_addr("x", c, (2, 3), "float32")
+        assert np.array_equal(np.asarray(c), np.asarray(conv, np.float32))
+    with pytest.raises(TypeError):
+        _host_addr("out", np.zeros((3, 2), np.float32).T, (2, 3), "float32")
+    s, p = _host_ids([3, 1], np.array([5, 6], np.int64))
+    assert s.dtype == p.dtype == np.int32 and list(p) == [5, 6]
+    with pytest.raises(ValueError):
+        _host_ids([0, 1], [5])
+    with pytest.raises(ValueError):
+        _host_ids([[0, 1]], [[5, 6]])
