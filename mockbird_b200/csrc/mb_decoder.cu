@@ -368,9 +368,11 @@ int step_staged(mb_decoder* d, int n, cudaStream_t st) {
     const int rc2 = mb::dec::run(d, n, d->g_streams, d->g_positions, d->g_hidden, nullptr, d->cap, false, true, true);
     e = cudaStreamEndCapture(d->cap, &g);
     cudaGraphExec_t ex = nullptr;
-    // (a split step's kernel nodes carry the priorities they were launched with)
+    // A split step's kernel nodes carry the priorities they were launched with;
+    // a one-chain step's graph runs at the priority of the stream it is launched on.
+    const bool split = d->split && d->side && n / 2 >= mb::dec::SPLIT_MIN_ROWS;
     if (rc2 == MB_OK && e == cudaSuccess)
-        e = cudaGraphInstantiate(&ex, g, d->split ? cudaGraphInstantiateFlagUseNodePriority : 0);
+        e = cudaGraphInstantiate(&ex, g, split ? cudaGraphInstantiateFlagUseNodePriority : 0);
     if (g) cudaGraphDestroy(g);
     if (rc2 != MB_OK) return rc2;
     if (e != cudaSuccess) return mb::dec::fail(d, MB_ERR_CUDA, std::string("decoder capture: ") + cudaGetErrorString(e));
