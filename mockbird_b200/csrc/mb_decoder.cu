@@ -208,7 +208,8 @@ int run(mb_decoder* d, int n, const int32_t* streams, const int32_t* positions, 
     if (forked) {  // the caller's stream ends behind both chains, whatever happened
         e = cudaEventRecord(d->ev_join, d->side);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(st, d->ev_join, 0);
-        if (e != cudaSuccess && rc == MB_OK) rc = fail(d, MB_ERR_CUDA, std::string("decoder join: ") + cudaGetErrorString(e));
+        if (e != cudaSuccess && rc == MB_OK)
+            rc = fail(d, MB_ERR_CUDA, std::string("decoder join: ") + cudaGetErrorString(e));
     }
     mb::launch_priority = saved;
     return rc;
